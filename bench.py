@@ -1,0 +1,405 @@
+#!/usr/bin/env python
+"""Benchmark of the fused Cayley + quaternion selective scan (forward) on B200.
+
+Workload (config 3 of the hot path): per GPU batch=4, seq_len=2048, d_inner=1536,
+d_state=64; x ~ N(0,1) [4,2048,1536] is the real part of S; delta =
+softplus(N(-3,1)); Lambda: Re = -exp(U(ln 1e-3, ln 1e-1)), Im ~ N(0, 0.5);
+B_t, C_t shared by all channels [4,2048,64,4] ~ N(0,1)/8; D = 1. fp32 by default
+(``--dtype bf16`` for bf16 inputs, state always fp32; ``--layout perchannel`` for
+the reference block's per-channel B/C [4,2048,1536,64,4]).
+
+One step = one fused scan launch over the whole batch (inputs resident in HBM).
+With N GPUs (torchrun, one process per GPU) every rank scans its own batch of 4
+(weak scaling over batch, no collective on the data path); the step time is the
+max over ranks. Prints one JSON line (rank 0).
+
+``--impl reference`` times the reference's sequential PyTorch CPU path (restated
+in ``oracle/``) on the host cores instead, on a bounded time-prefix of the same
+workload per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+BATCH, SEQ, CHANNELS, STATE = 4, 2048, 1536, 64
+METRIC = "quaternion SSM scan forward tokens/s (config 3: B=4/GPU, T=2048, D=1536, N=64)"
+# algorithmic FLOPs per (b, t, d, n) element of the fused forward with a real
+# signal: Cayley from (delta, Lambda) 15, q (x) h 28, x*B 4, + 4, C (x) h 28, sum over n 4
+FLOPS_PER_ELEM_SREAL = 83
+FLOPS_PER_ELEM_SQUAT = 83 - 4 + 28  # B (x) S instead of x*B
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__,
+                                 formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--dtype", choices=["fp32", "bf16"], default="fp32")
+    ap.add_argument("--layout", choices=["shared", "perchannel"], default="shared")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--cpu-budget-s", type=float, default=15.0,
+                    help="seconds of CPU work for the cpu_baseline sample")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------- plumbing
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        backend = "nccl" if (args.impl == "b200" and torch.cuda.is_available()) else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        import datetime
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        dist.barrier()
+
+
+def make_inputs(dev, dtype, layout, seed):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    f32 = torch.float32
+    x = torch.randn(BATCH, SEQ, CHANNELS, generator=g, device=dev, dtype=f32)
+    delta = torch.nn.functional.softplus(
+        torch.randn(BATCH, SEQ, CHANNELS, generator=g, device=dev, dtype=f32) - 3.0)
+    lam = torch.empty(CHANNELS, STATE, 4, device=dev, dtype=f32)
+    u = torch.rand(CHANNELS, STATE, generator=g, device=dev, dtype=f32)
+    lam[..., 0] = -torch.exp(u * (math.log(1e-1) - math.log(1e-3)) + math.log(1e-3))
+    lam[..., 1:] = 0.5 * torch.randn(CHANNELS, STATE, 3, generator=g, device=dev, dtype=f32)
+    bc_shape = (BATCH, SEQ, STATE, 4) if layout == "shared" else (BATCH, SEQ, CHANNELS, STATE, 4)
+    Bm = torch.randn(*bc_shape, generator=g, device=dev, dtype=f32) / math.sqrt(STATE)
+    Cm = torch.randn(*bc_shape, generator=g, device=dev, dtype=f32) / math.sqrt(STATE)
+    Dk = torch.ones(CHANNELS, device=dev, dtype=f32)
+    cast = torch.bfloat16 if dtype == "bf16" else f32
+    return dict(delta=delta.to(cast), Lambda=lam, B=Bm.to(cast), C=Cm.to(cast), x=x.to(cast), D=Dk)
+
+
+def algorithmic_bytes(inp, y_bytes):
+    return sum(t.numel() * t.element_size() for t in inp.values()) + y_bytes
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev):
+        self.proc = None
+        self.path = None
+        try:
+            self.uuid = str(torch.cuda.get_device_properties(dev).uuid)
+        except Exception:
+            self.uuid = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(prefix="mqc_clocks_", suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 10:
+                continue
+            if self.uuid and self.uuid.replace("GPU-", "") not in parts[1]:
+                continue
+            rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+
+        def num(s):
+            try:
+                return float(s)
+            except ValueError:
+                return None
+
+        sm = [num(r[2]) for r in rows if num(r[2]) is not None]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, val in zip(names, r[6:10]):
+                if val.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": num(rows[0][3]), "samples": len(rows),
+                "reasons": sorted(reasons)}
+
+
+def timed(fn, steps, warmup, world, stream):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    return e0.elapsed_time(e1)
+
+
+def max_over_ranks(val, world, dev):
+    if world == 1:
+        return val
+    t = torch.tensor([val], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+def fp32_peak_tflops(dev):
+    """FP32 FMA peak measured now (same clocks as the timed region)."""
+    import ctypes
+
+    from mambaqc_b200 import _lib
+    out = torch.zeros(1, device=dev)
+    n = ctypes.c_int64(0)
+    stream = torch.cuda.current_stream(dev)
+    iters = 4096
+    for _ in range(2):
+        _lib.call("mqc_probe_fp32_fma", out.data_ptr(), iters, ctypes.byref(n), stream.cuda_stream)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 5
+    e0.record(stream)
+    for _ in range(reps):
+        _lib.call("mqc_probe_fp32_fma", out.data_ptr(), iters, ctypes.byref(n), stream.cuda_stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3 / reps
+    return 2.0 * n.value / sec / 1e12
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except Exception:
+            pass
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+# ----------------------------------------------------------- CPU reference leg
+
+def cpu_reference_sample(budget_s, dtype_name, layout, seed=0):
+    """The reference's sequential fp32 PyTorch path (oracle restatement) on a
+    time-prefix of the config-3 workload; returns (tokens/s, sample description, threads)."""
+    from oracle import ref
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(seed)
+    slab = 8
+    lam = torch.empty(CHANNELS, STATE, 4)
+    lam[..., 0] = -torch.exp(torch.empty(CHANNELS, STATE).uniform_(math.log(1e-3), math.log(1e-1),
+                                                                   generator=g))
+    lam[..., 1:] = 0.5 * torch.randn(CHANNELS, STATE, 3, generator=g)
+    Dk = torch.ones(CHANNELS)
+    h = None
+    steps = 0
+    t_start = time.perf_counter()
+    while steps < SEQ:
+        x = torch.randn(BATCH, slab, CHANNELS, generator=g)
+        delta = torch.nn.functional.softplus(torch.randn(BATCH, slab, CHANNELS, generator=g) - 3.0)
+        shape = (BATCH, slab, STATE, 4) if layout == "shared" else (BATCH, slab, CHANNELS, STATE, 4)
+        Bm = torch.randn(*shape, generator=g) / 8
+        Cm = torch.randn(*shape, generator=g) / 8
+        _, h = ref.ssm_scan_cayley(delta, lam, Bm, Cm, x, Dk, h0=h, t_slab=slab)
+        steps += slab
+        if time.perf_counter() - t_start > budget_s:
+            break
+    elapsed = time.perf_counter() - t_start
+    sample = (f"first {steps} of {SEQ} timesteps of config 3 (B={BATCH}, D={CHANNELS}, "
+              f"N={STATE}, {layout} B/C, fp32), Cayley + sequential recurrence")
+    return BATCH * steps / elapsed, sample, threads, steps, elapsed
+
+
+# ----------------------------------------------------------------- main legs
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return 0
+    per_step_budget = max(0.5, 150.0 / max(1, args.steps + args.warmup))
+    vals = []
+    info = None
+    for i in range(args.warmup + args.steps):
+        v, sample, threads, steps, elapsed = cpu_reference_sample(per_step_budget, args.dtype,
+                                                                 args.layout, seed=i)
+        if i >= args.warmup:
+            vals.append(v)
+            info = (sample, threads)
+    value = statistics.mean(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * BATCH * SEQ / value, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": "config3_fused_scan_forward", "batch_per_gpu": BATCH,
+                   "seq_len": SEQ, "d_inner": CHANNELS, "d_state": STATE, "layout": args.layout},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": info[1], "kind": "port",
+                         "sample": info[0] + " per step; tokens/s extrapolated over the prefix"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_b200(args, world, rank, local):
+    from mambaqc_b200 import _lib
+    from mambaqc_b200.kernels import ssm_scan_cayley
+
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    inp = make_inputs(dev, args.dtype, args.layout, seed=1234 + rank)
+    stream = torch.cuda.current_stream(dev)
+    out = {}
+
+    def step():
+        out["y"] = ssm_scan_cayley(inp["delta"], inp["Lambda"], inp["B"], inp["C"], inp["x"],
+                                   inp["D"])
+
+    step()
+    torch.cuda.synchronize()
+    _lib.check_device_status(dev)
+    y_bytes = out["y"].numel() * out["y"].element_size()
+
+    clocks = ClockSampler(dev)
+    clocks.start()
+    ms_total = timed(step, args.steps, args.warmup, world, stream)
+    clk = clocks.stop()
+    _lib.check_device_status(dev)
+    ms_step_local = ms_total / args.steps
+    ms_step = max_over_ranks(ms_step_local, world, dev)
+    tokens = BATCH * SEQ * world
+    value = tokens / (ms_step / 1e3)
+
+    # roofline of the dominant (only) kernel: FP32 issue bound, with the HBM view beside it
+    elems = BATCH * SEQ * CHANNELS * STATE
+    flops = elems * FLOPS_PER_ELEM_SREAL
+    abytes = algorithmic_bytes(inp, y_bytes)
+    sec = ms_step_local / 1e3
+    peaks, peak_kind = measured_peaks()
+    fp32_peak = fp32_peak_tflops(dev)
+    roofline = {"bound": "fp32", "achieved": flops / sec / 1e12, "peak": fp32_peak,
+                "unit": "TFLOP/s", "frac": flops / sec / 1e12 / fp32_peak,
+                "peak_source": "FP32 FMA probe (mqc_probe_fp32_fma) run by bench.py, same clocks",
+                "algorithmic_flops_per_launch": flops, "traffic": None}
+    roofline_hbm = {"bound": "hbm", "achieved": abytes / sec / 1e9, "peak": peaks["hbm_gbs"],
+                    "unit": "GB/s", "frac": abytes / sec / 1e9 / peaks["hbm_gbs"],
+                    "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+                    "algorithmic_bytes_per_launch": abytes, "traffic": None}
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, inp, dev, world, stream, ssm_scan_cayley)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, sample, threads, steps, elapsed = cpu_reference_sample(args.cpu_budget_s, args.dtype,
+                                                                 args.layout)
+        cpu = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": f"{sample}; {elapsed:.1f} s on {threads} threads"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32" if args.dtype == "fp32" else "bf16 inputs, f32 state",
+            "data": "synthetic (seeded, config-3 distributions)",
+            "config": {"workload": "config3_fused_scan_forward", "batch_per_gpu": BATCH,
+                       "global_batch": BATCH * world, "seq_len": SEQ, "d_inner": CHANNELS,
+                       "d_state": STATE, "layout": args.layout, "signal": "real x",
+                       "parallelism": f"dp{world} (batch shards, no data-path collective)",
+                       "l2": "inputs larger than L2 (310+ MB per step)"},
+            "roofline": roofline, "roofline_hbm": roofline_hbm,
+            "gpu_launches": args.steps, "clocks": clk, "e2e": e2e, "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_e2e(args, inp, dev, world, stream, op):
+    """Same metric through the public API with host buffers: every step copies its
+    inputs from pinned host memory and reads y back, inside the timed region."""
+    host = {k: v.cpu().pin_memory() for k, v in inp.items()}
+    y_host = torch.empty(BATCH, SEQ, CHANNELS, 4, dtype=inp["delta"].dtype).pin_memory()
+    dev_bufs = {k: torch.empty_like(v) for k, v in inp.items()}
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = y_host.numel() * y_host.element_size()
+
+    def step():
+        for k, v in host.items():
+            dev_bufs[k].copy_(v, non_blocking=True)
+        y = op(dev_bufs["delta"], dev_bufs["Lambda"], dev_bufs["B"], dev_bufs["C"],
+               dev_bufs["x"], dev_bufs["D"])
+        y_host.copy_(y, non_blocking=True)
+
+    steps = max(3, min(args.steps, 10))
+    ms = timed(step, steps, max(3, min(args.warmup, 3)), world, stream) / steps
+    ms = max_over_ranks(ms, world, dev)
+    return {"value": BATCH * SEQ * world / (ms / 1e3), "unit": "tokens/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms,
+            "steps": steps, "path": "pinned host -> device copies, fused scan, y -> pinned host"}
+
+
+def main():
+    args = parse_args()
+    world, rank, local = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            return run_reference(args, world, rank)
+        return run_b200(args, world, rank, local)
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

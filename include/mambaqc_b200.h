@@ -1,0 +1,201 @@
+/*
+ * mambaqc_b200 -- C ABI of the B200 (sm_100a) quaternion SSM hot path.
+ *
+ * Every entry point takes raw device pointers, sizes in elements and a CUDA
+ * stream (cudaStream_t passed as void*; NULL = legacy default stream), launches
+ * asynchronously on that stream and never synchronises. Entry points allocate no
+ * device memory, except where a declaration below says otherwise.
+ * Tensors are dense and row-major (C order) unless a stride is given; a
+ * quaternion is the last axis of 4 scalars (r, i, j, k), the layout of the
+ * reference's [..., 4] tensors. Return value: MQC_OK or an mqc_status code; on
+ * failure mqc_last_error() gives a human-readable message for the calling host
+ * thread.
+ *
+ * Each declaration cites the reference (polux06/mambaqc) Python function it
+ * replaces, as path:line inside that project.
+ */
+#ifndef MAMBAQC_B200_H_
+#define MAMBAQC_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MQC_API __attribute__((visibility("default")))
+#else
+#define MQC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Storage type of floating-point tensor arguments. Arithmetic is fp32. */
+typedef enum mqc_dtype {
+  MQC_DTYPE_F32 = 0,
+  MQC_DTYPE_BF16 = 1
+} mqc_dtype;
+
+typedef enum mqc_status {
+  MQC_OK = 0,
+  MQC_ERR_INVALID_VALUE = 1, /* bad size, null pointer, unknown flag         */
+  MQC_ERR_MISALIGNED = 2,    /* pointer not aligned to its vector width      */
+  MQC_ERR_UNSUPPORTED = 3,   /* valid but not implemented (e.g. d_state>256) */
+  MQC_ERR_CUDA = 4,          /* CUDA runtime error at launch                 */
+  MQC_ERR_DEVICE_TIMEOUT = 5 /* a bounded device-side wait gave up           */
+} mqc_status;
+
+/* Bits a kernel ORs into a caller-provided device status word (int32). */
+#define MQC_DEVICE_STATUS_TIMEOUT 0x1
+
+/* Library version, "major.minor.patch". */
+MQC_API const char* mqc_version(void);
+/* Static description of an mqc_status code. */
+MQC_API const char* mqc_status_string(int status);
+/* Detail of the last failing call on this host thread ("" if none). */
+MQC_API const char* mqc_last_error(void);
+
+/* ---- quaternion algebra: mambaqc/kernels/quaternion_ops.py ---------------- */
+
+/* out[i] = p[i] (x) q[i] (Hamilton product), i < n quaternions.
+ * Replaces quaternion_multiply(p, q), quaternion_ops.py:259-303, and
+ * quaternion_multiply_batched, quaternion_ops.py:306-357 (dense case). */
+MQC_API int mqc_qmul(const void* p, const void* q, void* out, int64_t n, int dtype, void* stream);
+
+/* out[i] = conj(q[i]). Replaces quaternion_conjugate, quaternion_ops.py:360-391. */
+MQC_API int mqc_qconj(const void* q, void* out, int64_t n, int dtype, void* stream);
+
+/* out[i] = conj(q[i]) / max(|q[i]|^2, eps).
+ * Replaces quaternion_inverse(q, eps), quaternion_ops.py:394-428. */
+MQC_API int mqc_qinv(const void* q, void* out, int64_t n, float eps, int dtype, void* stream);
+
+/* out[i] = |q[i]| (one scalar per quaternion, same dtype).
+ * Replaces quaternion_norm, quaternion_ops.py:431-461. */
+MQC_API int mqc_qnorm(const void* q, void* out, int64_t n, int dtype, void* stream);
+
+/* q[i] = (1 - z[i]/2)^-1 (x) (1 + z[i]/2), |1 - z/2|^2 clamped below by eps.
+ * Replaces cayley_discretization_fused(z, eps), cayley_transform.py:132-195. */
+MQC_API int mqc_cayley(const void* z, void* q, int64_t n, float eps, int dtype, void* stream);
+
+/* dz[i] = (dq/dz[i])^T dq[i]: the vector-Jacobian product of mqc_cayley, with the
+ * eps clamp treated as a constant where active. The reference has no GPU
+ * backward (its Cayley kernel, cayley_transform.py:24-129, is not
+ * differentiable); this is the gradient of cayley_discretization_reference,
+ * cayley_transform.py:199-223, as torch autograd computes it on the CPU. */
+MQC_API int mqc_cayley_bwd(const void* z, const void* dq, void* dz, int64_t n, float eps, int dtype,
+                   void* stream);
+
+/* ---- prefix product: mambaqc/kernels/parallel_scan.py --------------------- */
+
+/* For q, out of shape [batch, seq_len, lanes, 4] (lanes = d_model * d_state):
+ * out[b,t,l] = q[b,t,l] (x) out[b,t-1,l], out[b,-1,l] = 1.
+ * When batch*lanes is too small to fill the GPU, time is split into chunks and
+ * the chunk products go to scratch taken with cudaMallocAsync on `stream` and
+ * released with cudaFreeAsync on the same stream (batch*chunks*lanes*16 bytes).
+ * Replaces parallel_scan_quaternion(q_sequence), parallel_scan.py:171-264. */
+MQC_API int mqc_prefix_prod(const void* q, void* out, int64_t batch, int64_t seq_len, int64_t lanes,
+                    int dtype, void* stream);
+
+/* ---- selective scan: mambaqc/kernels/ssm_fused.py + block._ssm_forward ------ */
+
+/* Flags of mqc_ssm_scan_args.flags */
+#define MQC_SSM_Q_GIVEN 0x1   /* q is given explicitly (else formed from delta, Lambda) */
+#define MQC_SSM_BC_SHARED 0x2 /* B, C are [B,T,N,4] shared by all channels           */
+#define MQC_SSM_S_REAL 0x4    /* s is a real signal x [B,T,D], S = (x, 0, 0, 0)      */
+
+/*
+ * Arguments of one selective scan over time, per (batch b, channel d, state n):
+ *
+ *   q_t   = Q_GIVEN ? q[b,t,d,n] : cayley(delta[b,t,d] * Lambda[d,n], eps)
+ *   h_t   = q_t (x) h_{t-1} + B_t (x) S_t,            h_{-1} = h0 or 0
+ *   y_t   = sum_n C_t (x) h_t + D[b,t,d] * S_t
+ *
+ * Shapes (B batch, T seq_len, D channels, N d_state):
+ *   delta [B,T,D] dtype           Lambda [D,N,4] fp32        q [B,T,D,N,4] dtype
+ *   Bm, Cm [B,T,N,4] (BC_SHARED) or [B,T,D,N,4], dtype
+ *   s  x [B,T,D] (S_REAL) or S [B,T,D,4], dtype
+ *   dskip fp32, element (b,t,d) at dskip[b*dskip_sb + t*dskip_st + d*dskip_sd]
+ *   h0 [B,D,N,4] fp32 or NULL (zero state); y [B,T,D,4] dtype; hT [B,D,N,4] fp32 or NULL
+ *   status: device int32 the kernel ORs MQC_DEVICE_STATUS_* into, or NULL.
+ *   wait_poll_limit: polls of a bounded device wait before giving up; <0 = default.
+ */
+typedef struct mqc_ssm_scan_args {
+  int64_t batch, seq_len, channels, d_state;
+  int32_t dtype;
+  int32_t flags;
+  float eps;
+  int32_t reserved0;
+  const void* delta;
+  const float* lambda_;
+  const void* q;
+  const void* Bm;
+  const void* Cm;
+  const void* s;
+  const float* dskip;
+  int64_t dskip_sb, dskip_st, dskip_sd;
+  const float* h0;
+  void* y;
+  float* hT;
+  int32_t* status;
+  int64_t wait_poll_limit;
+} mqc_ssm_scan_args;
+
+/* Full scan over T. With MQC_SSM_Q_GIVEN this replaces
+ * ssm_forward_fused(q, B, S, C, D), ssm_fused.py:340-401; without it, it is the
+ * fused form of QuaternionMamba2Block._ssm_forward lines
+ * models/quaternion_mamba2_block.py:214-228 (z = Delta*Lambda, Cayley, scan)
+ * that never materialises z or q. */
+MQC_API int mqc_ssm_scan_fwd(const mqc_ssm_scan_args* args, void* stream);
+
+/* One step with explicit q: h_new = q (x) h_prev + B (x) S, y = sum_n C (x) h_new + D*S.
+ * q, Bm, Cm, h_prev, h_new [B,D,N,4]; S [B,D,4]; dskip [B,D] fp32; y [B,D,4].
+ * q, Bm, Cm, S, y in dtype; h_prev, h_new fp32.
+ * Replaces ssm_step_fused(q, B, S, C, D, h_prev), ssm_fused.py:258-337. */
+MQC_API int mqc_ssm_step(const void* q, const void* Bm, const void* S, const void* Cm,
+                 const float* dskip, const float* h_prev, float* h_new, void* y, int64_t batch,
+                 int64_t channels, int64_t d_state, int dtype, void* stream);
+
+/* ---- quaternion LayerNorm: mambaqc/kernels/quaternion_norm.py -------------- */
+
+#define MQC_QLN_PADDED_COMPAT 0x1 /* reproduce the reference Triton kernel's padded lanes */
+
+/* Row-wise norm LayerNorm over d_model quaternions for `rows` rows:
+ *   n = sqrt(|q|^2 + eps); mu, var = mean, biased variance of n over the row;
+ *   out = gamma * (n - mu)/sqrt(var + eps) * q/(n + eps) + beta.
+ * q, out [rows, d_model, 4] dtype; gamma [d_model], beta [d_model, 4] fp32;
+ * mean, rstd [rows] fp32 (saved for the backward) or NULL.
+ * Replaces quaternion_layer_norm_fused, quaternion_norm.py:119-174 (and the
+ * forward of QuaternionLayerNorm, :177-215). */
+MQC_API int mqc_qln_fwd(const void* q, const float* gamma, const float* beta, void* out, float* mean,
+                float* rstd, int64_t rows, int64_t d_model, float eps, int flags, int dtype,
+                void* stream);
+
+/* Bytes of workspace mqc_qln_bwd needs for `rows` x `d_model` (0 if nothing to do). */
+MQC_API size_t mqc_qln_bwd_workspace_size(int64_t rows, int64_t d_model);
+
+/* Backward of mqc_qln_fwd (exact form, not the padded-compat one): from q, gamma,
+ * dout = dL/dout and the saved mean/rstd, writes dq [rows, d_model, 4] (dtype) and
+ * the parameter gradients dgamma [d_model], dbeta [d_model, 4] (fp32, summed over
+ * rows in a fixed order). `workspace` (16-byte aligned, caller-owned) holds
+ * per-CTA partial sums. The reference has no GPU backward; this is the gradient
+ * torch autograd takes through quaternion_layer_norm_reference,
+ * quaternion_norm.py:219-245. */
+MQC_API int mqc_qln_bwd(const void* q, const float* gamma, const void* dout, const float* mean,
+                const float* rstd, void* dq, float* dgamma, float* dbeta, void* workspace,
+                size_t workspace_bytes, int64_t rows, int64_t d_model, float eps, int dtype,
+                void* stream);
+
+/* ---- diagnostics ---------------------------------------------------------- */
+
+/* Launches a pure FP32 FMA-chain kernel (no memory traffic) that keeps every SM's
+ * FP32 pipes busy for `iters` iterations and stores the number of FMAs it issues
+ * in *fmas_per_launch. Timing it gives the FP32 peak that the scan kernels'
+ * FP32-issue roofline is measured against. No counterpart in the reference.
+ * `out`: one device float, written only in a case that never occurs. */
+MQC_API int mqc_probe_fp32_fma(float* out, int64_t iters, int64_t* fmas_per_launch, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MAMBAQC_B200_H_ */

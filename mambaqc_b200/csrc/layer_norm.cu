@@ -1,0 +1,293 @@
+// Quaternion LayerNorm (norm-only rescale that preserves each quaternion's
+// direction), forward and backward.
+//
+// Reference: quaternion_layer_norm_fused / quaternion_layer_norm_reference,
+// mambaqc/kernels/quaternion_norm.py:119-174 and :219-245. One CTA owns one row
+// of d_model quaternions; each thread keeps VPT quaternions of the row in
+// registers (16-byte coalesced loads), so the row is read from HBM once and
+// written once. Mean and variance of the norms are two-pass over registers
+// (mean first, then centred squares), with warp-shuffle + shared-memory sums.
+#include "mqc_common.cuh"
+#include "mqc_host.h"
+
+namespace mqc {
+namespace {
+
+constexpr int kVpt = 8;           // quaternions per thread
+constexpr int kMaxRowThreads = 512;
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v += __shfl_xor_sync(0xffffffffu, v, 16);
+  v += __shfl_xor_sync(0xffffffffu, v, 8);
+  v += __shfl_xor_sync(0xffffffffu, v, 4);
+  v += __shfl_xor_sync(0xffffffffu, v, 2);
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();  // red[] reuse across calls
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float s = 0.f;
+  for (int i = 0; i < nw; ++i) s += red[i];  // same order on every thread
+  return s;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kMaxRowThreads) qln_fwd_kernel(
+    const T* __restrict__ q, const float* __restrict__ gamma, const float* __restrict__ beta,
+    T* __restrict__ out, float* __restrict__ mean_out, float* __restrict__ rstd_out, int D,
+    float eps, int pad_lanes) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const T* qr = q + row * D * 4;
+  T* orow = out + row * D * 4;
+  float4 v[kVpt];
+  float nrm[kVpt];
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < kVpt; ++j) {
+    const int d = threadIdx.x + j * blockDim.x;
+    v[j] = f4_zero();
+    nrm[j] = 0.f;
+    if (d < D) {
+      v[j] = QIO<T>::ld_stream(qr + d * 4);
+      const float4 a = v[j];
+      nrm[j] = sqrtf(fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, a.w * a.w))) + eps);
+      s += nrm[j];
+    }
+  }
+  const float pad_norm = sqrtf(eps);
+  float tot = block_sum(s, red);
+  if (pad_lanes) tot += float(pad_lanes) * pad_norm;
+  const float mu = tot / float(D);
+  float s2 = 0.f;
+#pragma unroll
+  for (int j = 0; j < kVpt; ++j) {
+    const int d = threadIdx.x + j * blockDim.x;
+    if (d < D) {
+      const float c = nrm[j] - mu;
+      s2 = fmaf(c, c, s2);
+    }
+  }
+  float tot2 = block_sum(s2, red);
+  if (pad_lanes) tot2 += float(pad_lanes) * (pad_norm - mu) * (pad_norm - mu);
+  const float var = tot2 / float(D);
+  const float sd = sqrtf(var + eps);
+  if (threadIdx.x == 0) {
+    if (mean_out) mean_out[row] = mu;
+    if (rstd_out) rstd_out[row] = 1.f / sd;
+  }
+#pragma unroll
+  for (int j = 0; j < kVpt; ++j) {
+    const int d = threadIdx.x + j * blockDim.x;
+    if (d < D) {
+      const float nh = (nrm[j] - mu) / sd;
+      const float g = __ldg(gamma + d) * nh;
+      const float dn = nrm[j] + eps;
+      const float4 bt = QIO<float>::ld(beta + d * 4);
+      float4 o;
+      o.x = fmaf(g, v[j].x / dn, bt.x);
+      o.y = fmaf(g, v[j].y / dn, bt.y);
+      o.z = fmaf(g, v[j].z / dn, bt.z);
+      o.w = fmaf(g, v[j].w / dn, bt.w);
+      QIO<T>::st_stream(orow + d * 4, o);
+    }
+  }
+}
+
+// Backward. Per row, with n = sqrt(|q|^2 + eps), nh = (n - mu) * rstd,
+// u = q / (n + eps), g = dL/dout and a = gamma * <g, u>:
+//   dL/dn = rstd * (a - mean(a) - nh * mean(a * nh)) - nh * a / (n + eps)
+//   dq    = gamma * nh * g / (n + eps) + dL/dn * q / n
+//   dgamma += nh * <g, u>,  dbeta += g        (summed over rows)
+// A CTA walks rows blockIdx.x, blockIdx.x + gridDim.x, ...; each thread keeps the
+// dgamma/dbeta partials of its own columns in registers and writes one partial
+// row per CTA; qln_bwd_reduce_kernel sums the partials in a fixed order, so the
+// parameter gradients are deterministic.
+constexpr int kVptB = 4;
+
+template <typename T>
+__global__ void __launch_bounds__(1024) qln_bwd_kernel(
+    const T* __restrict__ q, const float* __restrict__ gamma, const T* __restrict__ dout,
+    const float* __restrict__ mean, const float* __restrict__ rstd, T* __restrict__ dq,
+    float* __restrict__ partial, int64_t rows, int D, float eps) {
+  __shared__ float red[32];
+  float dg[kVptB];
+  float4 db[kVptB];
+  float gm[kVptB];
+#pragma unroll
+  for (int j = 0; j < kVptB; ++j) {
+    dg[j] = 0.f;
+    db[j] = f4_zero();
+    const int d = threadIdx.x + j * blockDim.x;
+    gm[j] = d < D ? __ldg(gamma + d) : 0.f;
+  }
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const T* qr = q + row * D * 4;
+    const T* gr = dout + row * D * 4;
+    const float mu = __ldg(mean + row), rs = __ldg(rstd + row);
+    float4 qv[kVptB], gv[kVptB];
+    float nrm[kVptB], nh[kVptB], av[kVptB];
+    float sa = 0.f, san = 0.f;
+#pragma unroll
+    for (int j = 0; j < kVptB; ++j) {
+      const int d = threadIdx.x + j * blockDim.x;
+      qv[j] = f4_zero();
+      gv[j] = f4_zero();
+      nrm[j] = 1.f;
+      nh[j] = 0.f;
+      av[j] = 0.f;
+      if (d < D) {
+        qv[j] = QIO<T>::ld(qr + d * 4);
+        gv[j] = QIO<T>::ld(gr + d * 4);
+        const float4 a = qv[j];
+        nrm[j] = sqrtf(fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, a.w * a.w))) + eps);
+        nh[j] = (nrm[j] - mu) * rs;
+        const float dn = nrm[j] + eps;
+        const float gu = fmaf(gv[j].x, a.x, fmaf(gv[j].y, a.y, fmaf(gv[j].z, a.z, gv[j].w * a.w))) / dn;
+        av[j] = gm[j] * gu;
+        sa += av[j];
+        san = fmaf(av[j], nh[j], san);
+        dg[j] = fmaf(nh[j], gu, dg[j]);
+        db[j].x += gv[j].x;
+        db[j].y += gv[j].y;
+        db[j].z += gv[j].z;
+        db[j].w += gv[j].w;
+      }
+    }
+    const float ma = block_sum(sa, red) / float(D);
+    const float man = block_sum(san, red) / float(D);
+#pragma unroll
+    for (int j = 0; j < kVptB; ++j) {
+      const int d = threadIdx.x + j * blockDim.x;
+      if (d < D) {
+        const float dn = nrm[j] + eps;
+        const float dldn = rs * (av[j] - ma - nh[j] * man) - nh[j] * av[j] / dn;
+        const float cg = gm[j] * nh[j] / dn;
+        const float cq = dldn / nrm[j];
+        float4 o;
+        o.x = fmaf(cg, gv[j].x, cq * qv[j].x);
+        o.y = fmaf(cg, gv[j].y, cq * qv[j].y);
+        o.z = fmaf(cg, gv[j].z, cq * qv[j].z);
+        o.w = fmaf(cg, gv[j].w, cq * qv[j].w);
+        QIO<T>::st(dq + row * D * 4 + d * 4, o);
+      }
+    }
+  }
+  float* prow = partial + int64_t(blockIdx.x) * D * 5;
+#pragma unroll
+  for (int j = 0; j < kVptB; ++j) {
+    const int d = threadIdx.x + j * blockDim.x;
+    if (d < D) {
+      prow[d] = dg[j];
+      reinterpret_cast<float4*>(prow + D)[d] = db[j];
+    }
+  }
+}
+
+// dgamma[d] = sum_c partial[c][d]; dbeta[d] = sum_c partial[c][D + 4d .. 4d+3]
+__global__ void qln_bwd_reduce_kernel(const float* __restrict__ partial, float* __restrict__ dgamma,
+                                      float* __restrict__ dbeta, int nparts, int D) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;  // 0 .. 5D-1
+  if (i >= 5 * D) return;
+  float s = 0.f;
+  for (int c = 0; c < nparts; ++c) s += partial[int64_t(c) * D * 5 + i];
+  if (i < D) dgamma[i] = s;
+  else dbeta[i - D] = s;
+}
+
+int qln_bwd_parts(int64_t rows) {
+  int64_t p = int64_t(num_sms()) * 2;
+  if (p > rows) p = rows;
+  return p < 1 ? 1 : int(p);
+}
+
+}  // namespace
+}  // namespace mqc
+
+using namespace mqc;
+
+extern "C" int mqc_qln_fwd(const void* q, const float* gamma, const float* beta, void* out,
+                           float* mean, float* rstd, int64_t rows, int64_t d_model, float eps,
+                           int flags, int dtype, void* stream) {
+  clear_error();
+  MQC_REQUIRE(dtype_ok(dtype), MQC_ERR_INVALID_VALUE, "mqc_qln_fwd: unknown dtype %d", dtype);
+  MQC_REQUIRE(rows >= 0 && d_model >= 0, MQC_ERR_INVALID_VALUE, "mqc_qln_fwd: negative size");
+  MQC_REQUIRE((flags & ~MQC_QLN_PADDED_COMPAT) == 0, MQC_ERR_INVALID_VALUE,
+              "mqc_qln_fwd: unknown flags 0x%x", flags);
+  if (rows == 0) return MQC_OK;
+  MQC_REQUIRE(d_model >= 1, MQC_ERR_INVALID_VALUE, "mqc_qln_fwd: d_model must be >= 1");
+  MQC_REQUIRE(d_model <= int64_t(kMaxRowThreads) * kVpt, MQC_ERR_UNSUPPORTED,
+              "mqc_qln_fwd: d_model=%lld > %d", (long long)d_model, kMaxRowThreads * kVpt);
+  MQC_REQUIRE(rows <= 0x7fffffff, MQC_ERR_UNSUPPORTED, "mqc_qln_fwd: too many rows");
+  MQC_REQUIRE(q && gamma && beta && out, MQC_ERR_INVALID_VALUE, "mqc_qln_fwd: null pointer");
+  const uintptr_t al = dtype == MQC_DTYPE_F32 ? 16 : 8;
+  MQC_REQUIRE(aligned(q, al) && aligned(out, al) && aligned(beta, 16), MQC_ERR_MISALIGNED,
+              "mqc_qln_fwd: q/out must be %d-byte and beta 16-byte aligned", int(al));
+  const int D = int(d_model);
+  int threads = (D + kVpt - 1) / kVpt;
+  threads = (threads + 31) / 32 * 32;
+  if (threads < 32) threads = 32;
+  int pad = 0;
+  if (flags & MQC_QLN_PADDED_COMPAT) {
+    int block = 1;
+    while (block < D) block <<= 1;
+    pad = block - D;
+  }
+  cudaStream_t st = as_stream(stream);
+  if (dtype == MQC_DTYPE_F32) {
+    qln_fwd_kernel<float><<<unsigned(rows), threads, 0, st>>>(
+        static_cast<const float*>(q), gamma, beta, static_cast<float*>(out), mean, rstd, D, eps,
+        pad);
+  } else {
+    qln_fwd_kernel<__nv_bfloat16><<<unsigned(rows), threads, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(q), gamma, beta, static_cast<__nv_bfloat16*>(out), mean,
+        rstd, D, eps, pad);
+  }
+  return check_launch("mqc_qln_fwd");
+}
+
+extern "C" size_t mqc_qln_bwd_workspace_size(int64_t rows, int64_t d_model) {
+  if (rows <= 0 || d_model <= 0) return 0;
+  return size_t(qln_bwd_parts(rows)) * size_t(d_model) * 5 * sizeof(float);
+}
+
+extern "C" int mqc_qln_bwd(const void* q, const float* gamma, const void* dout, const float* mean,
+                           const float* rstd, void* dq, float* dgamma, float* dbeta,
+                           void* workspace, size_t workspace_bytes, int64_t rows, int64_t d_model,
+                           float eps, int dtype, void* stream) {
+  clear_error();
+  MQC_REQUIRE(dtype_ok(dtype), MQC_ERR_INVALID_VALUE, "mqc_qln_bwd: unknown dtype %d", dtype);
+  MQC_REQUIRE(rows >= 0 && d_model >= 1, MQC_ERR_INVALID_VALUE, "mqc_qln_bwd: bad size");
+  MQC_REQUIRE(d_model <= 1024 * kVptB, MQC_ERR_UNSUPPORTED, "mqc_qln_bwd: d_model=%lld > %d",
+              (long long)d_model, 1024 * kVptB);
+  MQC_REQUIRE(q && gamma && dout && mean && rstd && dq && dgamma && dbeta, MQC_ERR_INVALID_VALUE,
+              "mqc_qln_bwd: null pointer");
+  const size_t need = mqc_qln_bwd_workspace_size(rows, d_model);
+  MQC_REQUIRE(rows == 0 || (workspace != nullptr && workspace_bytes >= need), MQC_ERR_INVALID_VALUE,
+              "mqc_qln_bwd: workspace of %zu bytes required (got %zu)", need, workspace_bytes);
+  const uintptr_t al = dtype == MQC_DTYPE_F32 ? 16 : 8;
+  MQC_REQUIRE(aligned(q, al) && aligned(dout, al) && aligned(dq, al) && aligned(workspace, 16),
+              MQC_ERR_MISALIGNED, "mqc_qln_bwd: misaligned pointer");
+  const int D = int(d_model);
+  cudaStream_t st = as_stream(stream);
+  if (rows == 0) {
+    cudaMemsetAsync(dgamma, 0, size_t(D) * 4, st);
+    cudaMemsetAsync(dbeta, 0, size_t(D) * 16, st);
+    return check_launch("mqc_qln_bwd");
+  }
+  int threads = (D + kVptB - 1) / kVptB;
+  threads = (threads + 31) / 32 * 32;
+  const int parts = qln_bwd_parts(rows);
+  float* partial = static_cast<float*>(workspace);
+  if (dtype == MQC_DTYPE_F32) {
+    qln_bwd_kernel<float><<<parts, threads, 0, st>>>(
+        static_cast<const float*>(q), gamma, static_cast<const float*>(dout), mean, rstd,
+        static_cast<float*>(dq), partial, rows, D, eps);
+  } else {
+    qln_bwd_kernel<__nv_bfloat16><<<parts, threads, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(q), gamma, static_cast<const __nv_bfloat16*>(dout), mean,
+        rstd, static_cast<__nv_bfloat16*>(dq), partial, rows, D, eps);
+  }
+  qln_bwd_reduce_kernel<<<(5 * D + 255) / 256, 256, 0, st>>>(partial, dgamma, dbeta, parts, D);
+  return check_launch("mqc_qln_bwd");
+}

@@ -1,0 +1,352 @@
+// Fused Cayley + quaternion selective scan, forward (sm_100a).
+//
+// Reference path: QuaternionMamba2Block._ssm_forward
+// (mambaqc/models/quaternion_mamba2_block.py:214-228) materialises
+// z = Delta * Lambda and q = Cayley(z) as [B,T,D,N,4] tensors and then runs
+// ssm_forward_fused (mambaqc/kernels/ssm_fused.py:340-401), a Python loop over T
+// that launches one step kernel per timestep and round-trips the state h through
+// HBM every step. Here one launch does the whole scan:
+//
+//  * every (batch b, channel d, state n) lane is an independent recurrence over
+//    t; the fp32 state h[b,d,n] lives in registers for all T steps;
+//  * q_t is formed in registers from Delta[b,t,d] and per-(d,n) constants
+//    derived from Lambda[d,n] (closed-form Cayley, one reciprocal) -- z and q
+//    are never written anywhere;
+//  * a thread owns G states of one channel (n = ng + NG*i, i < G) and NG
+//    consecutive lanes cover one channel's N states; the readout
+//    y_t = sum_n C_t (x) h_t is summed in-thread over G and then across the NG
+//    lanes with a warp-shuffle reduce-scatter;
+//  * channels shared B_t/C_t ([B,T,N,4]) are staged per chunk of TC timesteps
+//    into shared memory by the bulk-copy (TMA) engine, double-buffered on
+//    mbarriers; per-channel B/C and explicit q stream from global with 16-byte
+//    (fp32) or 8-byte (bf16) vector loads;
+//  * Delta and x (or S) of the next chunk are loaded cooperatively into
+//    registers while the current chunk computes, then parked in shared memory;
+//  * the grid gives every SM the same number of channels (balanced partition of
+//    each batch's channels), one CTA per SM.
+//
+// Every device-side wait is bounded; on timeout the kernel ORs
+// MQC_DEVICE_STATUS_TIMEOUT into the caller's status word, drains its own bulk
+// copies in flight (bounded) and returns.
+#include "ssm_scan_common.cuh"
+
+namespace mqc {
+namespace scan {
+
+template <typename T, int G, int NG, bool BC_SHARED, bool S_REAL, bool Q_GIVEN>
+__global__ void __launch_bounds__(G == 8 ? kMaxThreadsG8 : kMaxThreads, 1)
+    ssm_scan_fwd_kernel(const FwdParams p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  const SmemLayout L = smem_layout<T, S_REAL>(p.tc, p.cpb, p.N, BC_SHARED);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);
+  T* sB = reinterpret_cast<T*>(smem_raw + L.off_b);
+  T* sC = reinterpret_cast<T*>(smem_raw + L.off_c);
+  float* sD = reinterpret_cast<float*>(smem_raw + L.off_delta);  // [2][tc][cpb]
+  float* sS = reinterpret_cast<float*>(smem_raw + L.off_s);      // [2][tc][cpb][S_REAL?1:4]
+
+  const int tid = threadIdx.x;
+  const int ng = tid % NG;
+  const int cl = tid / NG;
+  const int b = blockIdx.y;
+  const int c0 = int((int64_t(p.D) * blockIdx.x) / p.nb);
+  const int c1 = int((int64_t(p.D) * (blockIdx.x + 1)) / p.nb);
+  const int nch = c1 - c0;
+  const bool active = cl < nch;
+  const int c = active ? c0 + cl : c0;
+  const int T_ = p.T, D = p.D, N = p.N, tc = p.tc, cpb = p.cpb;
+  const int nchunks = (T_ + tc - 1) / tc;
+  constexpr int SW = S_REAL ? 1 : 4;
+
+  const T* __restrict__ gdelta = static_cast<const T*>(p.delta);
+  const T* __restrict__ gs = static_cast<const T*>(p.s);
+  const T* __restrict__ gB = static_cast<const T*>(p.Bm);
+  const T* __restrict__ gC = static_cast<const T*>(p.Cm);
+  const T* __restrict__ gq = static_cast<const T*>(p.q);
+
+  // ---- per-lane constants and state ----
+  float4 h[G];
+  LamConst lc[G];
+  bool nok[G];
+#pragma unroll
+  for (int i = 0; i < G; ++i) {
+    const int n = ng + NG * i;
+    nok[i] = n < N;
+    h[i] = f4_zero();
+    lc[i] = LamConst{0.f, 0.f, 0.f, 0.f, 0.f};
+    if (active && nok[i]) {
+      if (p.h0 != nullptr) h[i] = QIO<float>::ld(p.h0 + ((int64_t(b) * D + c) * N + n) * 4);
+      if (!Q_GIVEN) lc[i] = make_lam_const(QIO<float>::ld(p.lam + (int64_t(c) * N + n) * 4));
+    }
+  }
+
+  // ---- bulk-copy ring for shared B/C ----
+  const uint32_t bc_row_bytes = uint32_t(N) * 4 * sizeof(T);
+  auto issue_chunk = [&](int k) {
+    const int stg = k % kStages;
+    const int t0 = k * tc;
+    const int len = min(tc, T_ - t0);
+    const uint32_t bytes = uint32_t(len) * bc_row_bytes;
+    mbar_arrive_expect_tx(&full[stg], 2 * bytes);
+    const int64_t goff = (int64_t(b) * T_ + t0) * N * 4;
+    bulk_g2s(sB + int64_t(stg) * tc * N * 4, gB + goff, bytes, &full[stg]);
+    bulk_g2s(sC + int64_t(stg) * tc * N * 4, gC + goff, bytes, &full[stg]);
+  };
+  auto drain = [&](int first, int last) {  // wait (bounded) for chunks first..last
+    for (int k = first; k <= last && k < nchunks; ++k)
+      mbar_wait_bounded(&full[k % kStages], uint32_t((k / kStages) & 1), kDrainPollLimit);
+  };
+
+  if (BC_SHARED) {
+    if (tid == 0) {
+      for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
+      fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0)
+      for (int k = 0; k < kStages && k < nchunks; ++k) issue_chunk(k);
+  }
+
+  // ---- cooperative staging of delta and s, one chunk ahead ----
+  const int nthreads = blockDim.x;
+  const int dx_elems = tc * cpb;  // per tensor per chunk
+  const int dx_per_thread = (dx_elems + nthreads - 1) / nthreads;
+  float rd[kMaxDxPerThread];
+  float4 rs[kMaxDxPerThread];
+  auto load_dx = [&](int k) {
+    const int t0 = k * tc;
+#pragma unroll
+    for (int j = 0; j < kMaxDxPerThread; ++j) {
+      rd[j] = 0.f;
+      rs[j] = f4_zero();
+      const int e = tid + j * nthreads;
+      if (j < dx_per_thread && e < dx_elems) {
+        const int tt = e / cpb, cc = e % cpb;
+        const int t = t0 + tt;
+        if (t < T_ && cc < nch) {
+          const int64_t row = int64_t(b) * T_ + t;
+          if (!Q_GIVEN) rd[j] = to_f(gdelta[row * D + c0 + cc]);
+          if (S_REAL) rs[j].x = to_f(gs[row * D + c0 + cc]);
+          else rs[j] = QIO<T>::ld(gs + (row * D + c0 + cc) * 4);
+        }
+      }
+    }
+  };
+  auto store_dx = [&](int buf) {
+#pragma unroll
+    for (int j = 0; j < kMaxDxPerThread; ++j) {
+      const int e = tid + j * nthreads;
+      if (j < dx_per_thread && e < dx_elems) {
+        sD[buf * dx_elems + e] = rd[j];
+        if (S_REAL) sS[buf * dx_elems + e] = rs[j].x;
+        else reinterpret_cast<float4*>(sS)[buf * dx_elems + e] = rs[j];
+      }
+    }
+  };
+
+  load_dx(0);
+  store_dx(0);
+  bool ok = true;
+  if (BC_SHARED) ok = mbar_wait_bounded(&full[0], 0u, p.wait_limit);
+  if (__syncthreads_or(!ok)) {
+    if (tid == 0) {
+      report_status(p.status, MQC_DEVICE_STATUS_TIMEOUT);
+      if (BC_SHARED) drain(0, kStages - 1);
+    }
+    return;
+  }
+
+  const float eps = p.eps;
+  for (int k = 0; k < nchunks; ++k) {
+    const int buf = k & 1;
+    const int stg = k % kStages;
+    const int t0 = k * tc;
+    const int len = min(tc, T_ - t0);
+    if (k + 1 < nchunks) load_dx(k + 1);
+
+    const float* dD = sD + buf * dx_elems;
+    const float* dS = sS + buf * dx_elems * SW;
+    const T* cB = sB + int64_t(stg) * tc * N * 4;
+    const T* cC = sC + int64_t(stg) * tc * N * 4;
+
+    for (int tt = 0; tt < len; ++tt) {
+      const int t = t0 + tt;
+      const int cli = active ? cl : 0;
+      const float dl = active ? dD[tt * cpb + cli] : 0.f;
+      const float dl2 = dl * dl;
+      float4 sv;
+      if (S_REAL) sv = make_float4(dS[tt * cpb + cli], 0.f, 0.f, 0.f);
+      else sv = reinterpret_cast<const float4*>(dS)[tt * cpb + cli];
+      if (!active) sv = f4_zero();
+      const int64_t lane_base = ((int64_t(b) * T_ + t) * D + c) * N;  // per-channel [b,t,c,0]
+      float4 yacc = f4_zero();
+#pragma unroll
+      for (int i = 0; i < G; ++i) {
+        const int n = ng + NG * i;
+        float4 Bv = f4_zero(), Cv = f4_zero();
+        if (nok[i]) {
+          if (BC_SHARED) {
+            Bv = QIO<T>::lds(cB + (tt * N + n) * 4);
+            Cv = QIO<T>::lds(cC + (tt * N + n) * 4);
+          } else if (active) {
+            Bv = QIO<T>::ld_stream(gB + (lane_base + n) * 4);
+            Cv = QIO<T>::ld_stream(gC + (lane_base + n) * 4);
+          }
+        }
+        float4 qv;
+        if (Q_GIVEN) {
+          qv = (active && nok[i]) ? QIO<T>::ld_stream(gq + (lane_base + n) * 4)
+                                  : make_float4(1.f, 0.f, 0.f, 0.f);
+        } else {
+          qv = cayley_from_const(dl, dl2, lc[i], eps);
+        }
+        float4 inj;
+        if (S_REAL) inj = make_float4(sv.x * Bv.x, sv.x * Bv.y, sv.x * Bv.z, sv.x * Bv.w);
+        else inj = qmul(Bv, sv);
+        h[i] = qmul_acc(qv, h[i], inj);
+        yacc = qmul_acc(Cv, h[i], yacc);
+      }
+      // skip term D * S and the store, by the lanes that hold the sums
+      float dsk = 0.f;
+      if (active && ng < 4)
+        dsk = __ldg(p.dskip + int64_t(b) * p.dsb + int64_t(t) * p.dst + int64_t(c) * p.dsd);
+      reduce_store_y<T, NG>(yacc, sv, dsk, ng, active,
+                            static_cast<T*>(p.y) + ((int64_t(b) * T_ + t) * D + c) * 4);
+    }
+
+    if (k + 1 < nchunks) store_dx(buf ^ 1);
+    ok = true;
+    if (BC_SHARED && k + 1 < nchunks)
+      ok = mbar_wait_bounded(&full[(k + 1) % kStages], uint32_t(((k + 1) / kStages) & 1),
+                             p.wait_limit);
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) {
+        report_status(p.status, MQC_DEVICE_STATUS_TIMEOUT);
+        if (BC_SHARED) drain(k + 1, k + kStages - 1);
+      }
+      return;
+    }
+    if (BC_SHARED && tid == 0 && k + kStages < nchunks) issue_chunk(k + kStages);
+  }
+
+  if (p.hT != nullptr && active) {
+#pragma unroll
+    for (int i = 0; i < G; ++i) {
+      const int n = ng + NG * i;
+      if (nok[i]) QIO<float>::st(p.hT + ((int64_t(b) * D + c) * N + n) * 4, h[i]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+template <typename T, int G, int NG, bool BC_SHARED, bool S_REAL, bool Q_GIVEN>
+int launch_fwd(const FwdParams& p0, cudaStream_t st) {
+  FwdParams p = p0;
+  const LaunchShape ls = choose_shape(p.B, p.T, p.D, p.N, NG, int(sizeof(T)), BC_SHARED,
+                                      S_REAL);
+  if (ls.threads == 0) return fail(MQC_ERR_UNSUPPORTED, "mqc_ssm_scan_fwd: %s", ls.why);
+  p.nb = ls.nb;
+  p.cpb = ls.cpb;
+  p.tc = ls.tc;
+  auto kern = ssm_scan_fwd_kernel<T, G, NG, BC_SHARED, S_REAL, Q_GIVEN>;
+  if (ls.smem > 48 * 1024) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(ls.smem));
+    if (e != cudaSuccess)
+      return fail(MQC_ERR_CUDA, "mqc_ssm_scan_fwd: smem attribute (%zu B): %s", ls.smem,
+                  cudaGetErrorString(e));
+  }
+  dim3 grid{unsigned(ls.nb), unsigned(p.B), 1u};
+  kern<<<grid, ls.threads, ls.smem, st>>>(p);
+  return check_launch("mqc_ssm_scan_fwd");
+}
+
+template <typename T, bool BC_SHARED, bool S_REAL, bool Q_GIVEN>
+int dispatch_ng(const FwdParams& p, cudaStream_t st) {
+  const int ng = lanes_per_channel(p.N);
+  switch (ng) {
+    case 1: return launch_fwd<T, 4, 1, BC_SHARED, S_REAL, Q_GIVEN>(p, st);
+    case 2: return launch_fwd<T, 4, 2, BC_SHARED, S_REAL, Q_GIVEN>(p, st);
+    case 4: return launch_fwd<T, 4, 4, BC_SHARED, S_REAL, Q_GIVEN>(p, st);
+    case 8: return launch_fwd<T, 4, 8, BC_SHARED, S_REAL, Q_GIVEN>(p, st);
+    case 16: return launch_fwd<T, 4, 16, BC_SHARED, S_REAL, Q_GIVEN>(p, st);
+    case 32:
+      if (p.N <= 128) return launch_fwd<T, 4, 32, BC_SHARED, S_REAL, Q_GIVEN>(p, st);
+      return launch_fwd<T, 8, 32, BC_SHARED, S_REAL, Q_GIVEN>(p, st);
+    default:
+      return fail(MQC_ERR_UNSUPPORTED, "mqc_ssm_scan_fwd: d_state=%d (supported 1..256)", p.N);
+  }
+}
+
+template <typename T>
+int dispatch_mode(const FwdParams& p, int flags, cudaStream_t st) {
+  const bool qg = flags & MQC_SSM_Q_GIVEN;
+  const bool sh = flags & MQC_SSM_BC_SHARED;
+  const bool sr = flags & MQC_SSM_S_REAL;
+  if (qg) {
+    if (sh) {
+      if (sr) return dispatch_ng<T, true, true, true>(p, st);
+      return dispatch_ng<T, true, false, true>(p, st);
+    }
+    if (sr) return dispatch_ng<T, false, true, true>(p, st);
+    return dispatch_ng<T, false, false, true>(p, st);
+  }
+  if (sh) {
+    if (sr) return dispatch_ng<T, true, true, false>(p, st);
+    return dispatch_ng<T, true, false, false>(p, st);
+  }
+  if (sr) return dispatch_ng<T, false, true, false>(p, st);
+  return dispatch_ng<T, false, false, false>(p, st);
+}
+
+}  // namespace scan
+}  // namespace mqc
+
+using namespace mqc;
+using namespace mqc::scan;
+
+extern "C" int mqc_ssm_scan_fwd(const mqc_ssm_scan_args* a, void* stream) {
+  clear_error();
+  FwdParams p{};
+  int rc = validate_and_fill(a, &p, "mqc_ssm_scan_fwd");
+  if (rc != MQC_OK || p.T == 0 || p.B == 0 || p.D == 0) return rc;
+  if (a->dtype == MQC_DTYPE_F32) return dispatch_mode<float>(p, a->flags, as_stream(stream));
+  return dispatch_mode<__nv_bfloat16>(p, a->flags, as_stream(stream));
+}
+
+extern "C" int mqc_ssm_step(const void* q, const void* Bm, const void* S, const void* Cm,
+                            const float* dskip, const float* h_prev, float* h_new, void* y,
+                            int64_t batch, int64_t channels, int64_t d_state, int dtype,
+                            void* stream) {
+  clear_error();
+  mqc_ssm_scan_args a{};
+  a.batch = batch;
+  a.seq_len = 1;
+  a.channels = channels;
+  a.d_state = d_state;
+  a.dtype = dtype;
+  a.flags = MQC_SSM_Q_GIVEN;
+  a.eps = 1e-6f;
+  a.q = q;
+  a.Bm = Bm;
+  a.Cm = Cm;
+  a.s = S;
+  a.dskip = dskip;
+  a.dskip_sb = channels;  // dskip [B, D]
+  a.dskip_st = 0;
+  a.dskip_sd = 1;
+  a.h0 = h_prev;
+  a.y = y;
+  a.hT = h_new;
+  a.status = nullptr;
+  a.wait_poll_limit = -1;
+  MQC_REQUIRE(h_prev != nullptr && h_new != nullptr, MQC_ERR_INVALID_VALUE,
+              "mqc_ssm_step: h_prev and h_new are required");
+  FwdParams p{};
+  int rc = validate_and_fill(&a, &p, "mqc_ssm_step");
+  if (rc != MQC_OK || p.B == 0 || p.D == 0) return rc;
+  if (dtype == MQC_DTYPE_F32) return dispatch_ng<float, false, false, true>(p, as_stream(stream));
+  return dispatch_ng<__nv_bfloat16, false, false, true>(p, as_stream(stream));
+}

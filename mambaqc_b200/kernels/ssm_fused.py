@@ -1,0 +1,162 @@
+"""Quaternion selective scan on the GPU: drop-in for ``mambaqc.kernels.ssm_fused``.
+
+Reference functions and their replacements:
+
+* ``ssm_step_fused(q, B, S, C, D, h_prev)`` (mambaqc/kernels/ssm_fused.py:258-337)
+  -> ``mqc_ssm_step``: one step, h' = q (x) h + B (x) S, y = sum_n C (x) h' + D*S.
+* ``ssm_forward_fused(q, B, S, C, D)`` (ssm_fused.py:340-401; a Python loop over
+  T with one kernel launch per step) -> one ``mqc_ssm_scan_fwd`` launch with the
+  state held in registers for all T steps.
+* ``ssm_scan_cayley(delta, Lambda, B, C, S, D)`` -- new: the fused form of
+  ``QuaternionMamba2Block._ssm_forward`` lines 214-228
+  (models/quaternion_mamba2_block.py): q_t = Cayley(delta_t * Lambda) is formed
+  in registers inside the scan, so neither z nor q is ever materialised.
+
+Shapes: B batch, T seq_len, D channels (d_inner), N d_state; quaternions on the
+last axis. B/C may be per-channel [B,T,D,N,4] (the reference block's layout) or
+shared by all channels [B,T,N,4]; S may be a quaternion signal [B,T,D,4] or a
+real one [B,T,D] (embedded as (x, 0, 0, 0), as the block does at :200-202).
+The state is fp32 in registers; inputs are float32 or bfloat16 (all the same).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from .. import _lib
+
+__all__ = ["ssm_step_fused", "ssm_forward_fused", "ssm_scan_cayley"]
+
+
+def _vec_align(dtype: torch.dtype) -> int:
+    return 16 if dtype == torch.float32 else 8
+
+
+def _prep(t: torch.Tensor, align: int) -> torch.Tensor:
+    return _lib.aligned_contig(t, align)
+
+
+def _skip_operand(D: torch.Tensor, bsz: int, seqlen: int, dm: int):
+    """fp32 skip weights and their (b, t, d) strides; accepts [D], [B,D] or [B,T,D] (any strides)."""
+    Df = D if D.dtype == torch.float32 else D.float()
+    if Df.dim() == 1:
+        assert Df.shape[0] == dm, f"D shape {tuple(D.shape)} vs channels {dm}"
+        return Df, 0, 0, Df.stride(0)
+    if Df.dim() == 2:
+        assert tuple(Df.shape) == (bsz, dm), f"D shape {tuple(D.shape)}"
+        return Df, Df.stride(0), 0, Df.stride(1)
+    assert tuple(Df.shape) == (bsz, seqlen, dm), f"D shape {tuple(D.shape)}"
+    return Df, Df.stride(0), Df.stride(1), Df.stride(2)
+
+
+def _run_scan(*, flags: int, q=None, delta=None, Lam=None, B, C, S, D, h0=None,
+              return_final_state=False, eps=1e-6, wait_poll_limit=-1):
+    ref = q if q is not None else delta
+    dt = ref.dtype
+    bsz, seqlen, dm = ref.shape[0], ref.shape[1], ref.shape[2]
+    shared = B.dim() == 4
+    ds = B.shape[2] if shared else B.shape[3]
+    s_real = S.dim() == 3
+    va = _vec_align(dt)
+    _lib.require_cuda(ref, B, C, S, D, h0, Lam, what="mambaqc_b200 scan")
+    for name, t in (("B", B), ("C", C), ("S", S)):
+        if t.dtype != dt:
+            raise TypeError(f"{name} dtype {t.dtype} != {dt}")
+    Bc = _prep(B, 16 if shared else va)
+    Cc = _prep(C, 16 if shared else va)
+    Sc = _prep(S, va)
+    qc = _prep(q, va) if q is not None else None
+    dc = _prep(delta, 4) if delta is not None else None
+    Lc = _prep(Lam.float(), 16) if Lam is not None else None
+    Df, dsb, dst, dsd = _skip_operand(D, bsz, seqlen, dm)
+    h0c = _prep(h0.float(), 16) if h0 is not None else None
+    y = torch.empty(bsz, seqlen, dm, 4, dtype=dt, device=ref.device)
+    hT = (torch.empty(bsz, dm, ds, 4, dtype=torch.float32, device=ref.device)
+          if return_final_state else None)
+    if shared:
+        flags |= _lib.MQC_SSM_BC_SHARED
+    if s_real:
+        flags |= _lib.MQC_SSM_S_REAL
+    status = _lib.status_word(ref.device)
+    a = _lib.SsmScanArgs(
+        batch=bsz, seq_len=seqlen, channels=dm, d_state=ds, dtype=_lib.dtype_code(ref),
+        flags=flags, eps=float(eps), reserved0=0,
+        delta=_lib.ptr(dc), lambda_=_lib.ptr(Lc), q=_lib.ptr(qc), Bm=Bc.data_ptr(),
+        Cm=Cc.data_ptr(), s=Sc.data_ptr(), dskip=Df.data_ptr(), dskip_sb=dsb, dskip_st=dst,
+        dskip_sd=dsd, h0=_lib.ptr(h0c), y=y.data_ptr(), hT=_lib.ptr(hT), status=status.data_ptr(),
+        wait_poll_limit=int(wait_poll_limit))
+    with torch.cuda.device(ref.device):
+        _lib.call("mqc_ssm_scan_fwd", ctypes.byref(a), _lib.stream_ptr(ref.device))
+    if _lib.sync_checks_enabled():
+        _lib.check_device_status(ref.device)
+    return y, hT
+
+
+def ssm_scan_cayley(delta: torch.Tensor, Lambda: torch.Tensor, B: torch.Tensor,
+                    C: torch.Tensor, S: torch.Tensor, D: torch.Tensor,
+                    h0: torch.Tensor | None = None, eps: float = 1e-6,
+                    return_final_state: bool = False, wait_poll_limit: int = -1):
+    """Fused Cayley + quaternion selective scan.
+
+    delta [B,T,D] (positive step sizes), Lambda [D,N,4] (fp32 continuous
+    dynamics), B/C [B,T,N,4] shared or [B,T,D,N,4] per-channel, S [B,T,D] real or
+    [B,T,D,4], D skip [D] / [B,D] / [B,T,D]. Computes, per (b, d, n),
+    q_t = (1 - delta_t Lambda/2)^-1 (x) (1 + delta_t Lambda/2) and
+    h_t = q_t (x) h_{t-1} + B_t (x) S_t, y_t = sum_n C_t (x) h_t + D S_t.
+
+    Returns y [B,T,D,4] (dtype of delta), plus the final fp32 state
+    h_T [B,D,N,4] when ``return_final_state``.
+    """
+    assert delta.dim() == 3, f"delta must be [B,T,D], got {tuple(delta.shape)}"
+    assert Lambda.dim() == 3 and Lambda.shape[-1] == 4, "Lambda must be [D,N,4]"
+    bsz, seqlen, dm = delta.shape
+    ds = Lambda.shape[1]
+    assert Lambda.shape[0] == dm
+    if B.dim() == 4:
+        assert tuple(B.shape) == (bsz, seqlen, ds, 4) and B.shape == C.shape
+    else:
+        assert tuple(B.shape) == (bsz, seqlen, dm, ds, 4) and B.shape == C.shape
+    assert tuple(S.shape) in ((bsz, seqlen, dm), (bsz, seqlen, dm, 4))
+    y, hT = _run_scan(flags=0, delta=delta, Lam=Lambda, B=B, C=C, S=S, D=D, h0=h0,
+                      return_final_state=return_final_state, eps=eps,
+                      wait_poll_limit=wait_poll_limit)
+    return (y, hT) if return_final_state else y
+
+
+def ssm_forward_fused(q: torch.Tensor, B: torch.Tensor, S: torch.Tensor, C: torch.Tensor,
+                      D: torch.Tensor, h0: torch.Tensor | None = None,
+                      return_final_state: bool = False):
+    """Full scan over time with explicit operators q [B,T,D,N,4] (zero initial state).
+
+    Mirrors ``ssm_forward_fused`` (mambaqc/kernels/ssm_fused.py:340-401): returns
+    y [B,T,D,4]; ``h0`` and ``return_final_state`` are optional extensions.
+    """
+    assert q.dim() == 5 and q.shape[-1] == 4
+    y, hT = _run_scan(flags=_lib.MQC_SSM_Q_GIVEN, q=q, B=B, C=C, S=S, D=D, h0=h0,
+                      return_final_state=return_final_state)
+    return (y, hT) if return_final_state else y
+
+
+def ssm_step_fused(q: torch.Tensor, B: torch.Tensor, S: torch.Tensor, C: torch.Tensor,
+                   D: torch.Tensor, h_prev: torch.Tensor):
+    """One step: (h_new, y). Mirrors ``ssm_step_fused`` (ssm_fused.py:258-337)."""
+    bsz, dm, ds, _ = q.shape
+    assert B.shape == (bsz, dm, ds, 4)
+    assert S.shape == (bsz, dm, 4)
+    assert C.shape == (bsz, dm, ds, 4)
+    assert D.shape == (bsz, dm)
+    assert h_prev.shape == (bsz, dm, ds, 4)
+    _lib.require_cuda(q, B, S, C, D, h_prev, what="ssm_step_fused")
+    va = _vec_align(q.dtype)
+    qc, Bc, Cc, Sc = (_prep(t, va) for t in (q, B, C, S))
+    Dc = _prep(D.float(), 4)
+    hp = _prep(h_prev.float(), 16)
+    h_new = torch.empty(bsz, dm, ds, 4, dtype=torch.float32, device=q.device)
+    y = torch.empty(bsz, dm, 4, dtype=q.dtype, device=q.device)
+    with torch.cuda.device(q.device):
+        _lib.call("mqc_ssm_step", qc.data_ptr(), Bc.data_ptr(), Sc.data_ptr(), Cc.data_ptr(),
+                  Dc.data_ptr(), hp.data_ptr(), h_new.data_ptr(), y.data_ptr(), bsz, dm, ds,
+                  _lib.dtype_code(qc), _lib.stream_ptr(q.device))
+    return h_new.to(h_prev.dtype), y

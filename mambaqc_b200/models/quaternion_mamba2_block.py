@@ -1,0 +1,94 @@
+"""QuaternionMamba2Block with the GPU fused scan: drop-in for
+``mambaqc.models.quaternion_mamba2_block.QuaternionMamba2Block``.
+
+Constructor signature, submodule names, parameter names/shapes and the order
+of random initialisation follow the reference (models/quaternion_mamba2_block.py:55-122),
+so a reference state_dict loads unchanged and ``torch.manual_seed(s)`` gives the
+same initial weights. The forward follows :124-230 with two differences:
+
+* ``_ssm_forward`` calls ``ssm_scan_cayley`` (one fused kernel) instead of
+  materialising z = Delta*Lambda and q = Cayley(z) and looping over time
+  (:214-228);
+* the output gate uses ``sigmoid(z[..., :d_model])``: the reference multiplies
+  a d_inner-wide gate with the d_model-wide projection (:160-161), which fails
+  for expand_factor != 1; its Lite block slices the same way
+  (quaternion_mamba2_lite_block.py:163).
+
+Projections, the causal conv and activations stay dense PyTorch ops (cuBLAS /
+cuDNN); the quaternion path (scan, LayerNorm) runs in ``libmambaqc_b200.so``.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from mambaqc_b200.kernels.ssm_fused import ssm_scan_cayley
+from mambaqc_b200.layers.causal_conv1d import CausalConv1d
+from mambaqc_b200.layers.quaternion_linear import (
+    quaternion_to_real_projection,
+    real_to_quaternion_projection,
+)
+from mambaqc_b200.layers.quaternion_norm import QuaternionLayerNorm
+
+__all__ = ["QuaternionMamba2Block"]
+
+
+class QuaternionMamba2Block(nn.Module):
+    """Single Quaternion Mamba-2 block: [batch, seq_len, d_model] -> same shape."""
+
+    def __init__(self, d_model: int, d_state: int = 64, d_conv: int = 4,
+                 expand_factor: int = 2, dt_rank: str | int = "auto", bias: bool = False):
+        super().__init__()
+        self.d_model = d_model
+        self.d_state = d_state
+        self.d_conv = d_conv
+        self.d_inner = d_model * expand_factor
+        self.dt_rank = max(16, d_model // 16) if dt_rank == "auto" else dt_rank
+        self.in_proj = nn.Linear(d_model, self.d_inner * 2, bias=bias)
+        self.conv1d = CausalConv1d(self.d_inner, kernel_size=d_conv, bias=True)
+        self.Lambda_alpha = nn.Parameter(torch.randn(self.d_inner, d_state) * 0.5 + 1.0)
+        self.Lambda_imag = nn.Parameter(torch.randn(self.d_inner, d_state, 3) * 0.1)
+        self.dt_proj = nn.Linear(self.d_inner, self.d_inner, bias=True)
+        self.B_proj = real_to_quaternion_projection(self.d_inner, self.d_inner * d_state, bias=False)
+        self.C_proj = real_to_quaternion_projection(self.d_inner, self.d_inner * d_state, bias=False)
+        self.D = nn.Parameter(torch.ones(self.d_inner))
+        self.gate_proj = nn.Linear(self.d_inner, self.d_inner, bias=False)
+        self.norm = QuaternionLayerNorm(self.d_inner, eps=1e-5)
+        self.out_proj = quaternion_to_real_projection(self.d_inner, d_model, bias=bias)
+        # Optional fixed Lambda [d_inner, d_state, 4] used instead of the
+        # (-softplus(alpha), tanh(imag)) parameterisation (not part of state_dict).
+        self.lambda_override: torch.Tensor | None = None
+
+    def ssm_lambda(self) -> torch.Tensor:
+        """Lambda [d_inner, d_state, 4] = (-softplus(alpha), tanh(imag)) (block.py:206-212)."""
+        if self.lambda_override is not None:
+            return self.lambda_override
+        real = -F.softplus(self.Lambda_alpha.float())
+        imag = torch.tanh(self.Lambda_imag.float())
+        return torch.cat([real.unsqueeze(-1), imag], dim=-1)
+
+    def forward(self, x: torch.Tensor, return_ssm_state: bool = False):
+        xz = self.in_proj(x)
+        x_inner, z = xz.chunk(2, dim=-1)
+        x_act = F.silu(self.conv1d(x_inner))
+        y_quat, h_T = self._ssm_forward(x_act, return_state=True)
+        y_real = self.out_proj(self.norm(y_quat))
+        out = x + torch.sigmoid(z[..., : self.d_model]) * y_real
+        return (out, h_T) if return_ssm_state else out
+
+    def _ssm_forward(self, x: torch.Tensor, return_state: bool = False):
+        bsz, seqlen, d_inner = x.shape
+        delta = F.softplus(self.dt_proj(x))
+        Bq = self.B_proj(x).view(bsz, seqlen, d_inner, self.d_state, 4)
+        Cq = self.C_proj(x).view(bsz, seqlen, d_inner, self.d_state, 4)
+        s_real = torch.sigmoid(self.gate_proj(x)) * x
+        dt = Bq.dtype
+        y, h_T = ssm_scan_cayley(delta.to(dt), self.ssm_lambda(), Bq, Cq.to(dt), s_real.to(dt),
+                                 self.D, return_final_state=True)
+        return (y, h_T) if return_state else y
+
+    def extra_repr(self) -> str:
+        return (f"d_model={self.d_model}, d_state={self.d_state}, d_inner={self.d_inner}, "
+                f"d_conv={self.d_conv}, dt_rank={self.dt_rank}")

@@ -1,0 +1,145 @@
+"""C-ABI checks that need no GPU: the library loads, exports every symbol that
+include/mambaqc_b200.h declares, and rejects bad arguments before touching the
+device (validation happens on the host, so these calls never launch)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from mambaqc_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "mambaqc_b200.h"
+
+INVALID, MISALIGNED, UNSUPPORTED = 1, 2, 3
+
+# The validation tests pass fake device pointers that must be rejected on the
+# host. They are kept off machines with a GPU, so that a future bug in the
+# validation can never turn one of them into a launch on a bogus address.
+no_gpu = pytest.mark.skipif(torch.cuda.is_available(),
+                            reason="fake-pointer validation tests run only on GPU-less hosts")
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^MQC_API\s+[\w\s\*]+?\b(mqc_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    for expected in ("mqc_qmul", "mqc_cayley", "mqc_prefix_prod", "mqc_ssm_scan_fwd",
+                     "mqc_ssm_step", "mqc_qln_fwd", "mqc_qln_bwd"):
+        assert expected in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_symbols():
+        assert hasattr(lib, name), f"{name} declared in the header but not exported"
+    # and the Python binding knows every declared entry point
+    assert set(declared_symbols()) <= set(_lib.exported_symbols())
+
+
+def test_version_and_status_strings():
+    lib = _lib.load()
+    assert lib.mqc_version().decode().count(".") == 2
+    assert lib.mqc_status_string(0) == b"success"
+    assert b"timed out" in lib.mqc_status_string(5)
+    assert lib.mqc_status_string(999) == b"unknown status"
+
+
+def test_struct_layout_matches_header():
+    # 4 int64 + 4 int32 + 7 pointers + 3 int64 + 4 pointers + 1 int64 on LP64
+    assert ctypes.sizeof(_lib.SsmScanArgs) == 4 * 8 + 4 * 4 + 7 * 8 + 3 * 8 + 4 * 8 + 8
+
+
+@no_gpu
+def test_elementwise_argument_validation_without_gpu():
+    lib = _lib.load()
+    fake = 0x10000  # never dereferenced: validation fails before any launch
+    assert lib.mqc_qmul(fake, fake, fake, 4, 7, None) == INVALID
+    assert b"dtype" in lib.mqc_last_error()
+    assert lib.mqc_qmul(fake, fake, fake, -1, 0, None) == INVALID
+    assert lib.mqc_qmul(None, fake, fake, 4, 0, None) == INVALID
+    assert lib.mqc_qmul(fake + 4, fake, fake, 4, 0, None) == MISALIGNED
+    assert lib.mqc_qinv(fake, fake + 2, 4, 1e-6, 1, None) == MISALIGNED
+    assert lib.mqc_cayley(fake, fake, 0, 1e-6, 0, None) == 0  # empty input is a no-op
+    assert lib.mqc_prefix_prod(fake, fake, 1, 4, -3, 0, None) == INVALID
+    assert lib.mqc_prefix_prod(fake + 4, fake, 1, 4, 3, 0, None) == MISALIGNED
+
+
+@no_gpu
+def test_scan_argument_validation_without_gpu():
+    lib = _lib.load()
+    fake = 0x10000
+    base = dict(batch=2, seq_len=8, channels=4, d_state=16, dtype=0, flags=0, eps=1e-6,
+                reserved0=0, delta=fake, lambda_=fake, q=None, Bm=fake, Cm=fake, s=fake,
+                dskip=fake, dskip_sb=0, dskip_st=0, dskip_sd=1, h0=None, y=fake, hT=None,
+                status=None, wait_poll_limit=-1)
+
+    def call(**kw):
+        a = _lib.SsmScanArgs(**{**base, **kw})
+        return lib.mqc_ssm_scan_fwd(ctypes.byref(a), None)
+
+    assert call(dtype=3) == INVALID
+    assert call(flags=0x80) == INVALID
+    assert call(d_state=300) == UNSUPPORTED
+    assert b"d_state" in lib.mqc_last_error()
+    assert call(delta=None) == INVALID
+    assert call(flags=_lib.MQC_SSM_Q_GIVEN, q=None) == INVALID
+    assert call(y=fake + 4) == MISALIGNED
+    assert call(flags=_lib.MQC_SSM_BC_SHARED, Bm=fake + 8, dtype=1) == MISALIGNED
+    assert call(flags=_lib.MQC_SSM_BC_SHARED, dtype=1, d_state=15) == UNSUPPORTED
+    assert call(dskip=None) == INVALID
+    assert call(batch=70000) == UNSUPPORTED
+    assert call(seq_len=0) == 0  # nothing to do
+
+
+@no_gpu
+def test_layernorm_argument_validation_without_gpu():
+    lib = _lib.load()
+    fake = 0x10000
+    assert lib.mqc_qln_fwd(fake, fake, fake, fake, None, None, 4, 8, 1e-5, 0x10, 0, None) == INVALID
+    assert lib.mqc_qln_fwd(fake, fake, fake, fake, None, None, 4, 100000, 1e-5, 0, 0, None) == UNSUPPORTED
+    assert lib.mqc_qln_fwd(fake + 4, fake, fake, fake, None, None, 4, 8, 1e-5, 0, 0, None) == MISALIGNED
+    need = lib.mqc_qln_bwd_workspace_size(64, 8)
+    assert need > 0 and lib.mqc_qln_bwd_workspace_size(0, 8) == 0
+    assert lib.mqc_qln_bwd(fake, fake, fake, fake, fake, fake, fake, fake, fake, need - 1, 64, 8,
+                           1e-5, 0, None) == INVALID
+    assert b"workspace" in lib.mqc_last_error()
+
+
+def test_python_api_has_no_cpu_path():
+    from mambaqc_b200.kernels import (cayley_discretization_fused, parallel_scan_quaternion,
+                                      quaternion_multiply, ssm_scan_cayley)
+    from mambaqc_b200.layers import QuaternionLayerNorm
+    p = torch.randn(3, 4)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        quaternion_multiply(p, p)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        cayley_discretization_fused(torch.zeros(1, 1, 1, 1, 4))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        parallel_scan_quaternion(torch.zeros(1, 2, 1, 1, 4))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        QuaternionLayerNorm(4)(torch.zeros(1, 1, 4, 4))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ssm_scan_cayley(torch.ones(1, 2, 3), torch.zeros(3, 4, 4), torch.zeros(1, 2, 4, 4),
+                        torch.zeros(1, 2, 4, 4), torch.zeros(1, 2, 3), torch.ones(3))
+
+
+def test_reference_preconditions_raise_assertion():
+    from mambaqc_b200.kernels import (cayley_discretization_fused, quaternion_layer_norm_fused,
+                                      quaternion_multiply, ssm_step_fused)
+    with pytest.raises(AssertionError):
+        quaternion_multiply(torch.zeros(3, 4), torch.zeros(2, 4))
+    with pytest.raises(AssertionError):
+        quaternion_multiply(torch.zeros(3, 3), torch.zeros(3, 3))
+    with pytest.raises(AssertionError):
+        cayley_discretization_fused(torch.zeros(2, 3, 4))
+    with pytest.raises(AssertionError):
+        quaternion_layer_norm_fused(torch.zeros(1, 2, 3, 4), torch.ones(4), torch.zeros(3, 4))
+    with pytest.raises(AssertionError):
+        ssm_step_fused(torch.zeros(1, 2, 3, 4), torch.zeros(1, 2, 3, 4), torch.zeros(1, 2, 3),
+                       torch.zeros(1, 2, 3, 4), torch.zeros(1, 2), torch.zeros(1, 2, 3, 4))

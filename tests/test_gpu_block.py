@@ -1,0 +1,40 @@
+"""Config 1: one QuaternionMamba2Block forward (fp32), d_model=128, d_state=16,
+d_conv=4, expand_factor=2, batch=2, seq_len=256, default torch init under seed 0,
+Lambda overridden with Re = -exp(U(log 1e-3, log 1e-1)), Im ~ N(0, 0.5). The
+block output and the final SSM state are compared with the fp64 CPU oracle of the
+reference block (same weights), plus the golden block made by the reference."""
+
+import pytest
+import torch
+
+from oracle import ref
+from tests.gpu_util import DEV, RTOL_F32, gen, make_lambda, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+from mambaqc_b200.models import QuaternionMamba2Block  # noqa: E402
+
+
+def test_golden_block(golden):
+    c = golden["block_f64"]
+    blk = QuaternionMamba2Block(16, d_state=4).to(DEV)
+    blk.load_state_dict({k: v.float() for k, v in c["state_dict"].items()})
+    with torch.no_grad():
+        out = blk(c["x"].to(DEV, torch.float32))
+    assert rel_l2(out, c["out"]) < RTOL_F32
+
+
+def test_config1_block_forward_and_state():
+    torch.manual_seed(0)
+    blk = QuaternionMamba2Block(128, d_state=16, d_conv=4, expand_factor=2)
+    g = gen(0)
+    x = torch.randn(2, 256, 128, generator=g)
+    lam = make_lambda(256, 16, g)
+    params = {k: v.double() for k, v in blk.state_dict().items()}
+    out_ref, h_ref = ref.block_forward(params, x.double(), d_state=16, Lam=lam, return_state=True)
+    blk = blk.to(DEV)
+    blk.lambda_override = lam.to(DEV, torch.float32)
+    with torch.no_grad():
+        out, h_T = blk(x.to(DEV), return_ssm_state=True)
+    assert rel_l2(out, out_ref) < RTOL_F32
+    assert rel_l2(h_T, h_ref) < RTOL_F32
