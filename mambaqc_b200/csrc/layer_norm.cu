@@ -105,6 +105,12 @@ __global__ void __launch_bounds__(kMaxRowThreads) qln_fwd_kernel(
 // parameter gradients are deterministic.
 constexpr int kVptB = 4;
 
+// Offset (in floats) of the dbeta partials: after parts*D dgamma partials,
+// rounded up to a multiple of 4 floats so every float4 store is 16-byte aligned.
+__host__ __device__ inline int64_t beta_partial_offset(int64_t parts, int64_t D) {
+  return (parts * D + 3) / 4 * 4;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(1024) qln_bwd_kernel(
     const T* __restrict__ q, const float* __restrict__ gamma, const T* __restrict__ dout,
@@ -173,26 +179,35 @@ __global__ void __launch_bounds__(1024) qln_bwd_kernel(
       }
     }
   }
-  float* prow = partial + int64_t(blockIdx.x) * D * 5;
+  // partial layout: [parts][D] dgamma, then (16-byte aligned) [parts][D] float4 dbeta
+  float* pg = partial + int64_t(blockIdx.x) * D;
+  float4* pb = reinterpret_cast<float4*>(partial + beta_partial_offset(gridDim.x, D)) +
+               int64_t(blockIdx.x) * D;
 #pragma unroll
   for (int j = 0; j < kVptB; ++j) {
     const int d = threadIdx.x + j * blockDim.x;
     if (d < D) {
-      prow[d] = dg[j];
-      reinterpret_cast<float4*>(prow + D)[d] = db[j];
+      pg[d] = dg[j];
+      pb[d] = db[j];
     }
   }
 }
 
-// dgamma[d] = sum_c partial[c][d]; dbeta[d] = sum_c partial[c][D + 4d .. 4d+3]
+// dgamma[d] = sum_c gamma_part[c][d]; dbeta[d][k] = sum_c beta_part[c][d][k]
 __global__ void qln_bwd_reduce_kernel(const float* __restrict__ partial, float* __restrict__ dgamma,
                                       float* __restrict__ dbeta, int nparts, int D) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;  // 0 .. 5D-1
   if (i >= 5 * D) return;
   float s = 0.f;
-  for (int c = 0; c < nparts; ++c) s += partial[int64_t(c) * D * 5 + i];
-  if (i < D) dgamma[i] = s;
-  else dbeta[i - D] = s;
+  if (i < D) {
+    for (int c = 0; c < nparts; ++c) s += partial[int64_t(c) * D + i];
+    dgamma[i] = s;
+  } else {
+    const float* pb = partial + beta_partial_offset(nparts, D);
+    const int j = i - D;  // element of the [D][4] block
+    for (int c = 0; c < nparts; ++c) s += pb[int64_t(c) * D * 4 + j];
+    dbeta[j] = s;
+  }
 }
 
 int qln_bwd_parts(int64_t rows) {
@@ -248,7 +263,8 @@ extern "C" int mqc_qln_fwd(const void* q, const float* gamma, const float* beta,
 
 extern "C" size_t mqc_qln_bwd_workspace_size(int64_t rows, int64_t d_model) {
   if (rows <= 0 || d_model <= 0) return 0;
-  return size_t(qln_bwd_parts(rows)) * size_t(d_model) * 5 * sizeof(float);
+  const int64_t parts = qln_bwd_parts(rows);
+  return size_t(beta_partial_offset(parts, d_model) + parts * d_model * 4) * sizeof(float);
 }
 
 extern "C" int mqc_qln_bwd(const void* q, const float* gamma, const void* dout, const float* mean,

@@ -16,6 +16,11 @@ from .parallel_scan import parallel_scan_quaternion
 from .quaternion_norm import quaternion_layer_norm_fused
 from .ssm_fused import ssm_step_fused, ssm_forward_fused, ssm_scan_cayley
 
+# Importing the submodule ``quaternion_norm`` (the LayerNorm file) rebinds the
+# package attribute of that name to the module; bind the function again so that
+# ``kernels.quaternion_norm`` is the quaternion norm, as its export list says.
+from .quaternion_ops import quaternion_norm  # noqa: E402,F811
+
 __all__ = [
     "quaternion_multiply",
     "quaternion_multiply_batched",
