@@ -61,29 +61,28 @@ __host__ __device__ inline SmemLayout smem_layout(int tc, int cpb, int N, bool b
 }
 
 // Per-(d, n) constants of the fused Cayley map, from Lambda = (l_r, l_i, l_j, l_k):
-// half = l_r / 2, (li, lj, lk) = Im Lambda, m = |Im Lambda|^2 / 4.
+// lr = l_r, (li, lj, lk) = Im Lambda, m = |Lambda|^2 / 4.
 struct LamConst {
-  float half, li, lj, lk, m;
+  float lr, li, lj, lk, m;
 };
 
 __device__ __forceinline__ LamConst make_lam_const(float4 lam) {
-  return LamConst{0.5f * lam.x, lam.y, lam.z, lam.w,
-                  0.25f * fmaf(lam.y, lam.y, fmaf(lam.z, lam.z, lam.w * lam.w))};
+  return LamConst{lam.x, lam.y, lam.z, lam.w,
+                  0.25f * fmaf(lam.x, lam.x, fmaf(lam.y, lam.y, fmaf(lam.z, lam.z, lam.w * lam.w)))};
 }
 
-// q = Cayley(delta * Lambda) in closed form, without forming z:
-// a = delta*l_r/2, |v|^2 = delta^2 * m, den = max((1-a)^2 + |v|^2, eps),
-// q = ((1-a)(1+a) - |v|^2, delta * Im Lambda) / den.
+// q = Cayley(delta * Lambda) in closed form, without forming z. With
+// w = delta*Lambda/2 = a + v and P = |w|^2 = delta^2 m:
+//   |1 - w|^2 = (1-a)^2 + |v|^2 = 1 + P - delta*l_r      (clamped below by eps)
+//   conj(1 - w) (x) (1 + w) = (1 - P) + delta * Im Lambda
+// so q = ((1 - P), delta * Im Lambda) / max(1 + P - delta l_r, eps).
 __device__ __forceinline__ float4 cayley_from_const(float dl, float dl2, const LamConst& c,
                                                     float eps) {
-  const float a = dl * c.half;
-  const float om = 1.f - a;
-  const float op = 1.f + a;
-  const float vv = dl2 * c.m;
-  const float den = fmaxf(fmaf(om, om, vv), eps);
-  const float inv = __frcp_rn(den);
+  const float P = dl2 * c.m;
+  const float den = fmaxf(fmaf(-dl, c.lr, 1.f + P), eps);
+  const float inv = rcp_nr(den);
   const float s = dl * inv;
-  return make_float4(fmaf(om, op, -vv) * inv, s * c.li, s * c.lj, s * c.lk);
+  return make_float4((1.f - P) * inv, s * c.li, s * c.lj, s * c.lk);
 }
 
 __device__ __forceinline__ float f4_get(const float4& v, int k) {
@@ -187,6 +186,10 @@ inline LaunchShape choose_shape(int B, int T, int D, int N, int NG, int esize, b
   ls.smem = smem;
   return ls;
 }
+
+// Warp-specialised kernel for channel-shared B/C without explicit q
+// (ssm_scan_fwd_shared.cu).
+int dispatch_shared(const FwdParams& p, int dtype, bool s_real, cudaStream_t st);
 
 inline int validate_and_fill(const mqc_ssm_scan_args* a, FwdParams* p, const char* name) {
   MQC_REQUIRE(a != nullptr, MQC_ERR_INVALID_VALUE, "%s: null args", name);

@@ -28,6 +28,9 @@
 // Every device-side wait is bounded; on timeout the kernel ORs
 // MQC_DEVICE_STATUS_TIMEOUT into the caller's status word, drains its own bulk
 // copies in flight (bounded) and returns.
+#include <cstdlib>
+#include <cstring>
+
 #include "ssm_scan_common.cuh"
 
 namespace mqc {
@@ -307,11 +310,26 @@ int dispatch_mode(const FwdParams& p, int flags, cudaStream_t st) {
 using namespace mqc;
 using namespace mqc::scan;
 
+namespace {
+// MQC_SCAN_IMPL=generic routes channel-shared B/C through the generic kernel
+// (for A/B comparisons); the default is the warp-specialised kernel.
+bool use_generic_kernel() {
+  static const bool generic = [] {
+    const char* v = getenv("MQC_SCAN_IMPL");
+    return v != nullptr && strcmp(v, "generic") == 0;
+  }();
+  return generic;
+}
+}  // namespace
+
 extern "C" int mqc_ssm_scan_fwd(const mqc_ssm_scan_args* a, void* stream) {
   clear_error();
   FwdParams p{};
   int rc = validate_and_fill(a, &p, "mqc_ssm_scan_fwd");
   if (rc != MQC_OK || p.T == 0 || p.B == 0 || p.D == 0) return rc;
+  const bool shared_fused = (a->flags & MQC_SSM_BC_SHARED) && !(a->flags & MQC_SSM_Q_GIVEN);
+  if (shared_fused && !use_generic_kernel())
+    return dispatch_shared(p, a->dtype, (a->flags & MQC_SSM_S_REAL) != 0, as_stream(stream));
   if (a->dtype == MQC_DTYPE_F32) return dispatch_mode<float>(p, a->flags, as_stream(stream));
   return dispatch_mode<__nv_bfloat16>(p, a->flags, as_stream(stream));
 }

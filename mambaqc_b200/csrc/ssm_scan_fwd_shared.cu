@@ -1,0 +1,352 @@
+// Fused Cayley + quaternion selective scan, forward, for B/C shared by all
+// channels ([B,T,N,4]; the layout of the hot-path configuration) -- the
+// warp-specialised kernel.
+//
+// Same math as ssm_scan_fwd.cu (QuaternionMamba2Block._ssm_forward,
+// mambaqc/models/quaternion_mamba2_block.py:214-228, without materialising z or
+// q), organised so that no block-wide barrier sits in the time loop:
+//
+//  * warp 0 is the producer: one lane streams the B_t/C_t tiles of each chunk of
+//    tc timesteps into a kRing-deep shared-memory ring with bulk copies (TMA
+//    engine), signalling `full[stage]` by transaction bytes and waiting on
+//    `empty[stage]` before it reuses a stage;
+//  * every other warp is a consumer that owns 32/NG channels x N states
+//    (G states per lane, n = ng + NG*i); it stages its own channels' delta and
+//    x (or S) one chunk ahead through registers into a warp-private buffer,
+//    waits on `full`, runs the chunk, and releases the stage with one arrive on
+//    `empty` -- warps drift freely and only meet in the ring;
+//  * B/C rows in shared memory are padded to NP = NG*G states with zeros, so
+//    the inner loop has no lane guards;
+//  * the per-step readout sum over n is in registers over G states (two
+//    accumulators) and a shuffle reduce-scatter over the NG lanes of a channel.
+//
+// All waits are bounded (poll limit); on timeout the kernel reports
+// MQC_DEVICE_STATUS_TIMEOUT, raises a shared abort flag so the other warps stop
+// at their next chunk, and the producer drains its copies in flight before it
+// exits.
+#include "ssm_scan_common.cuh"
+
+namespace mqc {
+namespace scan {
+
+constexpr int kRing = 3;
+constexpr int kV2MaxThreads = 512;
+constexpr int kV2MaxDx = 8;   // staged delta/x elements per lane per chunk (real signal)
+constexpr int kV2MaxDxQ = 2;  // the same for a quaternion signal S (4x the registers)
+constexpr size_t kV2SmemBudget = 220 * 1024;
+
+struct V2Layout {
+  size_t off_b, off_c, off_dx, off_sx, total;
+};
+
+// [full x kRing][empty x kRing][abort flag] | sB [kRing][tc][np][4] | sC |
+// per consumer warp: delta [2][tc][cpw] f32 | s [2][tc][cpw][sw] f32
+template <typename T>
+__host__ __device__ inline V2Layout v2_layout(int tc, int np, int warps, int cpw, int sw) {
+  V2Layout L;
+  size_t off = 128;
+  const size_t ring = size_t(kRing) * tc * np * 4 * sizeof(T);
+  L.off_b = off;
+  off = align_up(off + ring, 128);
+  L.off_c = off;
+  off = align_up(off + ring, 128);
+  L.off_dx = off;
+  off = align_up(off + size_t(warps) * 2 * tc * cpw * sizeof(float), 16);
+  L.off_sx = off;
+  off = align_up(off + size_t(warps) * 2 * tc * cpw * sw * sizeof(float), 16);
+  L.total = off;
+  return L;
+}
+
+template <typename T, int G, int NG, bool S_REAL>
+__global__ void __launch_bounds__(kV2MaxThreads, 1)
+    scan_fwd_shared_kernel(const FwdParams p, const int np) {
+  constexpr int CPW = 32 / NG;  // channels per consumer warp
+  constexpr int SW = S_REAL ? 1 : 4;
+  constexpr unsigned kFull = 0xffffffffu;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps_c = (blockDim.x >> 5) - 1;
+  const int T_ = p.T, D = p.D, N = p.N, tc = p.tc;
+  const int b = blockIdx.y;
+  const int c0 = int((int64_t(D) * blockIdx.x) / p.nb);
+  const int c1 = int((int64_t(D) * (blockIdx.x + 1)) / p.nb);
+  const int nch = c1 - c0;
+  const int busy_warps = (nch + CPW - 1) / CPW;
+  const int nchunks = (T_ + tc - 1) / tc;
+
+  const V2Layout L = v2_layout<T>(tc, np, nwarps_c, CPW, SW);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);
+  uint64_t* empty = full + kRing;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kRing);
+  T* sB = reinterpret_cast<T*>(smem_raw + L.off_b);
+  T* sC = reinterpret_cast<T*>(smem_raw + L.off_c);
+
+  // zero the padding states n in [N, np) of every ring row once; copies never touch them
+  if (np != N) {
+    const int pad = np - N;
+    for (int i = threadIdx.x; i < kRing * tc * pad; i += blockDim.x) {
+      const int row = i / pad, n = N + i % pad;
+      QIO<T>::st(sB + (int64_t(row) * np + n) * 4, f4_zero());
+      QIO<T>::st(sC + (int64_t(row) * np + n) * 4, f4_zero());
+    }
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kRing; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], uint32_t(busy_warps));
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // ------------------------------------------------------------- producer
+  if (warp == 0) {
+    if (lane == 0) {
+      const T* gB = static_cast<const T*>(p.Bm);
+      const T* gC = static_cast<const T*>(p.Cm);
+      const uint32_t row_bytes = uint32_t(N) * 4 * sizeof(T);
+      int issued = 0;
+      bool ok = true;
+      for (int k = 0; k < nchunks; ++k) {
+        const int st = k % kRing;
+        if (k >= kRing) {
+          ok = mbar_wait_bounded(&empty[st], uint32_t(((k / kRing) - 1) & 1), p.wait_limit);
+          if (!ok) break;
+        }
+        if (*abort_flag) break;
+        const int t0 = k * tc;
+        const int len = min(tc, T_ - t0);
+        mbar_arrive_expect_tx(&full[st], 2u * uint32_t(len) * row_bytes);
+        const int64_t g0 = (int64_t(b) * T_ + t0) * N * 4;
+        T* dB = sB + int64_t(st) * tc * np * 4;
+        T* dC = sC + int64_t(st) * tc * np * 4;
+        if (np == N) {
+          bulk_g2s(dB, gB + g0, uint32_t(len) * row_bytes, &full[st]);
+          bulk_g2s(dC, gC + g0, uint32_t(len) * row_bytes, &full[st]);
+        } else {
+          for (int tt = 0; tt < len; ++tt) {
+            bulk_g2s(dB + int64_t(tt) * np * 4, gB + g0 + int64_t(tt) * N * 4, row_bytes, &full[st]);
+            bulk_g2s(dC + int64_t(tt) * np * 4, gC + g0 + int64_t(tt) * N * 4, row_bytes, &full[st]);
+          }
+        }
+        issued = k + 1;
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        report_status(p.status, MQC_DEVICE_STATUS_TIMEOUT);
+      }
+      // the CTA must outlive its copies: wait (bounded) for the last ones issued
+      for (int k = issued > kRing ? issued - kRing : 0; k < issued; ++k)
+        mbar_wait_bounded(&full[k % kRing], uint32_t((k / kRing) & 1), kDrainPollLimit);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------- consumers
+  const int cw = warp - 1;
+  if (cw >= busy_warps) return;
+  const int lc_ch = lane / NG;  // channel slot within the warp
+  const int ng = lane % NG;
+  const int cl = cw * CPW + lc_ch;
+  const bool active = cl < nch;
+  const int c = active ? c0 + cl : c0;
+
+  float4 h[G];
+  LamConst lc[G];
+#pragma unroll
+  for (int i = 0; i < G; ++i) {
+    const int n = ng + NG * i;
+    h[i] = f4_zero();
+    lc[i] = LamConst{0.f, 0.f, 0.f, 0.f, 0.f};
+    if (active && n < N) {
+      if (p.h0 != nullptr) h[i] = QIO<float>::ld(p.h0 + ((int64_t(b) * D + c) * N + n) * 4);
+      lc[i] = make_lam_const(QIO<float>::ld(p.lam + (int64_t(c) * N + n) * 4));
+    }
+  }
+  const bool d_const = p.dst == 0;
+  const float dsk0 = active ? __ldg(p.dskip + int64_t(b) * p.dsb + int64_t(c) * p.dsd) : 0.f;
+
+  // warp-private staging of delta and s: [2][tc][CPW] (+ [SW] for s)
+  float* wdel = reinterpret_cast<float*>(smem_raw + L.off_dx) + int64_t(cw) * 2 * tc * CPW;
+  float* wsig = reinterpret_cast<float*>(smem_raw + L.off_sx) + int64_t(cw) * 2 * tc * CPW * SW;
+  const T* gdelta = static_cast<const T*>(p.delta);
+  const T* gs = static_cast<const T*>(p.s);
+  const int per_chunk = tc * CPW;
+  constexpr int MD = S_REAL ? kV2MaxDx : kV2MaxDxQ;
+  float rd[MD];
+  float4 rs[MD];
+  auto load_dx = [&](int k) {
+    const int t0 = k * tc;
+#pragma unroll
+    for (int j = 0; j < MD; ++j) {
+      const int e = lane + 32 * j;
+      rd[j] = 0.f;
+      rs[j] = f4_zero();
+      if (e < per_chunk) {
+        const int tt = e / CPW, cc = cw * CPW + e % CPW;
+        if (t0 + tt < T_ && cc < nch) {
+          const int64_t idx = (int64_t(b) * T_ + t0 + tt) * D + c0 + cc;
+          rd[j] = to_f(gdelta[idx]);
+          if (S_REAL) rs[j].x = to_f(gs[idx]);
+          else rs[j] = QIO<T>::ld(gs + idx * 4);
+        }
+      }
+    }
+  };
+  auto store_dx = [&](int buf) {
+#pragma unroll
+    for (int j = 0; j < MD; ++j) {
+      const int e = lane + 32 * j;
+      if (e < per_chunk) {
+        wdel[buf * per_chunk + e] = rd[j];
+        if (S_REAL) wsig[buf * per_chunk + e] = rs[j].x;
+        else reinterpret_cast<float4*>(wsig)[buf * per_chunk + e] = rs[j];
+      }
+    }
+  };
+
+  load_dx(0);
+  store_dx(0);
+  __syncwarp();
+
+  const float eps = p.eps;
+  T* yb = static_cast<T*>(p.y) + (int64_t(b) * T_ * D + c) * 4;
+  for (int k = 0; k < nchunks; ++k) {
+    const int st = k % kRing;
+    const int buf = k & 1;
+    bool ok = *abort_flag == 0;
+    if (ok) ok = mbar_wait_bounded(&full[st], uint32_t((k / kRing) & 1), p.wait_limit);
+    if (!__all_sync(kFull, ok)) {
+      if (lane == 0) {
+        *abort_flag = 1;
+        report_status(p.status, MQC_DEVICE_STATUS_TIMEOUT);
+      }
+      return;
+    }
+    if (k + 1 < nchunks) load_dx(k + 1);
+
+    const int t0 = k * tc;
+    const int len = min(tc, T_ - t0);
+    const float* cdel = wdel + buf * per_chunk;
+    const float* csig = wsig + buf * per_chunk * SW;
+    const T* rowB = sB + int64_t(st) * tc * np * 4 + ng * 4;
+    const T* rowC = sC + int64_t(st) * tc * np * 4 + ng * 4;
+    for (int tt = 0; tt < len; ++tt) {
+      const int t = t0 + tt;
+      const float dl = cdel[tt * CPW + lc_ch];
+      const float dl2 = dl * dl;
+      float4 sv;
+      if (S_REAL) sv = make_float4(csig[tt * CPW + lc_ch], 0.f, 0.f, 0.f);
+      else sv = reinterpret_cast<const float4*>(csig)[tt * CPW + lc_ch];
+      float4 ya = f4_zero(), yb2 = f4_zero();
+#pragma unroll
+      for (int i = 0; i < G; ++i) {
+        const float4 Bv = QIO<T>::lds(rowB + (tt * np + NG * i) * 4);
+        const float4 Cv = QIO<T>::lds(rowC + (tt * np + NG * i) * 4);
+        const float4 qv = cayley_from_const(dl, dl2, lc[i], eps);
+        float4 inj;
+        if (S_REAL) inj = make_float4(sv.x * Bv.x, sv.x * Bv.y, sv.x * Bv.z, sv.x * Bv.w);
+        else inj = qmul(Bv, sv);
+        h[i] = qmul_acc(qv, h[i], inj);
+        if (i & 1) yb2 = qmul_acc(Cv, h[i], yb2);
+        else ya = qmul_acc(Cv, h[i], ya);
+      }
+      ya.x += yb2.x;
+      ya.y += yb2.y;
+      ya.z += yb2.z;
+      ya.w += yb2.w;
+      float dsk = dsk0;
+      if (!d_const)
+        dsk = (active && ng < 4)
+                  ? __ldg(p.dskip + int64_t(b) * p.dsb + int64_t(t) * p.dst + int64_t(c) * p.dsd)
+                  : 0.f;
+      reduce_store_y<T, NG>(ya, sv, dsk, ng, active, yb + int64_t(t) * D * 4);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+    if (k + 1 < nchunks) {
+      store_dx(buf ^ 1);
+      __syncwarp();
+    }
+  }
+
+  if (p.hT != nullptr && active) {
+#pragma unroll
+    for (int i = 0; i < G; ++i) {
+      const int n = ng + NG * i;
+      if (n < N) QIO<float>::st(p.hT + ((int64_t(b) * D + c) * N + n) * 4, h[i]);
+    }
+  }
+}
+
+template <typename T, int G, int NG, bool S_REAL>
+int launch_shared(FwdParams p, cudaStream_t st) {
+  constexpr int CPW = 32 / NG;
+  const int np = NG * G;
+  const int sw = S_REAL ? 1 : 4;
+  const int sms = num_sms();
+  int nb = (sms + p.B - 1) / p.B;
+  if (nb > p.D) nb = p.D;
+  if (nb < 1) nb = 1;
+  int cpb = (p.D + nb - 1) / nb;
+  const int cap = (kV2MaxThreads / 32 - 1) * CPW;
+  if (cpb > cap) {
+    nb = (p.D + cap - 1) / cap;
+    cpb = (p.D + nb - 1) / nb;
+  }
+  const int warps = (cpb + CPW - 1) / CPW;
+  int tc = kMaxTc;
+  const int max_dx = S_REAL ? kV2MaxDx : kV2MaxDxQ;
+  while (tc > 1 && tc * CPW > 32 * max_dx) tc >>= 1;
+  if (tc > p.T) tc = p.T;
+  size_t smem = v2_layout<T>(tc, np, warps, CPW, sw).total;
+  while (smem > kV2SmemBudget && tc > 1) {
+    tc >>= 1;
+    smem = v2_layout<T>(tc, np, warps, CPW, sw).total;
+  }
+  if (smem > kV2SmemBudget)
+    return fail(MQC_ERR_UNSUPPORTED, "mqc_ssm_scan_fwd: shared staging does not fit (N=%d)", p.N);
+  p.nb = nb;
+  p.cpb = cpb;
+  p.tc = tc;
+  auto kern = scan_fwd_shared_kernel<T, G, NG, S_REAL>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess)
+    return fail(MQC_ERR_CUDA, "mqc_ssm_scan_fwd: smem attribute (%zu B): %s", smem,
+                cudaGetErrorString(e));
+  dim3 grid{unsigned(nb), unsigned(p.B), 1u};
+  kern<<<grid, 32 * (warps + 1), smem, st>>>(p, np);
+  return check_launch("mqc_ssm_scan_fwd(shared)");
+}
+
+template <typename T, bool S_REAL>
+int dispatch_shared_t(const FwdParams& p, cudaStream_t st) {
+  // G = 8 states per lane; NG = lanes per channel (power of two covering N/8)
+  const int need = (p.N + 7) / 8;
+  int ng = 1;
+  while (ng < need) ng <<= 1;
+  switch (ng) {
+    case 1: return launch_shared<T, 8, 1, S_REAL>(p, st);
+    case 2: return launch_shared<T, 8, 2, S_REAL>(p, st);
+    case 4: return launch_shared<T, 8, 4, S_REAL>(p, st);
+    case 8: return launch_shared<T, 8, 8, S_REAL>(p, st);
+    case 16: return launch_shared<T, 8, 16, S_REAL>(p, st);
+    case 32: return launch_shared<T, 8, 32, S_REAL>(p, st);
+    default:
+      return fail(MQC_ERR_UNSUPPORTED, "mqc_ssm_scan_fwd: d_state=%d (supported 1..256)", p.N);
+  }
+}
+
+int dispatch_shared(const FwdParams& p, int dtype, bool s_real, cudaStream_t st) {
+  if (dtype == MQC_DTYPE_F32)
+    return s_real ? dispatch_shared_t<float, true>(p, st) : dispatch_shared_t<float, false>(p, st);
+  return s_real ? dispatch_shared_t<__nv_bfloat16, true>(p, st)
+                : dispatch_shared_t<__nv_bfloat16, false>(p, st);
+}
+
+}  // namespace scan
+}  // namespace mqc

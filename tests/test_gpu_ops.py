@@ -176,6 +176,21 @@ def test_cayley_backward_matches_oracle():
                                rtol=1e-4, atol=1e-2)
 
 
+def test_cayley_denominator_sweep():
+    """Real z from -2e3 to just below the pole z = 2: |1 - z/2|^2 spans ~1e-6 .. 1e6, so the
+    reciprocal is exercised over 12 decades; every output within a few ulp of fp64."""
+    zr = torch.cat([-torch.logspace(-6, 3.3, 4000, dtype=torch.float64),
+                    2.0 - torch.logspace(-2.9, 0, 2000, dtype=torch.float64)])
+    z = torch.zeros(1, 1, 1, zr.numel(), 4, dtype=torch.float64)
+    z[..., 0] = zr
+    z[..., 1] = 1e-3 * zr
+    z32 = g32(z)
+    q = cayley_discretization_fused(z32).cpu().double()
+    truth = ref.cayley(z32.cpu().double())
+    rel = ((q - truth).norm(dim=-1) / truth.norm(dim=-1)).max().item()
+    assert rel < 1e-6, rel
+
+
 def test_cayley_large_bf16_and_stability():
     g = gen(8)
     z = torch.randn(2, 16, 96, 64, 4, generator=g)
