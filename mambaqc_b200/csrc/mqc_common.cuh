@@ -240,6 +240,26 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 // Poll limit used to drain copies still in flight on an error path.
 constexpr long long kDrainPollLimit = 1ll << 22;
 
+// 4-byte asynchronous global -> shared copy (LDGSTS) that bypasses registers;
+// with `valid` false nothing is read and the 4 destination bytes are zero-filled.
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_addr(dst)), "l"(src),
+               "r"(valid ? 4 : 0)
+               : "memory");
+}
+// 16-byte variant (both addresses 16-byte aligned), zero-filled when !valid.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
 __device__ __forceinline__ void report_status(int* status, int code) {
   if (status != nullptr) atomicOr(status, code);
 }

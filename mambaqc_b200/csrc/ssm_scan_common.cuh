@@ -82,7 +82,7 @@ __device__ __forceinline__ float4 cayley_from_const(float dl, float dl2, const L
   const float den = fmaxf(fmaf(-dl, c.lr, 1.f + P), eps);
   const float inv = rcp_nr(den);
   const float s = dl * inv;
-  return make_float4((1.f - P) * inv, s * c.li, s * c.lj, s * c.lk);
+  return make_float4(fmaf(-P, inv, inv), s * c.li, s * c.lj, s * c.lk);
 }
 
 __device__ __forceinline__ float f4_get(const float4& v, int k) {

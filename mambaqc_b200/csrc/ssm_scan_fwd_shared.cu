@@ -24,13 +24,18 @@
 // MQC_DEVICE_STATUS_TIMEOUT, raises a shared abort flag so the other warps stop
 // at their next chunk, and the producer drains its copies in flight before it
 // exits.
+#include <cstdlib>
+#include <type_traits>
+
 #include "ssm_scan_common.cuh"
 
 namespace mqc {
 namespace scan {
 
 constexpr int kRing = 3;
-constexpr int kV2MaxThreads = 512;
+// CTA size cap: 8 states per lane need ~128 registers per thread (512 threads);
+// 4 states per lane fit in ~80 (768 threads).
+__host__ __device__ constexpr int v2_max_threads(int g) { return g == 4 ? 768 : 512; }
 constexpr int kV2MaxDx = 8;   // staged delta/x elements per lane per chunk (real signal)
 constexpr int kV2MaxDxQ = 2;  // the same for a quaternion signal S (4x the registers)
 constexpr size_t kV2SmemBudget = 220 * 1024;
@@ -59,7 +64,7 @@ __host__ __device__ inline V2Layout v2_layout(int tc, int np, int warps, int cpw
 }
 
 template <typename T, int G, int NG, bool S_REAL>
-__global__ void __launch_bounds__(kV2MaxThreads, 1)
+__global__ void __launch_bounds__(v2_max_threads(G), 1)
     scan_fwd_shared_kernel(const FwdParams p, const int np) {
   constexpr int CPW = 32 / NG;  // channels per consumer warp
   constexpr int SW = S_REAL ? 1 : 4;
@@ -175,9 +180,24 @@ __global__ void __launch_bounds__(kV2MaxThreads, 1)
   const T* gdelta = static_cast<const T*>(p.delta);
   const T* gs = static_cast<const T*>(p.s);
   const int per_chunk = tc * CPW;
-  constexpr int MD = S_REAL ? kV2MaxDx : kV2MaxDxQ;
+  // fp32 inputs: delta / s go global -> shared with cp.async (no registers held
+  // across the chunk); bf16 inputs (2-byte elements) go through registers.
+  constexpr bool kAsync = std::is_same<T, float>::value;
+  constexpr int MD = kAsync ? 1 : (S_REAL ? kV2MaxDx : kV2MaxDxQ);
   float rd[MD];
   float4 rs[MD];
+  auto issue_dx_async = [&](int k, int buf) {
+    const int t0 = k * tc;
+    for (int e = lane; e < per_chunk; e += 32) {
+      const int tt = e / CPW, cc = cw * CPW + e % CPW;
+      const bool v = (t0 + tt < T_) && (cc < nch);
+      const int64_t idx = v ? (int64_t(b) * T_ + t0 + tt) * D + c0 + cc : 0;
+      cp_async4(wdel + buf * per_chunk + e, gdelta + idx, v);
+      if (S_REAL) cp_async4(wsig + buf * per_chunk + e, gs + idx, v);
+      else cp_async16(wsig + (buf * per_chunk + e) * 4, gs + idx * 4, v);
+    }
+    cp_async_commit();
+  };
   auto load_dx = [&](int k) {
     const int t0 = k * tc;
 #pragma unroll
@@ -208,8 +228,13 @@ __global__ void __launch_bounds__(kV2MaxThreads, 1)
     }
   };
 
-  load_dx(0);
-  store_dx(0);
+  if constexpr (kAsync) {
+    issue_dx_async(0, 0);
+    cp_async_wait_all();
+  } else {
+    load_dx(0);
+    store_dx(0);
+  }
   __syncwarp();
 
   const float eps = p.eps;
@@ -226,7 +251,10 @@ __global__ void __launch_bounds__(kV2MaxThreads, 1)
       }
       return;
     }
-    if (k + 1 < nchunks) load_dx(k + 1);
+    if (k + 1 < nchunks) {
+      if constexpr (kAsync) issue_dx_async(k + 1, buf ^ 1);
+      else load_dx(k + 1);
+    }
 
     const int t0 = k * tc;
     const int len = min(tc, T_ - t0);
@@ -268,7 +296,8 @@ __global__ void __launch_bounds__(kV2MaxThreads, 1)
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);
     if (k + 1 < nchunks) {
-      store_dx(buf ^ 1);
+      if constexpr (kAsync) cp_async_wait_all();
+      else store_dx(buf ^ 1);
       __syncwarp();
     }
   }
@@ -292,7 +321,7 @@ int launch_shared(FwdParams p, cudaStream_t st) {
   if (nb > p.D) nb = p.D;
   if (nb < 1) nb = 1;
   int cpb = (p.D + nb - 1) / nb;
-  const int cap = (kV2MaxThreads / 32 - 1) * CPW;
+  const int cap = (v2_max_threads(G) / 32 - 1) * CPW;
   if (cpb > cap) {
     nb = (p.D + cap - 1) / cap;
     cpb = (p.D + nb - 1) / nb;
@@ -323,22 +352,39 @@ int launch_shared(FwdParams p, cudaStream_t st) {
   return check_launch("mqc_ssm_scan_fwd(shared)");
 }
 
-template <typename T, bool S_REAL>
-int dispatch_shared_t(const FwdParams& p, cudaStream_t st) {
-  // G = 8 states per lane; NG = lanes per channel (power of two covering N/8)
-  const int need = (p.N + 7) / 8;
+template <typename T, int G, bool S_REAL>
+int dispatch_shared_g(const FwdParams& p, cudaStream_t st) {
+  // NG = lanes per channel: the power of two covering ceil(N / G), at most 32
+  const int need = (p.N + G - 1) / G;
   int ng = 1;
   while (ng < need) ng <<= 1;
   switch (ng) {
-    case 1: return launch_shared<T, 8, 1, S_REAL>(p, st);
-    case 2: return launch_shared<T, 8, 2, S_REAL>(p, st);
-    case 4: return launch_shared<T, 8, 4, S_REAL>(p, st);
-    case 8: return launch_shared<T, 8, 8, S_REAL>(p, st);
-    case 16: return launch_shared<T, 8, 16, S_REAL>(p, st);
-    case 32: return launch_shared<T, 8, 32, S_REAL>(p, st);
+    case 1: return launch_shared<T, G, 1, S_REAL>(p, st);
+    case 2: return launch_shared<T, G, 2, S_REAL>(p, st);
+    case 4: return launch_shared<T, G, 4, S_REAL>(p, st);
+    case 8: return launch_shared<T, G, 8, S_REAL>(p, st);
+    case 16: return launch_shared<T, G, 16, S_REAL>(p, st);
+    case 32: return launch_shared<T, G, 32, S_REAL>(p, st);
     default:
-      return fail(MQC_ERR_UNSUPPORTED, "mqc_ssm_scan_fwd: d_state=%d (supported 1..256)", p.N);
+      return fail(MQC_ERR_UNSUPPORTED, "mqc_ssm_scan_fwd: d_state=%d (supported 1..%d)", p.N,
+                  32 * G);
   }
+}
+
+// States per lane: 8 by default; MQC_SCAN_G=4 selects 4 (twice the warps, half
+// the registers per thread) for tuning comparisons.
+int states_per_lane() {
+  static const int g = [] {
+    const char* v = getenv("MQC_SCAN_G");
+    return (v != nullptr && v[0] == '4' && v[1] == '\0') ? 4 : 8;
+  }();
+  return g;
+}
+
+template <typename T, bool S_REAL>
+int dispatch_shared_t(const FwdParams& p, cudaStream_t st) {
+  if (states_per_lane() == 4 && p.N <= 128) return dispatch_shared_g<T, 4, S_REAL>(p, st);
+  return dispatch_shared_g<T, 8, S_REAL>(p, st);
 }
 
 int dispatch_shared(const FwdParams& p, int dtype, bool s_real, cudaStream_t st) {
