@@ -96,6 +96,22 @@ MQC_API int mqc_cayley_bwd(const void* z, const void* dq, void* dz, int64_t n, f
 MQC_API int mqc_prefix_prod(const void* q, void* out, int64_t batch, int64_t seq_len, int64_t lanes,
                     int dtype, void* stream);
 
+/* Same result as mqc_prefix_prod, allocating nothing. No counterpart in the
+ * reference. For callers that cannot allocate device memory while they run --
+ * e.g. a server that gives all device memory to its own allocator at start-up,
+ * or a process on a fixed device-memory budget where an allocation failing
+ * mid-run is not acceptable. When time is split into chunks, the chunk products
+ * live in a fixed 4 MiB static device array that every GPU loading this library
+ * holds until exit; sizes needing more (batch * chunks * lanes * 16 bytes) are
+ * rejected with MQC_ERR_UNSUPPORTED and a message giving the bytes needed. The
+ * first call on a device looks up the array's device address (set-up, once per
+ * device, with that device current); make that first call before any stream
+ * capture. All calls share the one array: calls that overlap on the GPU (e.g.
+ * on two streams of one device) race. Nothing in the array needs clearing
+ * between calls: each call writes every entry it reads. */
+MQC_API int mqc_prefix_prod_noalloc(const void* q, void* out, int64_t batch, int64_t seq_len,
+                                    int64_t lanes, int dtype, void* stream);
+
 /* ---- selective scan: mambaqc/kernels/ssm_fused.py + block._ssm_forward ------ */
 
 /* Flags of mqc_ssm_scan_args.flags */

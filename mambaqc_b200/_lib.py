@@ -59,6 +59,7 @@ _SIGNATURES = {
     "mqc_cayley": [_c_void_p, _c_void_p, _i64, _f32, _i32, _c_void_p],
     "mqc_cayley_bwd": [_c_void_p, _c_void_p, _c_void_p, _i64, _f32, _i32, _c_void_p],
     "mqc_prefix_prod": [_c_void_p, _c_void_p, _i64, _i64, _i64, _i32, _c_void_p],
+    "mqc_prefix_prod_noalloc": [_c_void_p, _c_void_p, _i64, _i64, _i64, _i32, _c_void_p],
     "mqc_ssm_scan_fwd": [ctypes.POINTER(SsmScanArgs), _c_void_p],
     "mqc_ssm_step": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                      _c_void_p, _c_void_p, _i64, _i64, _i64, _i32, _c_void_p],

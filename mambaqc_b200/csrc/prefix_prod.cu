@@ -11,6 +11,8 @@
 //   pass 1: P[b,c,l] = q[end_c] (x) ... (x) q[start_c]        (reads q)
 //   pass 2: carry = P[c-1] (x) ... (x) P[0]; run chunk c from carry (reads q, writes out)
 // Products are combined later (x) earlier, preserving the non-commutative order.
+#include <mutex>
+
 #include "mqc_common.cuh"
 #include "mqc_host.h"
 
@@ -148,4 +150,112 @@ extern "C" int mqc_prefix_prod(const void* q, void* out, int64_t batch, int64_t 
               "mqc_prefix_prod: pointers must be %d-byte aligned", int(al));
   if (dtype == MQC_DTYPE_F32) return launch<float>(q, out, batch, seq_len, lanes, as_stream(stream));
   return launch<__nv_bfloat16>(q, out, batch, seq_len, lanes, as_stream(stream));
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant (mqc_prefix_prod_noalloc)
+//
+// Some callers cannot allocate device memory while they run: a server that
+// hands all device memory to its own allocator at start-up, or a process with a
+// fixed device-memory budget in which an allocation failing mid-run is not
+// acceptable. For them the chunked path takes its chunk products from this
+// fixed file-scope array instead of cudaMallocAsync. Every GPU that loads the
+// library holds the array (4 MiB) until the process exits.
+// ---------------------------------------------------------------------------
+
+namespace mqc {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // 4 MiB = 262144 chunk products
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+constexpr int kMaxDevicesNoAlloc = 64;
+std::mutex g_noalloc_mutex;
+float* g_noalloc_ptr[kMaxDevicesNoAlloc] = {};
+
+// Device address of g_noalloc_scratch on the current device. In host code the
+// array's name is only a host-side stand-in, so the address is looked up once per
+// device (with that device current) and cached.
+int noalloc_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess)
+    return fail(MQC_ERR_CUDA, "mqc_prefix_prod_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevicesNoAlloc)
+    return fail(MQC_ERR_UNSUPPORTED, "mqc_prefix_prod_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(MQC_ERR_CUDA, "mqc_prefix_prod_noalloc: cudaGetSymbolAddress: %s",
+                  cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return MQC_OK;
+}
+
+template <typename T>
+int launch_noalloc(const void* qv, void* outv, int64_t batch, int64_t seq_len, int64_t lanes,
+                   cudaStream_t st) {
+  const T* q = static_cast<const T*>(qv);
+  T* out = static_cast<T*>(outv);
+  const int64_t lane_blocks = (lanes + kThreads - 1) / kThreads;
+  MQC_REQUIRE(lane_blocks <= 0x7fffffff && batch <= 65535, MQC_ERR_UNSUPPORTED,
+              "mqc_prefix_prod_noalloc: grid too large (batch=%lld lanes=%lld)", (long long)batch,
+              (long long)lanes);
+  // same time-chunk choice as mqc_prefix_prod
+  const int64_t want_threads = int64_t(num_sms()) * 1024;
+  const int64_t have = batch * lanes;
+  int64_t nchunks = 1;
+  if (have < want_threads && seq_len >= 64) {
+    nchunks = (want_threads + have - 1) / have;
+    const int64_t max_chunks = seq_len / 32;
+    if (nchunks > max_chunks) nchunks = max_chunks;
+    if (nchunks > 1024) nchunks = 1024;
+  }
+  if (nchunks <= 1) {
+    dim3 grid{unsigned(lane_blocks), unsigned(batch), 1u};
+    prefix_seq_kernel<T><<<grid, kThreads, 0, st>>>(q, out, seq_len, lanes);
+    return check_launch("mqc_prefix_prod_noalloc");
+  }
+  const int64_t chunk = (seq_len + nchunks - 1) / nchunks;
+  nchunks = (seq_len + chunk - 1) / chunk;
+  const size_t need = size_t(batch) * size_t(nchunks) * size_t(lanes) * 16;
+  MQC_REQUIRE(need <= kNoAllocScratchBytes, MQC_ERR_UNSUPPORTED,
+              "mqc_prefix_prod_noalloc: this size needs %zu bytes of chunk scratch "
+              "(batch*chunks*lanes*16 with %lld chunks); the static maximum is %zu bytes",
+              need, (long long)nchunks, kNoAllocScratchBytes);
+  float* P = nullptr;
+  int rc = noalloc_scratch(&P);
+  if (rc != MQC_OK) return rc;
+  // Pass 1 writes every chunk product that pass 2 reads, so nothing left in the
+  // array by an earlier call is ever read and nothing needs clearing.
+  dim3 grid{unsigned(lane_blocks), unsigned(nchunks), unsigned(batch)};
+  prefix_chunk_total_kernel<T><<<grid, kThreads, 0, st>>>(q, P, seq_len, lanes, chunk);
+  prefix_chunk_apply_kernel<T><<<grid, kThreads, 0, st>>>(q, P, out, seq_len, lanes, chunk);
+  return check_launch("mqc_prefix_prod_noalloc(chunked)");
+}
+
+}  // namespace
+}  // namespace mqc
+
+extern "C" int mqc_prefix_prod_noalloc(const void* q, void* out, int64_t batch, int64_t seq_len,
+                                       int64_t lanes, int dtype, void* stream) {
+  using namespace mqc;
+  clear_error();
+  MQC_REQUIRE(dtype_ok(dtype), MQC_ERR_INVALID_VALUE, "mqc_prefix_prod_noalloc: unknown dtype %d",
+              dtype);
+  MQC_REQUIRE(batch >= 0 && seq_len >= 0 && lanes >= 0, MQC_ERR_INVALID_VALUE,
+              "mqc_prefix_prod_noalloc: negative size");
+  if (batch == 0 || seq_len == 0 || lanes == 0) return MQC_OK;
+  MQC_REQUIRE(q != nullptr && out != nullptr, MQC_ERR_INVALID_VALUE,
+              "mqc_prefix_prod_noalloc: null pointer");
+  const uintptr_t al = dtype == MQC_DTYPE_F32 ? 16 : 8;
+  MQC_REQUIRE(aligned(q, al) && aligned(out, al), MQC_ERR_MISALIGNED,
+              "mqc_prefix_prod_noalloc: pointers must be %d-byte aligned", int(al));
+  if (dtype == MQC_DTYPE_F32)
+    return launch_noalloc<float>(q, out, batch, seq_len, lanes, as_stream(stream));
+  return launch_noalloc<__nv_bfloat16>(q, out, batch, seq_len, lanes, as_stream(stream));
 }
