@@ -154,7 +154,15 @@ typedef struct mqc_ssm_scan_args {
   float* hT;
   int32_t* status;
   int64_t wait_poll_limit;
+  /* Optional state checkpoints for the backward: with ckpt != NULL and
+   * ckpt_every = MQC_SSM_CKPT_EVERY, the state after steps K-1, 2K-1, ... (K =
+   * ckpt_every, all < T-1) is written to ckpt [B, ceil(T/K)-1, D, N, 4] fp32. */
+  float* ckpt;
+  int64_t ckpt_every;
 } mqc_ssm_scan_args;
+
+/* The checkpoint interval the backward expects. */
+#define MQC_SSM_CKPT_EVERY 8
 
 /* Full scan over T. With MQC_SSM_Q_GIVEN this replaces
  * ssm_forward_fused(q, B, S, C, D), ssm_fused.py:340-401; without it, it is the
@@ -162,6 +170,53 @@ typedef struct mqc_ssm_scan_args {
  * models/quaternion_mamba2_block.py:214-228 (z = Delta*Lambda, Cayley, scan)
  * that never materialises z or q. */
 MQC_API int mqc_ssm_scan_fwd(const mqc_ssm_scan_args* args, void* stream);
+
+/*
+ * Backward of mqc_ssm_scan_fwd without Q_GIVEN (the fused Cayley form). The
+ * reference has no GPU backward (its Triton kernels are not differentiable);
+ * this computes the gradients torch autograd takes through the reference's CPU
+ * composition (block._ssm_forward lines 214-228 with cayley_discretization_reference
+ * and the ssm_step_reference loop). Per (b, d, n), in reverse time:
+ *   lambda_t = conj(C_t) (x) dy_t + conj(q_{t+1}) (x) lambda_{t+1}   (+ dhT at t = T-1)
+ *   dq_t = lambda_t (x) conj(h_{t-1});  dz_t = (dq/dz)^T dq_t;  z_t = delta_t Lambda
+ *   ddelta_t = sum_n <dz_t, Lambda>;     dLambda += delta_t dz_t
+ *   dB_t = lambda_t (x) conj(S_t);       dS_t = sum_n conj(B_t) (x) lambda_t + D dy_t
+ *   dC_t = dy_t (x) conj(h_t);           dh0 = conj(q_0) (x) lambda_0
+ * States are recomputed from the forward's checkpoints (MQC_SSM_CKPT_EVERY).
+ * Inputs as in mqc_ssm_scan_args; dy [B,T,D,4] dtype; dhT [B,D,N,4] fp32 or NULL.
+ * Outputs: ddelta [B,T,D] dtype; dlambda_part [B,D,N,4] fp32 (per-batch partial
+ * sums, to be summed over B); ds like s (dtype); dh0 [B,D,N,4] fp32 or NULL;
+ * dBm/dCm: with BC_SHARED fp32 [B,T,N,4] accumulators the caller zero-fills,
+ * otherwise dtype [B,T,D,N,4]. The gradient of the skip weight D is
+ * sum <dy, S>, which needs no scan. Shared dB/dC are summed over channels with
+ * float atomics, so their low bits can vary from run to run.
+ */
+typedef struct mqc_ssm_scan_bwd_args {
+  int64_t batch, seq_len, channels, d_state;
+  int32_t dtype;
+  int32_t flags; /* MQC_SSM_BC_SHARED, MQC_SSM_S_REAL */
+  float eps;
+  int32_t ckpt_every;
+  const void* delta;
+  const float* lambda_;
+  const void* Bm;
+  const void* Cm;
+  const void* s;
+  const float* dskip;
+  int64_t dskip_sb, dskip_st, dskip_sd;
+  const float* h0;
+  const float* ckpt;
+  const void* dy;
+  const float* dhT;
+  void* ddelta;
+  float* dlambda_part;
+  void* dBm;
+  void* dCm;
+  void* ds;
+  float* dh0;
+} mqc_ssm_scan_bwd_args;
+
+MQC_API int mqc_ssm_scan_bwd(const mqc_ssm_scan_bwd_args* args, void* stream);
 
 /* One step with explicit q: h_new = q (x) h_prev + B (x) S, y = sum_n C (x) h_new + D*S.
  * q, Bm, Cm, h_prev, h_new [B,D,N,4]; S [B,D,4]; dskip [B,D] fp32; y [B,D,4].

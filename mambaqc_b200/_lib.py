@@ -46,7 +46,26 @@ class SsmScanArgs(ctypes.Structure):
         ("Cm", _c_void_p), ("s", _c_void_p), ("dskip", _c_void_p),
         ("dskip_sb", _i64), ("dskip_st", _i64), ("dskip_sd", _i64),
         ("h0", _c_void_p), ("y", _c_void_p), ("hT", _c_void_p), ("status", _c_void_p),
-        ("wait_poll_limit", _i64),
+        ("wait_poll_limit", _i64), ("ckpt", _c_void_p), ("ckpt_every", _i64),
+    ]
+
+
+MQC_SSM_CKPT_EVERY = 8
+
+
+class SsmScanBwdArgs(ctypes.Structure):
+    """Mirror of ``mqc_ssm_scan_bwd_args``."""
+
+    _fields_ = [
+        ("batch", _i64), ("seq_len", _i64), ("channels", _i64), ("d_state", _i64),
+        ("dtype", ctypes.c_int32), ("flags", ctypes.c_int32), ("eps", _f32),
+        ("ckpt_every", ctypes.c_int32),
+        ("delta", _c_void_p), ("lambda_", _c_void_p), ("Bm", _c_void_p), ("Cm", _c_void_p),
+        ("s", _c_void_p), ("dskip", _c_void_p),
+        ("dskip_sb", _i64), ("dskip_st", _i64), ("dskip_sd", _i64),
+        ("h0", _c_void_p), ("ckpt", _c_void_p), ("dy", _c_void_p), ("dhT", _c_void_p),
+        ("ddelta", _c_void_p), ("dlambda_part", _c_void_p), ("dBm", _c_void_p),
+        ("dCm", _c_void_p), ("ds", _c_void_p), ("dh0", _c_void_p),
     ]
 
 
@@ -61,6 +80,7 @@ _SIGNATURES = {
     "mqc_prefix_prod": [_c_void_p, _c_void_p, _i64, _i64, _i64, _i32, _c_void_p],
     "mqc_prefix_prod_noalloc": [_c_void_p, _c_void_p, _i64, _i64, _i64, _i32, _c_void_p],
     "mqc_ssm_scan_fwd": [ctypes.POINTER(SsmScanArgs), _c_void_p],
+    "mqc_ssm_scan_bwd": [ctypes.POINTER(SsmScanBwdArgs), _c_void_p],
     "mqc_ssm_step": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                      _c_void_p, _c_void_p, _i64, _i64, _i64, _i32, _c_void_p],
     "mqc_qln_fwd": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,

@@ -32,6 +32,9 @@ struct FwdParams {
   float* hT;
   int* status;
   long long wait_limit;
+  float* ckpt;     // [B, nck, D, N, 4] or nullptr
+  int ckpt_every;  // K: checkpoint after steps K-1, 2K-1, ... < T-1
+  int nck;         // number of checkpoints = ceil(T / K) - 1
   int nb;   // CTAs per batch row
   int cpb;  // max channels per CTA
   int tc;   // timesteps per chunk
@@ -83,6 +86,18 @@ __device__ __forceinline__ float4 cayley_from_const(float dl, float dl2, const L
   const float inv = rcp_nr(den);
   const float s = dl * inv;
   return make_float4(fmaf(-P, inv, inv), s * c.li, s * c.lj, s * c.lk);
+}
+
+// Stores the G states of one lane as checkpoint k (state after step (k+1)*K - 1).
+template <int G, int NG>
+__device__ __forceinline__ void store_ckpt(const FwdParams& p, int b, int c, int ng, int k,
+                                           const float4 (&h)[G]) {
+  float* base = p.ckpt + ((int64_t(b) * p.nck + k) * p.D + c) * int64_t(p.N) * 4;
+#pragma unroll
+  for (int i = 0; i < G; ++i) {
+    const int n = ng + NG * i;
+    if (n < p.N) QIO<float>::st(base + int64_t(n) * 4, h[i]);
+  }
 }
 
 __device__ __forceinline__ float f4_get(const float4& v, int k) {
@@ -254,6 +269,16 @@ inline int validate_and_fill(const mqc_ssm_scan_args* a, FwdParams* p, const cha
   p->hT = a->hT;
   p->status = a->status;
   p->wait_limit = a->wait_poll_limit < 0 ? kDefaultPollLimit : a->wait_poll_limit;
+  p->ckpt = a->ckpt;
+  p->ckpt_every = 0;
+  p->nck = 0;
+  if (a->ckpt != nullptr) {
+    MQC_REQUIRE(a->ckpt_every == MQC_SSM_CKPT_EVERY, MQC_ERR_UNSUPPORTED,
+                "%s: ckpt_every must be %d", name, MQC_SSM_CKPT_EVERY);
+    MQC_REQUIRE(aligned(a->ckpt, 16), MQC_ERR_MISALIGNED, "%s: ckpt must be 16-byte aligned", name);
+    p->ckpt_every = int(a->ckpt_every);
+    p->nck = (p->T + p->ckpt_every - 1) / p->ckpt_every - 1;
+  }
   if (lanes_per_channel(p->N) == 0)
     return fail(MQC_ERR_UNSUPPORTED, "%s: d_state=%d unsupported", name, p->N);
   return MQC_OK;

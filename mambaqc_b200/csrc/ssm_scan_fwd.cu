@@ -214,6 +214,8 @@ __global__ void __launch_bounds__(G == 8 ? kMaxThreadsG8 : kMaxThreads, 1)
         dsk = __ldg(p.dskip + int64_t(b) * p.dsb + int64_t(t) * p.dst + int64_t(c) * p.dsd);
       reduce_store_y<T, NG>(yacc, sv, dsk, ng, active,
                             static_cast<T*>(p.y) + ((int64_t(b) * T_ + t) * D + c) * 4);
+      if (p.ckpt != nullptr && active && (t + 1) % p.ckpt_every == 0 && t + 1 < T_)
+        store_ckpt<G, NG>(p, b, c, ng, (t + 1) / p.ckpt_every - 1, h);
     }
 
     if (k + 1 < nchunks) store_dx(buf ^ 1);

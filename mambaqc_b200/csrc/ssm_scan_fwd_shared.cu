@@ -292,6 +292,8 @@ __global__ void __launch_bounds__(v2_max_threads(G), 1)
                   ? __ldg(p.dskip + int64_t(b) * p.dsb + int64_t(t) * p.dst + int64_t(c) * p.dsd)
                   : 0.f;
       reduce_store_y<T, NG>(ya, sv, dsk, ng, active, yb + int64_t(t) * D * 4);
+      if (p.ckpt != nullptr && active && (t + 1) % p.ckpt_every == 0 && t + 1 < T_)
+        store_ckpt<G, NG>(p, b, c, ng, (t + 1) / p.ckpt_every - 1, h);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);

@@ -52,7 +52,7 @@ def _skip_operand(D: torch.Tensor, bsz: int, seqlen: int, dm: int):
 
 
 def _run_scan(*, flags: int, q=None, delta=None, Lam=None, B, C, S, D, h0=None,
-              return_final_state=False, eps=1e-6, wait_poll_limit=-1):
+              return_final_state=False, eps=1e-6, wait_poll_limit=-1, ckpt=None):
     ref = q if q is not None else delta
     dt = ref.dtype
     bsz, seqlen, dm = ref.shape[0], ref.shape[1], ref.shape[2]
@@ -86,7 +86,8 @@ def _run_scan(*, flags: int, q=None, delta=None, Lam=None, B, C, S, D, h0=None,
         delta=_lib.ptr(dc), lambda_=_lib.ptr(Lc), q=_lib.ptr(qc), Bm=Bc.data_ptr(),
         Cm=Cc.data_ptr(), s=Sc.data_ptr(), dskip=Df.data_ptr(), dskip_sb=dsb, dskip_st=dst,
         dskip_sd=dsd, h0=_lib.ptr(h0c), y=y.data_ptr(), hT=_lib.ptr(hT), status=status.data_ptr(),
-        wait_poll_limit=int(wait_poll_limit))
+        wait_poll_limit=int(wait_poll_limit), ckpt=_lib.ptr(ckpt),
+        ckpt_every=_lib.MQC_SSM_CKPT_EVERY if ckpt is not None else 0)
     with torch.cuda.device(ref.device):
         _lib.call("mqc_ssm_scan_fwd", ctypes.byref(a), _lib.stream_ptr(ref.device))
     if _lib.sync_checks_enabled():
@@ -94,11 +95,100 @@ def _run_scan(*, flags: int, q=None, delta=None, Lam=None, B, C, S, D, h0=None,
     return y, hT
 
 
+def _n_ckpt(seqlen: int) -> int:
+    k = _lib.MQC_SSM_CKPT_EVERY
+    return (seqlen + k - 1) // k - 1
+
+
+def _sum_to(g: torch.Tensor, like: torch.Tensor) -> torch.Tensor:
+    """Reduce a [B,T,D] skip gradient to the shape the skip weight was given in."""
+    if like.dim() == 1:
+        g = g.sum(dim=(0, 1))
+    elif like.dim() == 2:
+        g = g.sum(dim=1)
+    return g.to(like.dtype)
+
+
+class _SsmScanCayley(torch.autograd.Function):
+    """Fused Cayley + scan with its backward (``mqc_ssm_scan_bwd``)."""
+
+    @staticmethod
+    def forward(ctx, delta, Lam, B, C, S, D, h0, eps, wait_poll_limit):
+        dt = delta.dtype
+        bsz, seqlen, dm = delta.shape
+        ds = Lam.shape[1]
+        va = _vec_align(dt)
+        need_grad = any(ctx.needs_input_grad[:7])
+        nck = _n_ckpt(seqlen)
+        ckpt = None
+        if need_grad and nck > 0:
+            ckpt = torch.empty(bsz, nck, dm, ds, 4, dtype=torch.float32, device=delta.device)
+        shared = B.dim() == 4
+        dc = _prep(delta, 4)
+        Lc = _prep(Lam.float(), 16)
+        Bc = _prep(B, 16 if shared else va)
+        Cc = _prep(C, 16 if shared else va)
+        Sc = _prep(S, va)
+        h0c = _prep(h0.float(), 16) if h0 is not None else None
+        y, hT = _run_scan(flags=0, delta=dc, Lam=Lc, B=Bc, C=Cc, S=Sc, D=D, h0=h0c,
+                          return_final_state=True, eps=eps, wait_poll_limit=wait_poll_limit,
+                          ckpt=ckpt)
+        if need_grad:
+            ctx.save_for_backward(dc, Lc, Bc, Cc, Sc, D, h0c, ckpt)
+        ctx.eps = eps
+        ctx.meta = (Lam.dtype, None if h0 is None else h0.dtype)
+        return y, hT
+
+    @staticmethod
+    def backward(ctx, gy, ghT):
+        dc, Lc, Bc, Cc, Sc, D, h0c, ckpt = ctx.saved_tensors
+        lam_dtype, h0_dtype = ctx.meta
+        has_h0 = h0_dtype is not None
+        dt = dc.dtype
+        bsz, seqlen, dm = dc.shape
+        ds = Lc.shape[1]
+        shared = Bc.dim() == 4
+        s_real = Sc.dim() == 3
+        va = _vec_align(dt)
+        dev = dc.device
+        if gy is None:
+            gy = torch.zeros(bsz, seqlen, dm, 4, dtype=dt, device=dev)
+        gyc = _prep(gy.to(dt), va)
+        ghTc = _prep(ghT.float(), 16) if ghT is not None else None
+        Df, dsb, dst, dsd = _skip_operand(D, bsz, seqlen, dm)
+        ddelta = torch.empty_like(dc)
+        dlam_part = torch.empty(bsz, dm, ds, 4, dtype=torch.float32, device=dev)
+        if shared:
+            dB = torch.zeros(Bc.shape, dtype=torch.float32, device=dev)
+            dC = torch.zeros(Cc.shape, dtype=torch.float32, device=dev)
+        else:
+            dB = torch.empty_like(Bc)
+            dC = torch.empty_like(Cc)
+        dS = torch.empty_like(Sc)
+        dh0 = torch.empty(bsz, dm, ds, 4, dtype=torch.float32, device=dev) if has_h0 else None
+        flags = (_lib.MQC_SSM_BC_SHARED if shared else 0) | (_lib.MQC_SSM_S_REAL if s_real else 0)
+        a = _lib.SsmScanBwdArgs(
+            batch=bsz, seq_len=seqlen, channels=dm, d_state=ds, dtype=_lib.dtype_code(dc),
+            flags=flags, eps=float(ctx.eps), ckpt_every=_lib.MQC_SSM_CKPT_EVERY,
+            delta=dc.data_ptr(), lambda_=Lc.data_ptr(), Bm=Bc.data_ptr(), Cm=Cc.data_ptr(),
+            s=Sc.data_ptr(), dskip=Df.data_ptr(), dskip_sb=dsb, dskip_st=dst, dskip_sd=dsd,
+            h0=_lib.ptr(h0c), ckpt=_lib.ptr(ckpt), dy=gyc.data_ptr(), dhT=_lib.ptr(ghTc),
+            ddelta=ddelta.data_ptr(), dlambda_part=dlam_part.data_ptr(), dBm=dB.data_ptr(),
+            dCm=dC.data_ptr(), ds=dS.data_ptr(), dh0=_lib.ptr(dh0))
+        with torch.cuda.device(dev):
+            _lib.call("mqc_ssm_scan_bwd", ctypes.byref(a), _lib.stream_ptr(dev))
+        # skip weight: dL/dD = <dy, S> (no scan involved)
+        gyf = gyc.float()
+        dD_full = gyf[..., 0] * Sc.float() if s_real else (gyf * Sc.float()).sum(-1)
+        return (ddelta, dlam_part.sum(0).to(lam_dtype), dB.to(dt), dC.to(dt), dS,
+                _sum_to(dD_full, D), None if dh0 is None else dh0.to(h0_dtype), None, None)
+
+
 def ssm_scan_cayley(delta: torch.Tensor, Lambda: torch.Tensor, B: torch.Tensor,
                     C: torch.Tensor, S: torch.Tensor, D: torch.Tensor,
                     h0: torch.Tensor | None = None, eps: float = 1e-6,
                     return_final_state: bool = False, wait_poll_limit: int = -1):
-    """Fused Cayley + quaternion selective scan.
+    """Fused Cayley + quaternion selective scan (differentiable).
 
     delta [B,T,D] (positive step sizes), Lambda [D,N,4] (fp32 continuous
     dynamics), B/C [B,T,N,4] shared or [B,T,D,N,4] per-channel, S [B,T,D] real or
@@ -107,7 +197,9 @@ def ssm_scan_cayley(delta: torch.Tensor, Lambda: torch.Tensor, B: torch.Tensor,
     h_t = q_t (x) h_{t-1} + B_t (x) S_t, y_t = sum_n C_t (x) h_t + D S_t.
 
     Returns y [B,T,D,4] (dtype of delta), plus the final fp32 state
-    h_T [B,D,N,4] when ``return_final_state``.
+    h_T [B,D,N,4] when ``return_final_state``. Gradients flow to every tensor
+    argument through ``mqc_ssm_scan_bwd`` (states recomputed from checkpoints
+    the forward writes every 8 steps when a gradient is needed).
     """
     assert delta.dim() == 3, f"delta must be [B,T,D], got {tuple(delta.shape)}"
     assert Lambda.dim() == 3 and Lambda.shape[-1] == 4, "Lambda must be [D,N,4]"
@@ -119,9 +211,8 @@ def ssm_scan_cayley(delta: torch.Tensor, Lambda: torch.Tensor, B: torch.Tensor,
     else:
         assert tuple(B.shape) == (bsz, seqlen, dm, ds, 4) and B.shape == C.shape
     assert tuple(S.shape) in ((bsz, seqlen, dm), (bsz, seqlen, dm, 4))
-    y, hT = _run_scan(flags=0, delta=delta, Lam=Lambda, B=B, C=C, S=S, D=D, h0=h0,
-                      return_final_state=return_final_state, eps=eps,
-                      wait_poll_limit=wait_poll_limit)
+    _lib.require_cuda(delta, Lambda, B, C, S, D, h0, what="ssm_scan_cayley")
+    y, hT = _SsmScanCayley.apply(delta, Lambda, B, C, S, D, h0, eps, wait_poll_limit)
     return (y, hT) if return_final_state else y
 
 

@@ -4,6 +4,8 @@ device (validation happens on the host, so these calls never launch)."""
 
 import ctypes
 import re
+import shutil
+import subprocess
 from pathlib import Path
 
 import pytest
@@ -50,9 +52,29 @@ def test_version_and_status_strings():
     assert lib.mqc_status_string(999) == b"unknown status"
 
 
-def test_struct_layout_matches_header():
-    # 4 int64 + 4 int32 + 7 pointers + 3 int64 + 4 pointers + 1 int64 on LP64
-    assert ctypes.sizeof(_lib.SsmScanArgs) == 4 * 8 + 4 * 4 + 7 * 8 + 3 * 8 + 4 * 8 + 8
+def _c_offsets(struct, fields, tmp_path):
+    """sizeof and offsetof of a header struct, from a tiny C program built with gcc."""
+    src = tmp_path / "layout.c"
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "mambaqc_b200.h"',
+             "int main(void) {", f'  printf("%zu\\n", sizeof({struct}));']
+    lines += [f'  printf("%zu\\n", offsetof({struct}, {f}));' for f in fields]
+    lines += ["  return 0;", "}"]
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", f"-I{HEADER.parent}", str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()
+    return [int(v) for v in out]
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="needs gcc")
+@pytest.mark.parametrize("cstruct,pystruct", [("mqc_ssm_scan_args", "SsmScanArgs"),
+                                              ("mqc_ssm_scan_bwd_args", "SsmScanBwdArgs")])
+def test_struct_layout_matches_header(cstruct, pystruct, tmp_path):
+    py = getattr(_lib, pystruct)
+    fields = [f for f, _ in py._fields_]
+    got = _c_offsets(cstruct, fields, tmp_path)
+    assert got[0] == ctypes.sizeof(py)
+    assert got[1:] == [getattr(py, f).offset for f in fields]
 
 
 @no_gpu
