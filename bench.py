@@ -50,8 +50,8 @@ def parse_args():
     ap = argparse.ArgumentParser(description=__doc__,
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--dtype", choices=["fp32", "bf16"], default="fp32")
     ap.add_argument("--layout", choices=["shared", "perchannel"], default="shared")
@@ -59,6 +59,10 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=15.0,
                     help="seconds of CPU work for the cpu_baseline sample")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the forward+backward and per-channel-layout sub-measurements")
+    ap.add_argument("--only", choices=["fwd_bwd", "perchannel"], default=None,
+                    help="run only this sub-measurement and print it (profiling aid)")
     return ap.parse_args()
 
 
@@ -125,7 +129,7 @@ class ClockSampler:
             os.close(fd)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
 
@@ -296,6 +300,16 @@ def run_b200(args, world, rank, local):
 
     dev = torch.device(f"cuda:{local}")
     torch.cuda.set_device(dev)
+    if args.only is not None:
+        stream = torch.cuda.current_stream(dev)
+        if args.only == "fwd_bwd":
+            inp = make_inputs(dev, args.dtype, args.layout, seed=1234 + rank)
+            res = run_fwd_bwd(args, inp, dev, world, stream, ssm_scan_cayley)
+        else:
+            res = run_perchannel(args, dev, world, stream, ssm_scan_cayley, measured_peaks()[0])
+        if rank == 0:
+            print(json.dumps({"only": args.only, **res}), flush=True)
+        return 0
     inp = make_inputs(dev, args.dtype, args.layout, seed=1234 + rank)
     stream = torch.cuda.current_stream(dev)
     out = {}
@@ -339,6 +353,15 @@ def run_b200(args, world, rank, local):
     if not args.no_e2e:
         e2e = run_e2e(args, inp, dev, world, stream, ssm_scan_cayley)
 
+    extras = {}
+    if not args.no_extras:
+        extras["fwd_bwd"] = run_fwd_bwd(args, inp, dev, world, stream, ssm_scan_cayley)
+        if args.layout == "shared":
+            del inp, out
+            torch.cuda.empty_cache()
+            extras["perchannel_fwd"] = run_perchannel(args, dev, world, stream, ssm_scan_cayley,
+                                                      peaks)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, sample, threads, steps, elapsed = cpu_reference_sample(args.cpu_budget_s, args.dtype,
@@ -360,6 +383,7 @@ def run_b200(args, world, rank, local):
                        "l2": "inputs larger than L2 (310+ MB per step)"},
             "roofline": roofline, "roofline_hbm": roofline_hbm,
             "gpu_launches": args.steps, "clocks": clk, "e2e": e2e, "cpu_baseline": cpu,
+            **extras,
         }
         print(json.dumps(line), flush=True)
     return 0
@@ -387,6 +411,54 @@ def run_e2e(args, inp, dev, world, stream, op):
     return {"value": BATCH * SEQ * world / (ms / 1e3), "unit": "tokens/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms,
             "steps": steps, "path": "pinned host -> device copies, fused scan, y -> pinned host"}
+
+
+def run_fwd_bwd(args, inp, dev, world, stream, op):
+    """Forward + backward of the fused scan (config 3 names both): one step = the
+    forward with checkpoints plus the backward for a fixed upstream gradient."""
+    leaves = {k: (v.detach().requires_grad_() if k != "D" else v) for k, v in inp.items()}
+    gy = torch.randn(BATCH, SEQ, CHANNELS, 4, device=dev, dtype=inp["delta"].dtype)
+
+    def step():
+        for v in leaves.values():
+            v.grad = None
+        y = op(leaves["delta"], leaves["Lambda"], leaves["B"], leaves["C"], leaves["x"],
+               leaves["D"])
+        y.backward(gy)
+
+    steps = max(3, min(args.steps, 10))
+    ms = timed(step, steps, max(3, min(args.warmup, 3)), world, stream) / steps
+    ms = max_over_ranks(ms, world, dev)
+    # kernels per step: scan forward, scan backward, plus torch's zero-fill of the
+    # shared dB/dC accumulators, the casts and the sums over batch
+    return {"value": BATCH * SEQ * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+            "steps": steps, "what": "scan forward (with checkpoints) + backward, fp32"}
+
+
+def run_perchannel(args, dev, world, stream, op, peaks):
+    """The reference block's layout: per-channel B/C [4,2048,1536,64,4]. HBM-bound:
+    the roofline is the measured copy bandwidth."""
+    inp = make_inputs(dev, args.dtype, "perchannel", seed=4321)
+    out = {}
+
+    def step():
+        out["y"] = op(inp["delta"], inp["Lambda"], inp["B"], inp["C"], inp["x"], inp["D"])
+
+    step()
+    torch.cuda.synchronize()
+    y_bytes = out["y"].numel() * out["y"].element_size()
+    steps = max(3, min(args.steps, 10))
+    ms = timed(step, steps, max(3, min(args.warmup, 3)), world, stream) / steps
+    abytes = algorithmic_bytes(inp, y_bytes)
+    gbs = abytes / (ms / 1e3) / 1e9
+    ms_max = max_over_ranks(ms, world, dev)
+    res = {"value": BATCH * SEQ * world / (ms_max / 1e3), "unit": "tokens/s", "ms_per_step": ms_max,
+           "steps": steps,
+           "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                        "frac": gbs / peaks["hbm_gbs"], "algorithmic_bytes_per_launch": abytes}}
+    del inp, out
+    torch.cuda.empty_cache()
+    return res
 
 
 def main():

@@ -141,37 +141,27 @@ __device__ __forceinline__ float4 cayley_closed(float4 z, float eps) {
 
 // Vector-Jacobian product of cayley_closed: given z and g = dL/dq, returns dL/dz.
 // With w = z/2 = (a, v), den = (1-a)^2 + |v|^2, D = max(den, eps),
-// num_r = (1-a)(1+a) - |v|^2, q = (num_r, 2v) / D. When den >= eps:
-//   dq_r/da = (2(1-a) num_r - 2a D) / D^2,   dq_r/dv = -4(1-a) v / D^2,
-//   dq_v/da = 4(1-a) v / D^2,                dq_v/dv = 2 I / D - 4 v v^T / D^2;
-// when den < eps, D is the constant eps and only the numerators vary.
+// num_r = (1-a)(1+a) - |v|^2, q = (num_r, 2v) / D, and u = 1 where the clamp is
+// inactive (den >= eps), u = 0 where it is (D is then the constant eps):
+//   dq_r/da = -2a/D + u 2(1-a) num_r/D^2     dq_r/dv = -2v/D - u 2 num_r v/D^2
+//   dq_v/da = u 4(1-a) v/D^2                 dq_v/dv = 2I/D - u 4 v v^T/D^2
+// Branch-free; dz = (dL/da, dL/dv) / 2.
 __device__ __forceinline__ float4 cayley_vjp(float4 z, float4 g, float eps) {
   const float a = 0.5f * z.x;
   const float v1 = 0.5f * z.y, v2 = 0.5f * z.z, v3 = 0.5f * z.w;
   const float om = 1.f - a;
-  const float op = 1.f + a;
   const float vv = fmaf(v1, v1, fmaf(v2, v2, v3 * v3));
   const float den = fmaf(om, om, vv);
+  const float D = fmaxf(den, eps);
+  const float inv = rcp_nr(D);
+  const float w = den >= eps ? inv * inv : 0.f;
+  const float num_r = fmaf(om, 1.f + a, -vv);
   const float gv = fmaf(g.y, v1, fmaf(g.z, v2, g.w * v3));
-  float da, d1, d2, d3;
-  if (den >= eps) {
-    const float inv = 1.f / den;
-    const float inv2 = inv * inv;
-    const float num_r = fmaf(om, op, -vv);
-    da = (g.x * fmaf(2.f * om, num_r, -2.f * a * den) + 4.f * om * gv) * inv2;
-    const float cv = -4.f * (om * g.x + gv) * inv2;  // coefficient of v
-    const float cg = 2.f * inv;                      // coefficient of g_v
-    d1 = fmaf(cv, v1, cg * g.y);
-    d2 = fmaf(cv, v2, cg * g.z);
-    d3 = fmaf(cv, v3, cg * g.w);
-  } else {
-    const float inv = 1.f / eps;
-    da = -2.f * a * g.x * inv;
-    d1 = 2.f * (g.y - g.x * v1) * inv;
-    d2 = 2.f * (g.z - g.x * v2) * inv;
-    d3 = 2.f * (g.w - g.x * v3) * inv;
-  }
-  return make_float4(0.5f * da, 0.5f * d1, 0.5f * d2, 0.5f * d3);
+  // halves folded in: dz = 0.5 * (dL/da, dL/dv)
+  const float hw = w * om;
+  const float da = fmaf(g.x, fmaf(hw, num_r, -a * inv), 2.f * hw * gv);
+  const float cv = -(g.x * fmaf(w, num_r, inv) + 2.f * w * gv);  // coefficient of v
+  return make_float4(da, fmaf(cv, v1, g.y * inv), fmaf(cv, v2, g.z * inv), fmaf(cv, v3, g.w * inv));
 }
 
 // ---------------------------------------------------------------------------

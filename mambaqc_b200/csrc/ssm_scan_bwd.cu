@@ -15,9 +15,12 @@
 //      buffer (only the lane itself reads them back),
 //   3. runs the adjoint recursion backwards over the K steps.
 // Per-(t, channel) results (ddelta, dS) are summed over the NG lanes with
-// shuffles; dLambda accumulates in registers over t; channel-shared dB/dC are
-// summed over the CTA's channels in a shared-memory tile with shared atomics,
-// then added to global fp32 accumulators with vector atomics once per sub-block.
+// shuffles; dLambda accumulates in registers over t; channel-shared dB/dC go to
+// a per-warp shared-memory slice, the slices are summed over the CTA's warps in a
+// fixed order at the end of each sub-block, and the CTA's sum is added to global
+// fp32 accumulators with one vector atomic per (t, n, tensor).
+#include <type_traits>
+
 #include "ssm_scan_common.cuh"
 
 namespace mqc {
@@ -27,6 +30,7 @@ constexpr int kSub = MQC_SSM_CKPT_EVERY;
 // Warps per CTA: the recomputed-state buffer is kSub * G * 32 lanes * 16 B per
 // warp, so the CTA shrinks as G grows (G=2: 8 warps, 64 KiB; G=8: 2 warps).
 __host__ __device__ constexpr int bwd_warps(int g) { return 16 / g; }
+constexpr int kMaxBwdSmem = 227 * 1024;
 
 struct BwdParams {
   int B, T, D, N;
@@ -68,17 +72,82 @@ __device__ __forceinline__ float lane_sum(float v) {
   return v;
 }
 
-template <typename T, int G, int NG, bool BC_SHARED, bool S_REAL>
+// In-register reduce-scatter of V values over the NG lanes of a channel by
+// recursive halving: afterwards the lane holds W = max(V / NG, 1) sums
+// v[0..W) whose original indices are base .. base + W - 1. Lanes that differ
+// only in ng bits >= log2(V) hold the same sums.
+template <int V, int NG>
+__device__ __forceinline__ int reduce_scatter(float (&v)[V], int ng) {
+  int base = 0;
+#pragma unroll
+  for (int lvl = 0; (1 << lvl) < NG; ++lvl) {
+    const int m = 1 << lvl;
+    constexpr int kUnused = 0;
+    (void)kUnused;
+    const int W = V >> lvl;
+    if (W > 1) {
+      const int half = W >> 1;
+      const bool upper = (ng & m) != 0;
+#pragma unroll
+      for (int j = 0; j < (V >> (lvl + 1)); ++j) {
+        const float send = upper ? v[j] : v[j + half];
+        const float keep = upper ? v[j + half] : v[j];
+        v[j] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+      }
+      if (upper) base += half;
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], m);
+    }
+  }
+  return base;
+}
+
+// Double-buffered shared-memory stage of one sub-block's inputs (fp32,
+// channel-shared B/C): B and C rows [kSub][2][N] float4, delta and x (or S) and
+// dy of the CTA's channels [kSub][cpb], and the lanes' start states
+// [warps][G][32] float4. Filled with cp.async one sub-block ahead.
+struct StageLayout {
+  size_t bc, dl, sx, gy, hst, bytes;
+};
+
+__host__ __device__ inline StageLayout stage_layout(int N, int cpb, int warps, int G, bool s_real) {
+  StageLayout L;
+  size_t off = 0;
+  L.bc = off;
+  off += size_t(kSub) * 2 * N * 16;
+  L.dl = off;
+  off = align_up(off + size_t(kSub) * cpb * 4, 16);
+  L.sx = off;
+  off = align_up(off + size_t(kSub) * cpb * (s_real ? 4 : 16), 16);
+  L.gy = off;
+  off += size_t(kSub) * cpb * 16;
+  L.hst = off;
+  off += size_t(warps) * G * 32 * 16;
+  L.bytes = off;
+  return L;
+}
+
+template <typename T, int G, int NG, bool BC_SHARED, bool S_REAL, bool STAGE>
 __global__ void __launch_bounds__(32 * bwd_warps(G))
     ssm_scan_bwd_kernel(const BwdParams p) {
   constexpr int kBwdWarps = bwd_warps(G);
   constexpr int CPW = 32 / NG;
   constexpr int NP = NG * G;
+  // fp32 with channel-shared B/C (when the stage fits): inputs staged in shared
+  // memory by cp.async
+  constexpr bool STAGED = STAGE && BC_SHARED && std::is_same<T, float>::value;
+  constexpr bool HS_REG = G == 2;      // recomputed states in registers (else shared)
+  constexpr int NV = S_REAL ? 2 : 8;   // per-(t, channel) sums: ddelta, dS (padded)
+  constexpr int V = kSub * NV;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  // per warp: [kSub][G][32 lanes] float4 recomputed states; then (shared B/C)
-  // the dB/dC tile [kSub][NP][8] floats
+  // [per warp: kSub x G x 32 lanes float4 states, when not in registers]
+  // [per warp: private dB/dC slice kSub x 2 x NP float4, for channel-shared B/C]
+  const size_t hs_bytes = HS_REG ? 0 : size_t(kBwdWarps) * kSub * G * 32 * 16;
   float4* hs_all = reinterpret_cast<float4*>(smem_raw);
-  float* acc = reinterpret_cast<float*>(smem_raw + size_t(kBwdWarps) * kSub * G * 32 * 16);
+  float4* slices = reinterpret_cast<float4*>(smem_raw + hs_bytes);
+  const size_t slice_bytes = BC_SHARED ? size_t(kBwdWarps) * kSub * 2 * NP * 16 : 0;
+  const StageLayout SL = stage_layout(p.N, p.cpb, kBwdWarps, G, S_REAL);
+  unsigned char* stage_base = smem_raw + hs_bytes + slice_bytes;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ng = lane % NG;
@@ -88,7 +157,8 @@ __global__ void __launch_bounds__(32 * bwd_warps(G))
   const bool active = cl < p.cpb && c_raw < p.D;
   const int c = active ? c_raw : 0;
   const int T_ = p.T, D = p.D, N = p.N;
-  float4* hs = hs_all + size_t(warp) * kSub * G * 32;
+  float4* hs_smem = hs_all + size_t(warp) * kSub * G * 32;
+  float4* slice = slices + size_t(warp) * kSub * 2 * NP;
 
   const T* gdelta = static_cast<const T*>(p.delta);
   const T* gs = static_cast<const T*>(p.s);
@@ -97,45 +167,126 @@ __global__ void __launch_bounds__(32 * bwd_warps(G))
   const T* gdy = static_cast<const T*>(p.dy);
 
   LamConst lc[G];
-  float4 lamq[G];   // Lambda as a quaternion (for z = delta * Lambda)
   float4 carry[G];  // conj(q_{t+1}) (x) lambda_{t+1}
   float4 dlam[G];
   float4 hstart[G];
+  bool nok[G];
 #pragma unroll
   for (int i = 0; i < G; ++i) {
     const int n = ng + NG * i;
-    lamq[i] = f4_zero();
+    nok[i] = active && n < N;
     carry[i] = f4_zero();
     dlam[i] = f4_zero();
     lc[i] = LamConst{0.f, 0.f, 0.f, 0.f, 0.f};
-    if (active && n < N) {
-      lamq[i] = QIO<float>::ld(p.lam + (int64_t(c) * N + n) * 4);
-      lc[i] = make_lam_const(lamq[i]);
+    if (nok[i]) {
+      lc[i] = make_lam_const(QIO<float>::ld(p.lam + (int64_t(c) * N + n) * 4));
       if (p.dhT != nullptr) carry[i] = QIO<float>::ld(p.dhT + ((int64_t(b) * D + c) * N + n) * 4);
     }
   }
+  const float eps = p.eps;
+  const int64_t bc_row = BC_SHARED ? int64_t(N) * 4 : int64_t(D) * N * 4;  // per-step stride
+  const int64_t bc_lane = BC_SHARED ? int64_t(ng) * 4 : (int64_t(c) * N + ng) * 4;
+  float4 hsr[HS_REG ? kSub : 1][G];
 
-  auto bc_index = [&](int t, int n) -> int64_t {  // element offset of B/C at (b, t, c, n)
-    if (BC_SHARED) return ((int64_t(b) * T_ + t) * N + n) * 4;
-    return (((int64_t(b) * T_ + t) * D + c) * N + n) * 4;
-  };
-  auto load_s = [&](int t) -> float4 {
-    if (!active) return f4_zero();
-    const int64_t row = (int64_t(b) * T_ + t) * D + c;
-    if (S_REAL) return make_float4(to_f(gs[row]), 0.f, 0.f, 0.f);
-    return QIO<T>::ld(gs + row * 4);
+  // issue the cp.async copies of sub-block `sb`'s inputs into stage buffer `buf`
+  auto issue_stage = [&](int sb, int buf) {
+    unsigned char* st = stage_base + size_t(buf) * SL.bytes;
+    const int t0 = sb * kSub;
+    const int len = min(kSub, T_ - t0);
+    const float* fB = reinterpret_cast<const float*>(gB);
+    const float* fC = reinterpret_cast<const float*>(gC);
+    float4* sbc = reinterpret_cast<float4*>(st + SL.bc);
+    for (int e = threadIdx.x; e < len * 2 * N; e += blockDim.x) {
+      const int tt = e / (2 * N), r = e % (2 * N), which = r / N, n = r % N;
+      const float* src = (which ? fC : fB) + ((int64_t(b) * T_ + t0 + tt) * N + n) * 4;
+      cp_async16(sbc + (tt * 2 + which) * N + n, src, true);
+    }
+    float* sdl = reinterpret_cast<float*>(st + SL.dl);
+    float* ssx = reinterpret_cast<float*>(st + SL.sx);
+    float4* sgy = reinterpret_cast<float4*>(st + SL.gy);
+    const float* fdelta = reinterpret_cast<const float*>(gdelta);
+    const float* fs = reinterpret_cast<const float*>(gs);
+    const float* fdy = reinterpret_cast<const float*>(gdy);
+    for (int e = threadIdx.x; e < len * p.cpb; e += blockDim.x) {
+      const int tt = e / p.cpb, cc = e % p.cpb;
+      const int ch = blockIdx.x * p.cpb + cc;
+      const bool v = ch < D;
+      const int64_t row = v ? (int64_t(b) * T_ + t0 + tt) * D + ch : 0;
+      cp_async4(sdl + e, fdelta + row, v);
+      if (S_REAL) cp_async4(ssx + e, fs + row, v);
+      else cp_async16(reinterpret_cast<float4*>(ssx) + e, fs + row * 4, v);
+      cp_async16(sgy + e, fdy + row * 4, v);
+    }
+    float4* shst = reinterpret_cast<float4*>(st + SL.hst);
+#pragma unroll
+    for (int i = 0; i < G; ++i) {
+      const int n = ng + NG * i;
+      const bool from_ckpt = sb > 0;
+      const bool v = nok[i] && (from_ckpt || p.h0 != nullptr);
+      const float* src = p.ckpt;
+      if (v) {
+        src = from_ckpt ? p.ckpt + ((int64_t(b) * p.nck + (sb - 1)) * D + c) * int64_t(N) * 4 +
+                              int64_t(n) * 4
+                        : p.h0 + ((int64_t(b) * D + c) * N + n) * 4;
+      }
+      cp_async16(shst + (warp * G + i) * 32 + lane, v ? src : p.lam, v);
+    }
+    cp_async_commit();
   };
 
   const int nsub = (T_ + kSub - 1) / kSub;
+  if constexpr (STAGED) {
+    issue_stage(nsub - 1, 0);
+    cp_async_wait_all();
+    __syncthreads();
+  }
   for (int sb = nsub - 1; sb >= 0; --sb) {
     const int t0 = sb * kSub;
     const int len = min(kSub, T_ - t0);
+    const int64_t row0 = (int64_t(b) * T_ + t0) * D + c;  // (b, t0, c) in [B,T,D]
+    const T* B0 = gB + (int64_t(b) * T_ + t0) * bc_row + bc_lane;
+    const T* C0 = gC + (int64_t(b) * T_ + t0) * bc_row + bc_lane;
+    const int buf = (nsub - 1 - sb) & 1;
+    const unsigned char* stg = stage_base + size_t(buf) * SL.bytes;
+    const float4* sbc = reinterpret_cast<const float4*>(stg + SL.bc) + ng;
+    const float* sdl = reinterpret_cast<const float*>(stg + SL.dl) + cl;
+    const float* ssx = reinterpret_cast<const float*>(stg + SL.sx);
+    const float4* sgy = reinterpret_cast<const float4*>(stg + SL.gy) + cl;
+    if constexpr (STAGED) {
+      if (sb > 0) issue_stage(sb - 1, buf ^ 1);
+    }
+    // inputs of step tt of this sub-block (staged or straight from global)
+    auto in_delta = [&](int tt) -> float {
+      if constexpr (STAGED) return sdl[tt * p.cpb];
+      else return active ? to_f(gdelta[row0 + int64_t(tt) * D]) : 0.f;
+    };
+    auto in_s = [&](int tt) -> float4 {
+      if constexpr (STAGED) {
+        if (S_REAL) return make_float4(ssx[tt * p.cpb + cl], 0.f, 0.f, 0.f);
+        return reinterpret_cast<const float4*>(ssx)[tt * p.cpb + cl];
+      } else {
+        if (!active) return f4_zero();
+        const int64_t row = row0 + int64_t(tt) * D;
+        if (S_REAL) return make_float4(to_f(gs[row]), 0.f, 0.f, 0.f);
+        return QIO<T>::ld(gs + row * 4);
+      }
+    };
+    auto in_dy = [&](int tt) -> float4 {
+      if constexpr (STAGED) return sgy[tt * p.cpb];
+      else return active ? QIO<T>::ld(gdy + (row0 + int64_t(tt) * D) * 4) : f4_zero();
+    };
+    auto in_bc = [&](int tt, int i, int which) -> float4 {
+      if constexpr (STAGED) return sbc[(tt * 2 + which) * N + NG * i];
+      else return QIO<T>::ld((which ? C0 : B0) + tt * bc_row + NG * i * 4);
+    };
     // ---- state before the sub-block
 #pragma unroll
     for (int i = 0; i < G; ++i) {
       const int n = ng + NG * i;
       hstart[i] = f4_zero();
-      if (active && n < N) {
+      if constexpr (STAGED) {
+        hstart[i] = reinterpret_cast<const float4*>(stg + SL.hst)[(warp * G + i) * 32 + lane];
+      } else if (nok[i]) {
         if (sb > 0)
           hstart[i] = QIO<float>::ld(p.ckpt + ((int64_t(b) * p.nck + (sb - 1)) * D + c) * int64_t(N) * 4 +
                                      int64_t(n) * 4);
@@ -148,124 +299,169 @@ __global__ void __launch_bounds__(32 * bwd_warps(G))
       float4 h[G];
 #pragma unroll
       for (int i = 0; i < G; ++i) h[i] = hstart[i];
-      for (int tt = 0; tt < len; ++tt) {
-        const int t = t0 + tt;
-        const float dl = active ? to_f(gdelta[(int64_t(b) * T_ + t) * D + c]) : 0.f;
-        const float dl2 = dl * dl;
-        const float4 sv = load_s(t);
 #pragma unroll
-        for (int i = 0; i < G; ++i) {
-          const int n = ng + NG * i;
-          float4 Bv = f4_zero();
-          if (active && n < N) Bv = QIO<T>::ld(gB + bc_index(t, n));
-          const float4 qv = cayley_from_const(dl, dl2, lc[i], p.eps);
-          float4 inj;
-          if (S_REAL) inj = make_float4(sv.x * Bv.x, sv.x * Bv.y, sv.x * Bv.z, sv.x * Bv.w);
-          else inj = qmul(Bv, sv);
-          h[i] = qmul_acc(qv, h[i], inj);
-          hs[(tt * G + i) * 32 + lane] = h[i];
-        }
-      }
-    }
-    if (BC_SHARED) {
-      // zero this sub-block's dB/dC tile
-      for (int e = threadIdx.x; e < kSub * NP * 8; e += blockDim.x) acc[e] = 0.f;
-      __syncthreads();
-    }
-    // ---- adjoint, backwards over the sub-block
-    for (int tt = len - 1; tt >= 0; --tt) {
-      const int t = t0 + tt;
-      const int64_t row = (int64_t(b) * T_ + t) * D + c;
-      const float dl = active ? to_f(gdelta[row]) : 0.f;
-      const float dl2 = dl * dl;
-      const float4 sv = load_s(t);
-      const float4 gy = active ? QIO<T>::ld(gdy + row * 4) : f4_zero();
-      float pd = 0.f;        // sum_n <dz, Lambda>
-      float4 psum = f4_zero();  // sum_n conj(B) (x) lambda (x component only for a real S)
+      for (int tt = 0; tt < kSub; ++tt) {
+        if (tt < len) {
+          const float dl = in_delta(tt);
+          const float dl2 = dl * dl;
+          const float4 sv = in_s(tt);
 #pragma unroll
-      for (int i = 0; i < G; ++i) {
-        const int n = ng + NG * i;
-        const bool ok = active && n < N;
-        float4 Bv = f4_zero(), Cv = f4_zero();
-        if (ok) {
-          Bv = QIO<T>::ld(gB + bc_index(t, n));
-          Cv = QIO<T>::ld(gC + bc_index(t, n));
-        }
-        const float4 hcur = hs[(tt * G + i) * 32 + lane];
-        const float4 hprev = tt > 0 ? hs[((tt - 1) * G + i) * 32 + lane] : hstart[i];
-        // lambda_t = conj(C_t) (x) dy_t + conj(q_{t+1}) (x) lambda_{t+1}
-        const float4 lam = qmul_acc(qconj(Cv), gy, carry[i]);
-        const float4 qv = cayley_from_const(dl, dl2, lc[i], p.eps);
-        const float4 dq = qmul(lam, qconj(hprev));
-        const float4 z = make_float4(dl * lamq[i].x, dl * lamq[i].y, dl * lamq[i].z, dl * lamq[i].w);
-        const float4 dz = cayley_vjp(z, dq, p.eps);
-        pd = fmaf(1.f, dot4(dz, lamq[i]), pd);
-        dlam[i] = axpy4(dl, dz, dlam[i]);
-        float4 dBv, dCv;
-        if (S_REAL) {
-          dBv = make_float4(sv.x * lam.x, sv.x * lam.y, sv.x * lam.z, sv.x * lam.w);
-          psum.x += dot4(Bv, lam);
-        } else {
-          dBv = qmul(lam, qconj(sv));
-          psum = qmul_acc(qconj(Bv), lam, psum);
-        }
-        dCv = qmul(gy, qconj(hcur));
-        if (ok) {
-          if (BC_SHARED) {
-            float* slot = acc + (tt * NP + n) * 8;
-            atomicAdd(slot + 0, dBv.x);
-            atomicAdd(slot + 1, dBv.y);
-            atomicAdd(slot + 2, dBv.z);
-            atomicAdd(slot + 3, dBv.w);
-            atomicAdd(slot + 4, dCv.x);
-            atomicAdd(slot + 5, dCv.y);
-            atomicAdd(slot + 6, dCv.z);
-            atomicAdd(slot + 7, dCv.w);
-          } else {
-            QIO<T>::st(static_cast<T*>(p.dB) + bc_index(t, n), dBv);
-            QIO<T>::st(static_cast<T*>(p.dC) + bc_index(t, n), dCv);
+          for (int i = 0; i < G; ++i) {
+            const float4 Bv = nok[i] ? in_bc(tt, i, 0) : f4_zero();
+            const float4 qv = cayley_from_const(dl, dl2, lc[i], eps);
+            float4 inj;
+            if (S_REAL) inj = make_float4(sv.x * Bv.x, sv.x * Bv.y, sv.x * Bv.z, sv.x * Bv.w);
+            else inj = qmul(Bv, sv);
+            h[i] = qmul_acc(qv, h[i], inj);
+            if constexpr (HS_REG) hsr[tt][i] = h[i];
+            else hs_smem[(tt * G + i) * 32 + lane] = h[i];
           }
         }
-        carry[i] = qmul(qconj(qv), lam);
       }
-      // per-(t, channel) sums over the NG lanes of the channel
-      pd = lane_sum<NG>(pd);
-      psum.x = lane_sum<NG>(psum.x);
-      if (!S_REAL) {
-        psum.y = lane_sum<NG>(psum.y);
-        psum.z = lane_sum<NG>(psum.z);
-        psum.w = lane_sum<NG>(psum.w);
+    }
+    // ---- adjoint, backwards over the sub-block
+    float part[V];  // per (tt, k): k = 0 ddelta, k >= 1 dS components; summed over n later
+#pragma unroll
+    for (int e = 0; e < V; ++e) part[e] = 0.f;
+#pragma unroll
+    for (int tt = kSub - 1; tt >= 0; --tt) {
+      if (tt < len) {
+        const int t = t0 + tt;
+        const float dl = in_delta(tt);
+        const float dl2 = dl * dl;
+        const float4 sv = in_s(tt);
+        const float4 gy = in_dy(tt);
+        float pd = 0.f;
+        float4 psum = f4_zero();
+        if (ng == 0 && active) {  // skip term D * dy, counted once per channel
+          const float dsk = __ldg(p.dskip + int64_t(b) * p.dsb + int64_t(t) * p.dst +
+                                  int64_t(c) * p.dsd);
+          psum = make_float4(dsk * gy.x, dsk * gy.y, dsk * gy.z, dsk * gy.w);
+        }
+#pragma unroll
+        for (int i = 0; i < G; ++i) {
+          float4 Bv = f4_zero(), Cv = f4_zero();
+          if (nok[i]) {
+            Bv = in_bc(tt, i, 0);
+            Cv = in_bc(tt, i, 1);
+          }
+          float4 hcur, hprev;
+          if constexpr (HS_REG) {
+            hcur = hsr[tt][i];
+            hprev = tt > 0 ? hsr[tt > 0 ? tt - 1 : 0][i] : hstart[i];
+          } else {
+            hcur = hs_smem[(tt * G + i) * 32 + lane];
+            hprev = tt > 0 ? hs_smem[((tt > 0 ? tt - 1 : 0) * G + i) * 32 + lane] : hstart[i];
+          }
+          // lambda_t = conj(C_t) (x) dy_t + conj(q_{t+1}) (x) lambda_{t+1}
+          const float4 lam = qmul_acc(qconj(Cv), gy, carry[i]);
+          const float4 qv = cayley_from_const(dl, dl2, lc[i], eps);
+          const float4 dq = qmul(lam, qconj(hprev));
+          const float4 lq = make_float4(lc[i].lr, lc[i].li, lc[i].lj, lc[i].lk);
+          const float4 z = make_float4(dl * lq.x, dl * lq.y, dl * lq.z, dl * lq.w);
+          const float4 dz = cayley_vjp(z, dq, eps);
+          pd += dot4(dz, lq);
+          dlam[i] = axpy4(dl, dz, dlam[i]);
+          float4 dBv;
+          if (S_REAL) {
+            dBv = make_float4(sv.x * lam.x, sv.x * lam.y, sv.x * lam.z, sv.x * lam.w);
+            psum.x += dot4(Bv, lam);
+          } else {
+            dBv = qmul(lam, qconj(sv));
+            psum = qmul_acc(qconj(Bv), lam, psum);
+          }
+          float4 dCv = qmul(gy, qconj(hcur));
+          if (BC_SHARED) {
+            if (!nok[i]) {
+              dBv = f4_zero();
+              dCv = f4_zero();
+            }
+            // sum over the CPW channels this warp holds (lanes ng + NG*k share n)
+#pragma unroll
+            for (int m = NG; m < 32; m <<= 1) {
+              dBv.x += __shfl_xor_sync(0xffffffffu, dBv.x, m);
+              dBv.y += __shfl_xor_sync(0xffffffffu, dBv.y, m);
+              dBv.z += __shfl_xor_sync(0xffffffffu, dBv.z, m);
+              dBv.w += __shfl_xor_sync(0xffffffffu, dBv.w, m);
+              dCv.x += __shfl_xor_sync(0xffffffffu, dCv.x, m);
+              dCv.y += __shfl_xor_sync(0xffffffffu, dCv.y, m);
+              dCv.z += __shfl_xor_sync(0xffffffffu, dCv.z, m);
+              dCv.w += __shfl_xor_sync(0xffffffffu, dCv.w, m);
+            }
+            // the warp's first channel lanes write every (tt, n < NP) slot, so the
+            // slice needs no clearing; consecutive n per lane: conflict-free
+            if (lane < NG) {
+              const int n = ng + NG * i;
+              slice[(tt * 2 + 0) * NP + n] = dBv;
+              slice[(tt * 2 + 1) * NP + n] = dCv;
+            }
+          } else if (nok[i]) {
+            T* dBp = static_cast<T*>(p.dB) + (B0 - gB) + tt * bc_row + NG * i * 4;
+            T* dCp = static_cast<T*>(p.dC) + (C0 - gC) + tt * bc_row + NG * i * 4;
+            QIO<T>::st(dBp, dBv);
+            QIO<T>::st(dCp, dCv);
+          }
+          carry[i] = qmul(qconj(qv), lam);
+        }
+        part[tt * NV + 0] = pd;
+        part[tt * NV + 1] = psum.x;
+        if (!S_REAL) {
+          part[tt * NV + 2] = psum.y;
+          part[tt * NV + 3] = psum.z;
+          part[tt * NV + 4] = psum.w;
+        }
       }
-      if (active && ng == 0) {
-        const float dsk = __ldg(p.dskip + int64_t(b) * p.dsb + int64_t(t) * p.dst + int64_t(c) * p.dsd);
-        QIO<T>::st1(static_cast<T*>(p.ddelta) + row, pd);
-        if (S_REAL) {
-          QIO<T>::st1(static_cast<T*>(p.ds) + row, fmaf(dsk, gy.x, psum.x));
-        } else {
-          QIO<T>::st(static_cast<T*>(p.ds) + row * 4, axpy4(dsk, gy, psum));
+    }
+    // ---- per-(t, channel) sums over the NG lanes of the channel, then stores
+    {
+      const int base = reduce_scatter<V, NG>(part, ng);
+      constexpr int W = (V / NG) > 0 ? (V / NG) : 1;
+      constexpr int kLogV = (V >= 64) ? 6 : (V >= 32 ? 5 : (V >= 16 ? 4 : (V >= 8 ? 3 : 1)));
+      const bool writer = active && (NG <= V || (ng >> kLogV) == 0);
+#pragma unroll
+      for (int j = 0; j < W; ++j) {
+        const int idx = base + j;
+        const int tt = idx / NV, k = idx % NV;
+        if (writer && tt < len) {
+          const int64_t row = row0 + int64_t(tt) * D;
+          if (k == 0) {
+            QIO<T>::st1(static_cast<T*>(p.ddelta) + row, part[j]);
+          } else if (S_REAL) {
+            QIO<T>::st1(static_cast<T*>(p.ds) + row, part[j]);
+          } else if (k <= 4) {
+            QIO<T>::st1(static_cast<T*>(p.ds) + row * 4 + (k - 1), part[j]);
+          }
         }
       }
     }
     if (BC_SHARED) {
+      // sum the warps' slices (fixed order) and add the CTA's share to global
       __syncthreads();
       float* dB = static_cast<float*>(p.dB);
       float* dC = static_cast<float*>(p.dC);
-      for (int e = threadIdx.x; e < len * N * 2; e += blockDim.x) {
-        const int which = e & 1, tn = e >> 1;
-        const int tt = tn / N, n = tn % N;
-        const float* slot = acc + (tt * NP + n) * 8 + which * 4;
-        const float4 v = make_float4(slot[0], slot[1], slot[2], slot[3]);
-        float* dst = (which ? dC : dB) + ((int64_t(b) * T_ + t0 + tt) * N + n) * 4;
+      for (int e = threadIdx.x; e < len * 2 * N; e += blockDim.x) {
+        const int n = e % N, tw = e / N;  // tw = tt * 2 + which
+        float4 v = slices[tw * NP + n];
+        for (int w = 1; w < kBwdWarps; ++w) {
+          const float4 u = slices[size_t(w) * kSub * 2 * NP + tw * NP + n];
+          v.x += u.x;
+          v.y += u.y;
+          v.z += u.z;
+          v.w += u.w;
+        }
+        const int tt = tw >> 1;
+        float* dst = ((tw & 1) ? dC : dB) + ((int64_t(b) * T_ + t0 + tt) * N + n) * 4;
         atomicAdd(reinterpret_cast<float4*>(dst), v);
       }
-      __syncthreads();
     }
+    if constexpr (STAGED) cp_async_wait_all();
+    if (BC_SHARED) __syncthreads();  // slices free; next stage (if any) visible
   }
 
 #pragma unroll
   for (int i = 0; i < G; ++i) {
     const int n = ng + NG * i;
-    if (active && n < N) {
+    if (nok[i]) {
       const int64_t off = ((int64_t(b) * D + c) * N + n) * 4;
       QIO<float>::st(p.dlam_part + off, dlam[i]);
       if (p.dh0 != nullptr) QIO<float>::st(p.dh0 + off, carry[i]);  // conj(q_0) (x) lambda_0
@@ -278,14 +474,20 @@ int launch_bwd(BwdParams p, cudaStream_t st) {
   constexpr int kBwdWarps = bwd_warps(G);
   constexpr int CPW = 32 / NG;
   p.cpb = kBwdWarps * CPW;
-  const size_t smem = size_t(kBwdWarps) * kSub * G * 32 * 16 +
-                      (BC_SHARED ? size_t(kSub) * NG * G * 8 * sizeof(float) : 0);
-  auto kern = ssm_scan_bwd_kernel<T, G, NG, BC_SHARED, S_REAL>;
+  const size_t base = (G == 2 ? 0 : size_t(kBwdWarps) * kSub * G * 32 * 16) +
+                      (BC_SHARED ? size_t(kBwdWarps) * kSub * 2 * NG * G * 16 : 0);
+  const size_t staged = base + 2 * stage_layout(p.N, p.cpb, kBwdWarps, G, S_REAL).bytes;
+  const bool can_stage =
+      BC_SHARED && std::is_same<T, float>::value && staged <= size_t(kMaxBwdSmem);
+  const size_t smem = can_stage ? staged : base;
+  auto kern = can_stage ? ssm_scan_bwd_kernel<T, G, NG, BC_SHARED, S_REAL, true>
+                        : ssm_scan_bwd_kernel<T, G, NG, BC_SHARED, S_REAL, false>;
   if (smem > 48 * 1024) {
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess)
-      return fail(MQC_ERR_CUDA, "mqc_ssm_scan_bwd: smem attribute: %s", cudaGetErrorString(e));
+      return fail(MQC_ERR_CUDA, "mqc_ssm_scan_bwd: smem attribute (%zu B): %s", smem,
+                  cudaGetErrorString(e));
   }
   dim3 grid{unsigned((p.D + p.cpb - 1) / p.cpb), unsigned(p.B), 1u};
   kern<<<grid, 32 * kBwdWarps, smem, st>>>(p);

@@ -38,3 +38,32 @@ def test_config1_block_forward_and_state():
         out, h_T = blk(x.to(DEV), return_ssm_state=True)
     assert rel_l2(out, out_ref) < RTOL_F32
     assert rel_l2(h_T, h_ref) < RTOL_F32
+
+
+def test_block_backward_matches_oracle_autograd():
+    """Forward + backward of a whole block (config-1 width, shorter sequence): every
+    parameter's gradient and the input gradient against torch autograd through the
+    fp64 oracle block. cuDNN TF32 is switched off so the conv runs in fp32."""
+    prev = torch.backends.cudnn.allow_tf32
+    torch.backends.cudnn.allow_tf32 = False
+    try:
+        torch.manual_seed(0)
+        blk = QuaternionMamba2Block(128, d_state=16, d_conv=4, expand_factor=2)
+        g = gen(3)
+        x = torch.randn(2, 64, 128, generator=g)
+        gout = torch.randn(2, 64, 128, generator=g)
+        params = {k: v.detach().double().requires_grad_() for k, v in blk.state_dict().items()}
+        xr = x.double().requires_grad_()
+        out_ref = ref.block_forward(params, xr, d_state=16)
+        (out_ref * gout.double()).sum().backward()
+        blk = blk.to(DEV)
+        xg = x.to(DEV).requires_grad_()
+        out = blk(xg)
+        (out * gout.to(DEV)).sum().backward()
+        assert rel_l2(out, out_ref.detach()) < RTOL_F32
+        assert rel_l2(xg.grad, xr.grad) < 1e-4
+        for name, p in blk.named_parameters():
+            err = rel_l2(p.grad, params[name].grad)
+            assert err < 1e-4, (name, err)
+    finally:
+        torch.backends.cudnn.allow_tf32 = prev
