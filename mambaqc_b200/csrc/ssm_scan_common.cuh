@@ -205,6 +205,8 @@ inline LaunchShape choose_shape(int B, int T, int D, int N, int NG, int esize, b
 // Warp-specialised kernel for channel-shared B/C without explicit q
 // (ssm_scan_fwd_shared.cu).
 int dispatch_shared(const FwdParams& p, int dtype, bool s_real, cudaStream_t st);
+// Streaming kernel for per-channel B/C and explicit q (ssm_scan_fwd_stream.cu).
+int dispatch_stream(const FwdParams& p, int dtype, bool s_real, bool q_given, cudaStream_t st);
 
 inline int validate_and_fill(const mqc_ssm_scan_args* a, FwdParams* p, const char* name) {
   MQC_REQUIRE(a != nullptr, MQC_ERR_INVALID_VALUE, "%s: null args", name);

@@ -313,8 +313,10 @@ using namespace mqc;
 using namespace mqc::scan;
 
 namespace {
-// MQC_SCAN_IMPL=generic routes channel-shared B/C through the generic kernel
-// (for A/B comparisons); the default is the warp-specialised kernel.
+// MQC_SCAN_IMPL=generic routes every mode through the generic kernel below (for
+// A/B comparisons). By default channel-shared B/C without explicit q take the
+// warp-specialised kernel and per-channel B/C take the streaming kernel; the
+// generic kernel then serves channel-shared B/C with explicit q.
 bool use_generic_kernel() {
   static const bool generic = [] {
     const char* v = getenv("MQC_SCAN_IMPL");
@@ -329,9 +331,13 @@ extern "C" int mqc_ssm_scan_fwd(const mqc_ssm_scan_args* a, void* stream) {
   FwdParams p{};
   int rc = validate_and_fill(a, &p, "mqc_ssm_scan_fwd");
   if (rc != MQC_OK || p.T == 0 || p.B == 0 || p.D == 0) return rc;
-  const bool shared_fused = (a->flags & MQC_SSM_BC_SHARED) && !(a->flags & MQC_SSM_Q_GIVEN);
-  if (shared_fused && !use_generic_kernel())
-    return dispatch_shared(p, a->dtype, (a->flags & MQC_SSM_S_REAL) != 0, as_stream(stream));
+  const bool shared = (a->flags & MQC_SSM_BC_SHARED) != 0;
+  const bool q_given = (a->flags & MQC_SSM_Q_GIVEN) != 0;
+  const bool s_real = (a->flags & MQC_SSM_S_REAL) != 0;
+  if (!use_generic_kernel()) {
+    if (shared && !q_given) return dispatch_shared(p, a->dtype, s_real, as_stream(stream));
+    if (!shared) return dispatch_stream(p, a->dtype, s_real, q_given, as_stream(stream));
+  }
   if (a->dtype == MQC_DTYPE_F32) return dispatch_mode<float>(p, a->flags, as_stream(stream));
   return dispatch_mode<__nv_bfloat16>(p, a->flags, as_stream(stream));
 }
@@ -367,6 +373,7 @@ extern "C" int mqc_ssm_step(const void* q, const void* Bm, const void* S, const 
   FwdParams p{};
   int rc = validate_and_fill(&a, &p, "mqc_ssm_step");
   if (rc != MQC_OK || p.B == 0 || p.D == 0) return rc;
+  if (!use_generic_kernel()) return dispatch_stream(p, dtype, false, true, as_stream(stream));
   if (dtype == MQC_DTYPE_F32) return dispatch_ng<float, false, false, true>(p, as_stream(stream));
   return dispatch_ng<__nv_bfloat16, false, false, true>(p, as_stream(stream));
 }
