@@ -27,7 +27,7 @@ import torch
 
 from .. import _lib
 
-__all__ = ["ssm_step_fused", "ssm_forward_fused", "ssm_scan_cayley"]
+__all__ = ["ssm_step_fused", "ssm_forward_fused", "ssm_scan_cayley", "ssm_scan_cayley_from_host"]
 
 
 def _vec_align(dtype: torch.dtype) -> int:
@@ -52,7 +52,7 @@ def _skip_operand(D: torch.Tensor, bsz: int, seqlen: int, dm: int):
 
 
 def _run_scan(*, flags: int, q=None, delta=None, Lam=None, B, C, S, D, h0=None,
-              return_final_state=False, eps=1e-6, wait_poll_limit=-1, ckpt=None):
+              return_final_state=False, eps=1e-6, wait_poll_limit=-1, ckpt=None, y=None):
     ref = q if q is not None else delta
     dt = ref.dtype
     bsz, seqlen, dm = ref.shape[0], ref.shape[1], ref.shape[2]
@@ -72,7 +72,11 @@ def _run_scan(*, flags: int, q=None, delta=None, Lam=None, B, C, S, D, h0=None,
     Lc = _prep(Lam.float(), 16) if Lam is not None else None
     Df, dsb, dst, dsd = _skip_operand(D, bsz, seqlen, dm)
     h0c = _prep(h0.float(), 16) if h0 is not None else None
-    y = torch.empty(bsz, seqlen, dm, 4, dtype=dt, device=ref.device)
+    if y is None:
+        y = torch.empty(bsz, seqlen, dm, 4, dtype=dt, device=ref.device)
+    else:
+        assert y.is_contiguous() and y.dtype == dt and tuple(y.shape) == (bsz, seqlen, dm, 4)
+        assert y.data_ptr() % va == 0
     hT = (torch.empty(bsz, dm, ds, 4, dtype=torch.float32, device=ref.device)
           if return_final_state else None)
     if shared:
@@ -251,3 +255,69 @@ def ssm_step_fused(q: torch.Tensor, B: torch.Tensor, S: torch.Tensor, C: torch.T
                   Dc.data_ptr(), hp.data_ptr(), h_new.data_ptr(), y.data_ptr(), bsz, dm, ds,
                   _lib.dtype_code(qc), _lib.stream_ptr(q.device))
     return h_new.to(h_prev.dtype), y
+
+
+def ssm_scan_cayley_from_host(delta: torch.Tensor, Lambda: torch.Tensor, B: torch.Tensor,
+                              C: torch.Tensor, S: torch.Tensor, D: torch.Tensor,
+                              device: torch.device | str | None = None,
+                              out: torch.Tensor | None = None, eps: float = 1e-6,
+                              _bufs: dict | None = None) -> torch.Tensor:
+    """``ssm_scan_cayley`` on host (CPU) tensors, pipelined over the batch.
+
+    For inputs that live in host memory: batch row b is copied to the GPU on one
+    stream while row b-1 is scanned on another and row b-2's output is copied
+    back on a third, so the PCIe transfers in both directions overlap the
+    kernels. Pinned host tensors give asynchronous copies (pageable ones work but
+    serialise). Returns y [B,T,D,4] in host memory (``out`` if given, pinned
+    when allocated here). Forward only (no autograd). ``_bufs`` may hold
+    reusable device buffers between calls (a dict the caller keeps).
+    """
+    assert delta.dim() == 3 and S.shape[:3] == delta.shape
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    bsz, seqlen, dm = delta.shape
+    dt = delta.dtype
+    if out is None:
+        out = torch.empty(bsz, seqlen, dm, 4, dtype=dt, pin_memory=True)
+    bufs = _bufs if _bufs is not None else {}
+    with torch.cuda.device(dev):
+        lam_d = Lambda.to(dev, torch.float32, non_blocking=True)
+        d_d = D.to(dev, non_blocking=True)
+        per_row = (delta, B, C, S)
+        if "streams" not in bufs:
+            bufs["streams"] = [torch.cuda.Stream(dev) for _ in range(3)]
+            bufs["slots"] = [[torch.empty(t.shape[1:], dtype=t.dtype, device=dev) for t in per_row]
+                             for _ in range(2)]
+            bufs["y"] = [torch.empty(seqlen, dm, 4, dtype=dt, device=dev) for _ in range(2)]
+        h2d, comp, d2h = bufs["streams"]
+        slots, ybufs = bufs["slots"], bufs["y"]
+        cur = torch.cuda.current_stream(dev)
+        h2d.wait_stream(cur)
+        comp.wait_stream(cur)
+        done_comp = [None, None]
+        done_d2h = [None, None]
+        for b in range(bsz):
+            k = b % 2
+            with torch.cuda.stream(h2d):
+                if done_comp[k] is not None:
+                    h2d.wait_event(done_comp[k])  # slot k free again
+                for dst, src in zip(slots[k], per_row):
+                    dst.copy_(src[b], non_blocking=True)
+                ready = torch.cuda.Event()
+                ready.record(h2d)
+            with torch.cuda.stream(comp):
+                comp.wait_event(ready)
+                if done_d2h[k] is not None:
+                    comp.wait_event(done_d2h[k])  # y buffer k copied out
+                dl, Bb, Cb, Sb = (t.unsqueeze(0) for t in slots[k])
+                _run_scan(flags=0, delta=dl, Lam=lam_d, B=Bb, C=Cb, S=Sb, D=d_d, eps=eps,
+                          y=ybufs[k].unsqueeze(0))
+                done_comp[k] = torch.cuda.Event()
+                done_comp[k].record(comp)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(done_comp[k])
+                out[b].copy_(ybufs[k], non_blocking=True)
+                done_d2h[k] = torch.cuda.Event()
+                done_d2h[k].record(d2h)
+        cur.wait_stream(d2h)
+        cur.wait_stream(comp)
+    return out
