@@ -63,6 +63,9 @@ def parse_args():
                     help="skip the forward+backward and per-channel-layout sub-measurements")
     ap.add_argument("--only", choices=["fwd_bwd", "perchannel"], default=None,
                     help="run only this sub-measurement and print it (profiling aid)")
+    ap.add_argument("--workload", choices=["config3", "config5"], default="config3",
+                    help="config5: B=1, T=65536, D=1536, N=64, bf16, channel-sharded over the "
+                         "GPUs with an NCCL all-gather of y (strong scaling)")
     return ap.parse_args()
 
 
@@ -77,7 +80,8 @@ def dist_setup(args):
         if backend == "nccl":
             torch.cuda.set_device(local)
         import datetime
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
+        kw = {"device_id": torch.device(f"cuda:{local}")} if backend == "nccl" else {}
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300), **kw)
     return world, rank, local
 
 
@@ -465,12 +469,84 @@ def run_perchannel(args, dev, world, stream, op, peaks):
     return res
 
 
+C5_SEQ = 65536
+
+
+def run_config5(args, world, rank, local):
+    """Long-sequence single-block scan forward, channel-sharded: every rank holds
+    D/world channels of delta/x/Lambda/D and the shared B/C, scans them
+    time-parallel, and one NCCL all-gather assembles y [1, T, D, 4] on every rank.
+    One step = local scan + all-gather + reassembly; max over ranks."""
+    from mambaqc_b200.kernels import ssm_scan_cayley
+    from mambaqc_b200.kernels.sharded import ssm_scan_cayley_channel_sharded
+    from mambaqc_b200.kernels.ssm_fused import auto_time_chunks
+
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    if CHANNELS % world:
+        raise SystemExit(f"{CHANNELS} channels do not split over {world} GPUs")
+    dl = CHANNELS // world
+    g = torch.Generator(device=dev).manual_seed(77)  # same B/C on every rank
+    bf = torch.bfloat16
+    Bm = (torch.randn(1, C5_SEQ, STATE, 4, generator=g, device=dev) / math.sqrt(STATE)).to(bf)
+    Cm = (torch.randn(1, C5_SEQ, STATE, 4, generator=g, device=dev) / math.sqrt(STATE)).to(bf)
+    g.manual_seed(1000 + rank)  # this rank's channels
+    x = torch.randn(1, C5_SEQ, dl, generator=g, device=dev).to(bf)
+    delta = torch.nn.functional.softplus(
+        torch.randn(1, C5_SEQ, dl, generator=g, device=dev) - 3.0).to(bf)
+    lam = torch.empty(dl, STATE, 4, device=dev)
+    u = torch.rand(dl, STATE, generator=g, device=dev)
+    lam[..., 0] = -torch.exp(u * (math.log(1e-1) - math.log(1e-3)) + math.log(1e-3))
+    lam[..., 1:] = 0.5 * torch.randn(dl, STATE, 3, generator=g, device=dev)
+    Dk = torch.ones(dl, device=dev)
+    nc = auto_time_chunks(1, C5_SEQ, dl, STATE, dev)
+    stream = torch.cuda.current_stream(dev)
+    out = {}
+
+    def step():
+        out["y"] = ssm_scan_cayley_channel_sharded(delta, lam, Bm, Cm, x, Dk, time_chunks=nc)
+
+    def scan_only():
+        out["yl"] = ssm_scan_cayley(delta, lam, Bm, Cm, x, Dk, time_chunks=nc)
+
+    with torch.no_grad():
+        step()
+        torch.cuda.synchronize()
+        assert out["y"].shape == (1, C5_SEQ, CHANNELS, 4)
+        steps = max(3, min(args.steps, 20))
+        ms = timed(step, steps, max(3, args.warmup), world, stream) / steps
+        ms_max = max_over_ranks(ms, world, dev)
+        ms_scan = timed(scan_only, steps, 3, world, stream) / steps
+        ms_scan_max = max_over_ranks(ms_scan, world, dev)
+    elems = C5_SEQ * CHANNELS * STATE
+    if rank == 0:
+        line = {
+            "metric": "config5 long-sequence scan forward tokens/s (B=1, T=65536, D=1536, N=64, "
+                      "channel-sharded, y all-gathered)",
+            "value": C5_SEQ / (ms_max / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": steps, "warmup": max(3, args.warmup), "ms_per_step": ms_max,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16 inputs, f32 state", "data": "synthetic (seeded, config-3 distributions)",
+            "config": {"workload": "config5_channel_sharded", "batch": 1, "seq_len": C5_SEQ,
+                       "d_inner": CHANNELS, "d_state": STATE, "channels_per_gpu": dl,
+                       "time_chunks": nc, "parallelism": f"channel shards x{world}, "
+                                                         "NCCL all_gather_into_tensor of y"},
+            "scan_only_ms": ms_scan_max,
+            "gather_and_reassembly_ms": ms_max - ms_scan_max,
+            "scan_fp32_tflops_per_gpu": elems / world * FLOPS_PER_ELEM_SREAL / (ms_scan_max / 1e3) / 1e12,
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse_args()
     world, rank, local = dist_setup(args)
     try:
         if args.impl == "reference":
             return run_reference(args, world, rank)
+        if args.workload == "config5":
+            return run_config5(args, world, rank, local)
         return run_b200(args, world, rank, local)
     finally:
         if dist.is_initialized():

@@ -171,6 +171,22 @@ typedef struct mqc_ssm_scan_args {
  * that never materialises z or q. */
 MQC_API int mqc_ssm_scan_fwd(const mqc_ssm_scan_args* args, void* stream);
 
+/* Time-parallel form of mqc_ssm_scan_fwd (fused Cayley, no Q_GIVEN, no
+ * checkpoints) for long sequences with few channels: T is cut into nchunks equal
+ * chunks (seq_len % nchunks == 0); every chunk is scanned from zero for its end
+ * state and operator product, the chunks are chained on the device, and every
+ * chunk is rescanned from its true start state. Same outputs as
+ * mqc_ssm_scan_fwd (y, optional hT; h0 honoured). The skip weight must be per
+ * channel (dskip_sb = dskip_st = 0). `workspace` (16-byte aligned, caller-owned)
+ * must hold mqc_ssm_scan_fwd_chunked_workspace_size(...) bytes. The reference's
+ * only time-parallel primitive is parallel_scan_quaternion (parallel_scan.py:171),
+ * which the model never calls; this is the scan of ssm_forward_fused
+ * (ssm_fused.py:340-401) made time-parallel. */
+MQC_API size_t mqc_ssm_scan_fwd_chunked_workspace_size(int64_t batch, int64_t channels,
+                                                       int64_t d_state, int64_t nchunks);
+MQC_API int mqc_ssm_scan_fwd_chunked(const mqc_ssm_scan_args* args, int64_t nchunks,
+                                     void* workspace, size_t workspace_bytes, void* stream);
+
 /*
  * Backward of mqc_ssm_scan_fwd without Q_GIVEN (the fused Cayley form). The
  * reference has no GPU backward (its Triton kernels are not differentiable);

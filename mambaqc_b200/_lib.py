@@ -81,6 +81,8 @@ _SIGNATURES = {
     "mqc_prefix_prod_noalloc": [_c_void_p, _c_void_p, _i64, _i64, _i64, _i32, _c_void_p],
     "mqc_ssm_scan_fwd": [ctypes.POINTER(SsmScanArgs), _c_void_p],
     "mqc_ssm_scan_bwd": [ctypes.POINTER(SsmScanBwdArgs), _c_void_p],
+    "mqc_ssm_scan_fwd_chunked": [ctypes.POINTER(SsmScanArgs), _i64, _c_void_p, ctypes.c_size_t,
+                                 _c_void_p],
     "mqc_ssm_step": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                      _c_void_p, _c_void_p, _i64, _i64, _i64, _i32, _c_void_p],
     "mqc_qln_fwd": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
@@ -90,7 +92,8 @@ _SIGNATURES = {
                     _c_void_p],
 }
 _SIGNATURES["mqc_probe_fp32_fma"] = [_c_void_p, _i64, ctypes.POINTER(_i64), _c_void_p]
-_SIZE_FUNCS = {"mqc_qln_bwd_workspace_size": [_i64, _i64]}
+_SIZE_FUNCS = {"mqc_qln_bwd_workspace_size": [_i64, _i64],
+               "mqc_ssm_scan_fwd_chunked_workspace_size": [_i64, _i64, _i64, _i64]}
 _STR_FUNCS = {"mqc_version": [], "mqc_status_string": [_i32], "mqc_last_error": []}
 
 _lock = threading.Lock()

@@ -1,0 +1,117 @@
+// Time-chunked (time-parallel) selective scan forward.
+//
+// For long sequences with few (b, d, n) lanes -- one channel shard of a long
+// sequence per GPU -- the sequential scan cannot fill the GPU. The scan
+// h_t = q_t (x) h_{t-1} + u_t is affine in h, and affine maps compose in order
+// (later (x) earlier): over a chunk of steps it is h -> P (x) h + h_loc with
+// P = q_last (x) ... (x) q_first and h_loc the chunk's final state from h = 0.
+// So with T cut into nc equal chunks (the chunk index folded into the batch:
+// [B, T, ...] is viewed as [B*nc, T/nc, ...], no copies):
+//   pass 1  state-only scan of every chunk from zero -> (P_c, h_loc_c)
+//   carry   H_{-1} = h0, H_c = P_c (x) H_{c-1} + h_loc_c   (sequential over c, per lane)
+//   pass 2  the regular fused scan of every chunk from H_{c-1} -> y
+// Pass 2 is the same kernel as the unchunked scan; the extra work is pass 1
+// (a scan without readout) and the carry (3 x 16 B per chunk and lane).
+#include "ssm_scan_common.cuh"
+
+namespace mqc {
+namespace scan {
+namespace {
+
+constexpr int kCarryThreads = 256;
+
+// grid (ceil(lanes / 256), batch); P, hloc, hin: [batch, nc, lanes, 4]; h0, hT: [batch, lanes, 4]
+__global__ void __launch_bounds__(kCarryThreads)
+    chunk_carry_kernel(const float* __restrict__ P, const float* __restrict__ hloc,
+                       const float* __restrict__ h0, float* __restrict__ hin,
+                       float* __restrict__ hT, int nc, int64_t lanes) {
+  const int64_t l = int64_t(blockIdx.x) * kCarryThreads + threadIdx.x;
+  if (l >= lanes) return;
+  const int64_t b = blockIdx.y;
+  float4 H = h0 != nullptr ? QIO<float>::ld(h0 + (b * lanes + l) * 4) : f4_zero();
+  for (int c = 0; c < nc; ++c) {
+    const int64_t idx = ((b * nc + c) * lanes + l) * 4;
+    QIO<float>::st(hin + idx, H);
+    H = qmul_acc(QIO<float>::ld(P + idx), H, QIO<float>::ld(hloc + idx));
+  }
+  if (hT != nullptr) QIO<float>::st(hT + (b * lanes + l) * 4, H);
+}
+
+size_t chunked_workspace(int64_t batch, int64_t nchunks, int64_t lanes) {
+  return size_t(3) * size_t(batch) * size_t(nchunks) * size_t(lanes) * 16;
+}
+
+}  // namespace
+}  // namespace scan
+}  // namespace mqc
+
+using namespace mqc;
+using namespace mqc::scan;
+
+extern "C" size_t mqc_ssm_scan_fwd_chunked_workspace_size(int64_t batch, int64_t channels,
+                                                          int64_t d_state, int64_t nchunks) {
+  if (batch <= 0 || channels <= 0 || d_state <= 0 || nchunks <= 0) return 0;
+  return chunked_workspace(batch, nchunks, channels * d_state);
+}
+
+extern "C" int mqc_ssm_scan_fwd_chunked(const mqc_ssm_scan_args* a, int64_t nchunks,
+                                        void* workspace, size_t workspace_bytes,
+                                        void* stream) {
+  clear_error();
+  const char* name = "mqc_ssm_scan_fwd_chunked";
+  MQC_REQUIRE(a != nullptr, MQC_ERR_INVALID_VALUE, "%s: null args", name);
+  MQC_REQUIRE(!(a->flags & MQC_SSM_Q_GIVEN), MQC_ERR_UNSUPPORTED,
+              "%s: explicit q is not supported (use the fused form)", name);
+  MQC_REQUIRE(a->ckpt == nullptr, MQC_ERR_UNSUPPORTED, "%s: no checkpoints (forward only)", name);
+  MQC_REQUIRE(nchunks >= 1, MQC_ERR_INVALID_VALUE, "%s: nchunks must be >= 1", name);
+  FwdParams p{};
+  int rc = validate_and_fill(a, &p, name);
+  if (rc != MQC_OK || p.T == 0 || p.B == 0 || p.D == 0) return rc;
+  if (nchunks == 1) return mqc_ssm_scan_fwd(a, stream);
+  MQC_REQUIRE(p.T % nchunks == 0, MQC_ERR_INVALID_VALUE, "%s: seq_len %d not divisible by %lld",
+              name, p.T, (long long)nchunks);
+  // chunks are folded into the batch, so the skip weight may vary over channels only
+  MQC_REQUIRE(a->dskip_sb == 0 && a->dskip_st == 0, MQC_ERR_UNSUPPORTED,
+              "%s: the skip weight must be per channel ([D], strides 0 over batch and time)", name);
+  MQC_REQUIRE(int64_t(p.B) * nchunks <= 65535, MQC_ERR_UNSUPPORTED,
+              "%s: batch * nchunks must be <= 65535", name);
+  const int64_t lanes = int64_t(p.D) * p.N;
+  const size_t need = chunked_workspace(p.B, nchunks, lanes);
+  MQC_REQUIRE(workspace != nullptr && workspace_bytes >= need && aligned(workspace, 16),
+              MQC_ERR_INVALID_VALUE, "%s: 16-byte aligned workspace of %zu bytes required", name,
+              need);
+  float* Pbuf = static_cast<float*>(workspace);
+  float* hloc = Pbuf + size_t(p.B) * nchunks * lanes * 4;
+  float* hin = hloc + size_t(p.B) * nchunks * lanes * 4;
+  cudaStream_t st = as_stream(stream);
+  const bool s_real = a->flags & MQC_SSM_S_REAL;
+  const bool shared = a->flags & MQC_SSM_BC_SHARED;
+
+  // pass 1: state-only scan of each chunk from zero, chunks folded into the batch
+  FwdParams p1 = p;
+  p1.B = int(int64_t(p.B) * nchunks);
+  p1.T = int(p.T / nchunks);
+  p1.h0 = nullptr;
+  p1.hT = hloc;
+  p1.pout = Pbuf;
+  p1.y = nullptr;
+  p1.ckpt = nullptr;
+  p1.nck = 0;
+  rc = dispatch_state_only(p1, a->dtype, s_real, shared, st);
+  if (rc != MQC_OK) return rc;
+
+  // carry: start state of every chunk, and the final state
+  dim3 grid{unsigned((lanes + kCarryThreads - 1) / kCarryThreads), unsigned(p.B), 1u};
+  chunk_carry_kernel<<<grid, kCarryThreads, 0, st>>>(Pbuf, hloc, p.h0, hin, p.hT, int(nchunks),
+                                                     lanes);
+  rc = check_launch("mqc_ssm_scan_fwd_chunked(carry)");
+  if (rc != MQC_OK) return rc;
+
+  // pass 2: the regular scan of every chunk from its start state
+  mqc_ssm_scan_args a2 = *a;
+  a2.batch = int64_t(p.B) * nchunks;
+  a2.seq_len = p.T / nchunks;
+  a2.h0 = hin;
+  a2.hT = nullptr;
+  return mqc_ssm_scan_fwd(&a2, stream);
+}

@@ -32,6 +32,7 @@ struct FwdParams {
   float* hT;
   int* status;
   long long wait_limit;
+  float* pout;     // [B, D, N, 4] operator product (state-only pass) or nullptr
   float* ckpt;     // [B, nck, D, N, 4] or nullptr
   int ckpt_every;  // K: checkpoint after steps K-1, 2K-1, ... < T-1
   int nck;         // number of checkpoints = ceil(T / K) - 1
@@ -207,6 +208,9 @@ inline LaunchShape choose_shape(int B, int T, int D, int N, int NG, int esize, b
 int dispatch_shared(const FwdParams& p, int dtype, bool s_real, cudaStream_t st);
 // Streaming kernel for per-channel B/C and explicit q (ssm_scan_fwd_stream.cu).
 int dispatch_stream(const FwdParams& p, int dtype, bool s_real, bool q_given, cudaStream_t st);
+// Pass 1 of the time-chunked scan: final state + operator product, no readout.
+int dispatch_state_only(const FwdParams& p, int dtype, bool s_real, bool bc_shared,
+                        cudaStream_t st);
 
 inline int validate_and_fill(const mqc_ssm_scan_args* a, FwdParams* p, const char* name) {
   MQC_REQUIRE(a != nullptr, MQC_ERR_INVALID_VALUE, "%s: null args", name);

@@ -20,7 +20,12 @@ namespace scan {
 
 constexpr int kStreamThreads = 256;
 
-template <typename T, int G, int NG, bool S_REAL, bool Q_GIVEN>
+// BC_SHARED: B/C are [B,T,N,4] (stride 0 over channels) instead of [B,T,D,N,4].
+// STATE_ONLY: no readout; the kernel returns the final state (p.hT) and the
+// product of the step operators P = q_{T-1} (x) ... (x) q_0 (p.pout) -- pass 1
+// of the time-chunked scan.
+template <typename T, int G, int NG, bool S_REAL, bool Q_GIVEN, bool BC_SHARED = false,
+          bool STATE_ONLY = false>
 __global__ void __launch_bounds__(kStreamThreads)
     scan_fwd_stream_kernel(const FwdParams p) {
   constexpr int CPW = 32 / NG;
@@ -61,6 +66,11 @@ __global__ void __launch_bounds__(kStreamThreads)
   const int64_t q_stride = int64_t(D) * N * 4;             // [B,T,D,N,4] per step
   const int64_t row0 = int64_t(b) * T_ * D + c;            // (b, 0, c)
   const int64_t e0 = (int64_t(b) * T_ * D + c) * N * 4 + int64_t(ng) * 4;  // (b, 0, c, ng)
+  const int64_t bc_stride = BC_SHARED ? int64_t(N) * 4 : q_stride;
+  const int64_t bc0 = BC_SHARED ? int64_t(b) * T_ * N * 4 + int64_t(ng) * 4 : e0;
+  float4 P[STATE_ONLY ? G : 1];
+#pragma unroll
+  for (int i = 0; i < (STATE_ONLY ? G : 1); ++i) P[i] = make_float4(1.f, 0.f, 0.f, 0.f);
 
   struct Step {
     float dl;
@@ -70,6 +80,7 @@ __global__ void __launch_bounds__(kStreamThreads)
   auto load_step = [&](int t, Step& s) {
     const int64_t row = row0 + int64_t(t) * row_stride;
     const int64_t e = e0 + int64_t(t) * q_stride;
+    const int64_t ebc = bc0 + int64_t(t) * bc_stride;
     s.dl = (!Q_GIVEN && active) ? to_f(gdelta[row]) : 0.f;
     s.sv = f4_zero();
     if (active) {
@@ -81,8 +92,13 @@ __global__ void __launch_bounds__(kStreamThreads)
       s.Bv[i] = s.Cv[i] = f4_zero();
       s.qv[i] = make_float4(1.f, 0.f, 0.f, 0.f);
       if (nok[i]) {
-        s.Bv[i] = QIO<T>::ld_stream(gB + e + NG * i * 4);
-        s.Cv[i] = QIO<T>::ld_stream(gC + e + NG * i * 4);
+        if (BC_SHARED) {
+          s.Bv[i] = QIO<T>::ld(gB + ebc + NG * i * 4);
+          if (!STATE_ONLY) s.Cv[i] = QIO<T>::ld(gC + ebc + NG * i * 4);
+        } else {
+          s.Bv[i] = QIO<T>::ld_stream(gB + ebc + NG * i * 4);
+          if (!STATE_ONLY) s.Cv[i] = QIO<T>::ld_stream(gC + ebc + NG * i * 4);
+        }
         if (Q_GIVEN) s.qv[i] = QIO<T>::ld_stream(gq + e + NG * i * 4);
       }
     }
@@ -107,8 +123,16 @@ __global__ void __launch_bounds__(kStreamThreads)
       if (S_REAL) inj = make_float4(sv.x * Bv.x, sv.x * Bv.y, sv.x * Bv.z, sv.x * Bv.w);
       else inj = qmul(Bv, sv);
       h[i] = qmul_acc(qv, h[i], inj);
-      if (i & 1) yb2 = qmul_acc(cur.Cv[i], h[i], yb2);
-      else ya = qmul_acc(cur.Cv[i], h[i], ya);
+      if constexpr (STATE_ONLY) {
+        P[i] = qmul(qv, P[i]);
+      } else {
+        if (i & 1) yb2 = qmul_acc(cur.Cv[i], h[i], yb2);
+        else ya = qmul_acc(cur.Cv[i], h[i], ya);
+      }
+    }
+    if constexpr (STATE_ONLY) {
+      cur = nxt;
+      continue;
     }
     ya.x += yb2.x;
     ya.y += yb2.y;
@@ -132,17 +156,25 @@ __global__ void __launch_bounds__(kStreamThreads)
       if (nok[i]) QIO<float>::st(p.hT + ((int64_t(b) * D + c) * N + n) * 4, h[i]);
     }
   }
+  if constexpr (STATE_ONLY) {
+#pragma unroll
+    for (int i = 0; i < G; ++i) {
+      const int n = ng + NG * i;
+      if (nok[i]) QIO<float>::st(p.pout + ((int64_t(b) * D + c) * N + n) * 4, P[i]);
+    }
+  }
 }
 
-template <typename T, int G, int NG, bool S_REAL, bool Q_GIVEN>
+template <typename T, int G, int NG, bool S_REAL, bool Q_GIVEN, bool BC_SHARED, bool STATE_ONLY>
 int launch_stream(const FwdParams& p, cudaStream_t st) {
   constexpr int CPB = kStreamThreads / 32 * (32 / NG);
   dim3 grid{unsigned((p.D + CPB - 1) / CPB), unsigned(p.B), 1u};
-  scan_fwd_stream_kernel<T, G, NG, S_REAL, Q_GIVEN><<<grid, kStreamThreads, 0, st>>>(p);
+  scan_fwd_stream_kernel<T, G, NG, S_REAL, Q_GIVEN, BC_SHARED, STATE_ONLY>
+      <<<grid, kStreamThreads, 0, st>>>(p);
   return check_launch("mqc_ssm_scan_fwd(stream)");
 }
 
-template <typename T, bool S_REAL, bool Q_GIVEN>
+template <typename T, bool S_REAL, bool Q_GIVEN, bool BC_SHARED, bool STATE_ONLY>
 int dispatch_stream_t(const FwdParams& p, cudaStream_t st) {
   // G = 2 states per lane up to N = 64 (NG = next power of two of N/2), then G = 4 / 8
   if (p.N <= 64) {
@@ -150,31 +182,47 @@ int dispatch_stream_t(const FwdParams& p, cudaStream_t st) {
     int ng = 1;
     while (ng < need) ng <<= 1;
     switch (ng) {
-      case 1: return launch_stream<T, 2, 1, S_REAL, Q_GIVEN>(p, st);
-      case 2: return launch_stream<T, 2, 2, S_REAL, Q_GIVEN>(p, st);
-      case 4: return launch_stream<T, 2, 4, S_REAL, Q_GIVEN>(p, st);
-      case 8: return launch_stream<T, 2, 8, S_REAL, Q_GIVEN>(p, st);
-      case 16: return launch_stream<T, 2, 16, S_REAL, Q_GIVEN>(p, st);
-      default: return launch_stream<T, 2, 32, S_REAL, Q_GIVEN>(p, st);
+      case 1: return launch_stream<T, 2, 1, S_REAL, Q_GIVEN, BC_SHARED, STATE_ONLY>(p, st);
+      case 2: return launch_stream<T, 2, 2, S_REAL, Q_GIVEN, BC_SHARED, STATE_ONLY>(p, st);
+      case 4: return launch_stream<T, 2, 4, S_REAL, Q_GIVEN, BC_SHARED, STATE_ONLY>(p, st);
+      case 8: return launch_stream<T, 2, 8, S_REAL, Q_GIVEN, BC_SHARED, STATE_ONLY>(p, st);
+      case 16: return launch_stream<T, 2, 16, S_REAL, Q_GIVEN, BC_SHARED, STATE_ONLY>(p, st);
+      default: return launch_stream<T, 2, 32, S_REAL, Q_GIVEN, BC_SHARED, STATE_ONLY>(p, st);
     }
   }
-  if (p.N <= 128) return launch_stream<T, 4, 32, S_REAL, Q_GIVEN>(p, st);
-  return launch_stream<T, 8, 32, S_REAL, Q_GIVEN>(p, st);
+  if (p.N <= 128) return launch_stream<T, 4, 32, S_REAL, Q_GIVEN, BC_SHARED, STATE_ONLY>(p, st);
+  return launch_stream<T, 8, 32, S_REAL, Q_GIVEN, BC_SHARED, STATE_ONLY>(p, st);
 }
 
 int dispatch_stream(const FwdParams& p, int dtype, bool s_real, bool q_given, cudaStream_t st) {
   if (dtype == MQC_DTYPE_F32) {
     if (q_given)
-      return s_real ? dispatch_stream_t<float, true, true>(p, st)
-                    : dispatch_stream_t<float, false, true>(p, st);
-    return s_real ? dispatch_stream_t<float, true, false>(p, st)
-                  : dispatch_stream_t<float, false, false>(p, st);
+      return s_real ? dispatch_stream_t<float, true, true, false, false>(p, st)
+                    : dispatch_stream_t<float, false, true, false, false>(p, st);
+    return s_real ? dispatch_stream_t<float, true, false, false, false>(p, st)
+                  : dispatch_stream_t<float, false, false, false, false>(p, st);
   }
   if (q_given)
-    return s_real ? dispatch_stream_t<__nv_bfloat16, true, true>(p, st)
-                  : dispatch_stream_t<__nv_bfloat16, false, true>(p, st);
-  return s_real ? dispatch_stream_t<__nv_bfloat16, true, false>(p, st)
-                : dispatch_stream_t<__nv_bfloat16, false, false>(p, st);
+    return s_real ? dispatch_stream_t<__nv_bfloat16, true, true, false, false>(p, st)
+                  : dispatch_stream_t<__nv_bfloat16, false, true, false, false>(p, st);
+  return s_real ? dispatch_stream_t<__nv_bfloat16, true, false, false, false>(p, st)
+                : dispatch_stream_t<__nv_bfloat16, false, false, false, false>(p, st);
+}
+
+int dispatch_state_only(const FwdParams& p, int dtype, bool s_real, bool bc_shared,
+                        cudaStream_t st) {
+  if (dtype == MQC_DTYPE_F32) {
+    if (bc_shared)
+      return s_real ? dispatch_stream_t<float, true, false, true, true>(p, st)
+                    : dispatch_stream_t<float, false, false, true, true>(p, st);
+    return s_real ? dispatch_stream_t<float, true, false, false, true>(p, st)
+                  : dispatch_stream_t<float, false, false, false, true>(p, st);
+  }
+  if (bc_shared)
+    return s_real ? dispatch_stream_t<__nv_bfloat16, true, false, true, true>(p, st)
+                  : dispatch_stream_t<__nv_bfloat16, false, false, true, true>(p, st);
+  return s_real ? dispatch_stream_t<__nv_bfloat16, true, false, false, true>(p, st)
+                : dispatch_stream_t<__nv_bfloat16, false, false, false, true>(p, st);
 }
 
 }  // namespace scan

@@ -188,10 +188,67 @@ class _SsmScanCayley(torch.autograd.Function):
                 _sum_to(dD_full, D), None if dh0 is None else dh0.to(h0_dtype), None, None)
 
 
+def auto_time_chunks(bsz: int, seqlen: int, channels: int, d_state: int,
+                     device: torch.device | None = None) -> int:
+    """Number of time chunks that lets a forward scan fill the GPU.
+
+    1 when batch * channels * d_state state lanes already cover ~2048 lanes per
+    SM (config 3 has 393K lanes on 148 SMs); otherwise the smallest power of two
+    that does, keeping >= 256 steps per chunk and dividing seq_len.
+    """
+    props = torch.cuda.get_device_properties(device if device is not None else
+                                             torch.cuda.current_device())
+    target = props.multi_processor_count * 2048
+    lanes = bsz * channels * d_state
+    nc = 1
+    while lanes * nc < target and seqlen % (2 * nc) == 0 and seqlen // (2 * nc) >= 256:
+        nc *= 2
+    return nc
+
+
+def _run_scan_chunked(delta, Lam, B, C, S, D, h0, eps, nchunks, return_final_state):
+    """Time-parallel forward (``mqc_ssm_scan_fwd_chunked``); no autograd."""
+    dt = delta.dtype
+    bsz, seqlen, dm = delta.shape
+    ds = Lam.shape[1]
+    shared = B.dim() == 4
+    va = _vec_align(dt)
+    dc = _prep(delta, 4)
+    Lc = _prep(Lam.float(), 16)
+    Bc = _prep(B, 16 if shared else va)
+    Cc = _prep(C, 16 if shared else va)
+    Sc = _prep(S, va)
+    Df, dsb, dst, dsd = _skip_operand(D, bsz, seqlen, dm)
+    if dsb != 0 or dst != 0:
+        raise ValueError("time-chunked scan needs a per-channel skip weight D [D]")
+    h0c = _prep(h0.float(), 16) if h0 is not None else None
+    y = torch.empty(bsz, seqlen, dm, 4, dtype=dt, device=delta.device)
+    hT = (torch.empty(bsz, dm, ds, 4, dtype=torch.float32, device=delta.device)
+          if return_final_state else None)
+    lib = _lib.load()
+    ws_bytes = lib.mqc_ssm_scan_fwd_chunked_workspace_size(bsz, dm, ds, nchunks)
+    ws = torch.empty(max(1, ws_bytes // 4), dtype=torch.float32, device=delta.device)
+    flags = (_lib.MQC_SSM_BC_SHARED if shared else 0) | (_lib.MQC_SSM_S_REAL if S.dim() == 3 else 0)
+    status = _lib.status_word(delta.device)
+    a = _lib.SsmScanArgs(
+        batch=bsz, seq_len=seqlen, channels=dm, d_state=ds, dtype=_lib.dtype_code(dc),
+        flags=flags, eps=float(eps), reserved0=0, delta=dc.data_ptr(), lambda_=Lc.data_ptr(),
+        q=None, Bm=Bc.data_ptr(), Cm=Cc.data_ptr(), s=Sc.data_ptr(), dskip=Df.data_ptr(),
+        dskip_sb=0, dskip_st=0, dskip_sd=dsd, h0=_lib.ptr(h0c), y=y.data_ptr(),
+        hT=_lib.ptr(hT), status=status.data_ptr(), wait_poll_limit=-1, ckpt=None, ckpt_every=0)
+    with torch.cuda.device(delta.device):
+        _lib.call("mqc_ssm_scan_fwd_chunked", ctypes.byref(a), int(nchunks), ws.data_ptr(),
+                  ws_bytes, _lib.stream_ptr(delta.device))
+    if _lib.sync_checks_enabled():
+        _lib.check_device_status(delta.device)
+    return y, hT
+
+
 def ssm_scan_cayley(delta: torch.Tensor, Lambda: torch.Tensor, B: torch.Tensor,
                     C: torch.Tensor, S: torch.Tensor, D: torch.Tensor,
                     h0: torch.Tensor | None = None, eps: float = 1e-6,
-                    return_final_state: bool = False, wait_poll_limit: int = -1):
+                    return_final_state: bool = False, wait_poll_limit: int = -1,
+                    time_chunks: int | str = "auto"):
     """Fused Cayley + quaternion selective scan (differentiable).
 
     delta [B,T,D] (positive step sizes), Lambda [D,N,4] (fp32 continuous
@@ -204,6 +261,10 @@ def ssm_scan_cayley(delta: torch.Tensor, Lambda: torch.Tensor, B: torch.Tensor,
     h_T [B,D,N,4] when ``return_final_state``. Gradients flow to every tensor
     argument through ``mqc_ssm_scan_bwd`` (states recomputed from checkpoints
     the forward writes every 8 steps when a gradient is needed).
+
+    ``time_chunks``: when no gradient is needed, a long sequence with few
+    channels is scanned time-parallel in that many chunks (``"auto"``: enough to
+    fill the GPU, see ``auto_time_chunks``; 1 disables it).
     """
     assert delta.dim() == 3, f"delta must be [B,T,D], got {tuple(delta.shape)}"
     assert Lambda.dim() == 3 and Lambda.shape[-1] == 4, "Lambda must be [D,N,4]"
@@ -216,6 +277,14 @@ def ssm_scan_cayley(delta: torch.Tensor, Lambda: torch.Tensor, B: torch.Tensor,
         assert tuple(B.shape) == (bsz, seqlen, dm, ds, 4) and B.shape == C.shape
     assert tuple(S.shape) in ((bsz, seqlen, dm), (bsz, seqlen, dm, 4))
     _lib.require_cuda(delta, Lambda, B, C, S, D, h0, what="ssm_scan_cayley")
+    needs_grad = torch.is_grad_enabled() and any(
+        t is not None and t.requires_grad for t in (delta, Lambda, B, C, S, D, h0))
+    if not needs_grad and D.dim() == 1 and wait_poll_limit < 0:
+        nc = (auto_time_chunks(bsz, seqlen, dm, ds, delta.device) if time_chunks == "auto"
+              else int(time_chunks))
+        if nc > 1:
+            y, hT = _run_scan_chunked(delta, Lambda, B, C, S, D, h0, eps, nc, return_final_state)
+            return (y, hT) if return_final_state else y
     y, hT = _SsmScanCayley.apply(delta, Lambda, B, C, S, D, h0, eps, wait_poll_limit)
     return (y, hT) if return_final_state else y
 

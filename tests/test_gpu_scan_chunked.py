@@ -1,0 +1,66 @@
+"""Time-chunked (time-parallel) scan forward vs the sequential GPU scan and the
+fp64 oracle: pass 1 (chunk end state + operator product), the on-device carry
+and pass 2 must reproduce the sequential recurrence."""
+
+import pytest
+import torch
+
+from oracle import ref
+from tests.gpu_util import DEV, RTOL_BF16, RTOL_F32, gen, make_scan_inputs, rel_l2, to_dev
+
+pytestmark = pytest.mark.gpu
+
+from mambaqc_b200.kernels import ssm_scan_cayley  # noqa: E402
+from mambaqc_b200.kernels.ssm_fused import auto_time_chunks  # noqa: E402
+
+
+def run(inp, dtype, nc, h0=None):
+    d = to_dev(inp, dtype)
+    with torch.no_grad():
+        y, hT = ssm_scan_cayley(d["delta"], d["Lambda"], d["B"], d["C"], d["S"], d["D"],
+                                h0=None if h0 is None else h0.to(DEV, torch.float32),
+                                return_final_state=True, time_chunks=nc)
+    torch.cuda.synchronize()
+    return y, hT
+
+
+@pytest.mark.parametrize("shared,s_real", [(True, True), (False, True), (True, False)])
+def test_chunked_matches_oracle(shared, s_real):
+    inp = make_scan_inputs(1, 1024, 4, 16, shared=shared, s_real=s_real, seed=3)
+    h0 = torch.randn(1, 4, 16, 4, generator=gen(4), dtype=torch.float64)
+    y_ref, h_ref = ref.ssm_scan_cayley(*(inp[k] for k in ("delta", "Lambda", "B", "C", "S", "D")),
+                                       h0=h0)
+    for nc in (2, 4, 8):
+        y, hT = run(inp, torch.float32, nc, h0=h0)
+        assert rel_l2(y, y_ref) < RTOL_F32, nc
+        assert rel_l2(hT, h_ref) < RTOL_F32, nc
+
+
+@pytest.mark.parametrize("shape", [(1, 4096, 12, 64), (2, 2048, 5, 16), (1, 1024, 3, 100)])
+def test_chunked_matches_sequential_gpu_scan(shape):
+    bsz, seqlen, dm, ds = shape
+    inp = make_scan_inputs(bsz, seqlen, dm, ds, shared=True, s_real=True, seed=sum(shape))
+    y1, h1 = run(inp, torch.float32, 1)
+    for nc in (2, 16, 32):
+        y, hT = run(inp, torch.float32, nc)
+        # both are fp32 evaluations of the same recurrence in different orders
+        assert rel_l2(y, y1) < RTOL_F32, nc
+        assert rel_l2(hT, h1) < RTOL_F32, nc
+
+
+def test_chunked_bf16_config5_like():
+    """bf16 inputs, fp32 state, a narrow channel shard of a long sequence."""
+    inp = make_scan_inputs(1, 8192, 8, 64, shared=True, s_real=True, seed=11)
+    y1, _ = run(inp, torch.float32, 1)
+    nc = auto_time_chunks(1, 8192, 8, 64)
+    assert nc > 1
+    yb, _ = run(inp, torch.bfloat16, "auto")
+    assert yb.dtype == torch.bfloat16
+    assert rel_l2(yb, y1) < RTOL_BF16
+
+
+def test_auto_chunks_policy():
+    assert auto_time_chunks(4, 2048, 1536, 64) == 1          # config 3 fills the GPU
+    assert auto_time_chunks(1, 65536, 1536, 64) >= 2          # config 5 on one GPU
+    assert auto_time_chunks(1, 65536, 192, 64) >= 16          # config 5 shard of 8 GPUs
+    assert auto_time_chunks(1, 300, 4, 16) == 1               # too short to split
