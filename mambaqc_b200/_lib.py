@@ -14,7 +14,9 @@ from pathlib import Path
 
 import torch
 
-LIB_PATH = Path(__file__).resolve().parent / "libmambaqc_b200.so"
+# MAMBAQC_B200_LIBRARY points at another build of the same library (to compare builds).
+LIB_PATH = Path(os.environ.get("MAMBAQC_B200_LIBRARY")
+                or Path(__file__).resolve().parent / "libmambaqc_b200.so")
 
 MQC_DTYPE_F32 = 0
 MQC_DTYPE_BF16 = 1

@@ -169,7 +169,7 @@ inline LaunchShape choose_shape(int B, int T, int D, int N, int NG, int esize, b
   LaunchShape ls{0, 0, 0, 0, 0, ""};
   const int max_threads = N > 128 ? kMaxThreadsG8 : kMaxThreads;
   const int sms = num_sms();
-  int nb = (sms + B - 1) / B;
+  int nb = sms / B;  // B * nb <= #SMs: no partial second wave
   if (nb > D) nb = D;
   if (nb < 1) nb = 1;
   int cpb = (D + nb - 1) / nb;
@@ -206,6 +206,9 @@ inline LaunchShape choose_shape(int B, int T, int D, int N, int NG, int esize, b
 // Warp-specialised kernel for channel-shared B/C without explicit q
 // (ssm_scan_fwd_shared.cu).
 int dispatch_shared(const FwdParams& p, int dtype, bool s_real, cudaStream_t st);
+// The same with packed two-lane FP32 arithmetic over pair-interleaved B/C rows
+// (ssm_scan_fwd_packed.cu).
+int dispatch_shared_packed(const FwdParams& p, int dtype, bool s_real, cudaStream_t st);
 // Streaming kernel for per-channel B/C and explicit q (ssm_scan_fwd_stream.cu).
 int dispatch_stream(const FwdParams& p, int dtype, bool s_real, bool q_given, cudaStream_t st);
 // Pass 1 of the time-chunked scan: final state + operator product, no readout.

@@ -324,6 +324,15 @@ bool use_generic_kernel() {
   }();
   return generic;
 }
+// MQC_SCAN_IMPL=scalar keeps channel-shared B/C on the unpacked warp-specialised
+// kernel (ssm_scan_fwd_shared.cu) instead of the packed one.
+bool use_scalar_shared_kernel() {
+  static const bool scalar = [] {
+    const char* v = getenv("MQC_SCAN_IMPL");
+    return v != nullptr && strcmp(v, "scalar") == 0;
+  }();
+  return scalar;
+}
 }  // namespace
 
 extern "C" int mqc_ssm_scan_fwd(const mqc_ssm_scan_args* a, void* stream) {
@@ -335,7 +344,9 @@ extern "C" int mqc_ssm_scan_fwd(const mqc_ssm_scan_args* a, void* stream) {
   const bool q_given = (a->flags & MQC_SSM_Q_GIVEN) != 0;
   const bool s_real = (a->flags & MQC_SSM_S_REAL) != 0;
   if (!use_generic_kernel()) {
-    if (shared && !q_given) return dispatch_shared(p, a->dtype, s_real, as_stream(stream));
+    if (shared && !q_given)
+      return use_scalar_shared_kernel() ? dispatch_shared(p, a->dtype, s_real, as_stream(stream))
+                                        : dispatch_shared_packed(p, a->dtype, s_real, as_stream(stream));
     if (!shared) return dispatch_stream(p, a->dtype, s_real, q_given, as_stream(stream));
   }
   if (a->dtype == MQC_DTYPE_F32) return dispatch_mode<float>(p, a->flags, as_stream(stream));

@@ -318,8 +318,10 @@ int launch_shared(FwdParams p, cudaStream_t st) {
   constexpr int CPW = 32 / NG;
   const int np = NG * G;
   const int sw = S_REAL ? 1 : 4;
+  // one CTA per SM: nb CTAs per batch row with B * nb <= #SMs (never a partial
+  // second wave); rows beyond #SMs simply queue
   const int sms = num_sms();
-  int nb = (sms + p.B - 1) / p.B;
+  int nb = sms / p.B;
   if (nb > p.D) nb = p.D;
   if (nb < 1) nb = 1;
   int cpb = (p.D + nb - 1) / nb;
