@@ -298,6 +298,18 @@ def run_reference(args, world, rank):
     return 0
 
 
+# DRAM bytes (read + write) of one launch of the dominant kernel, from one ncu
+# capture (dram__bytes_read.sum + dram__bytes_write.sum; the capture is
+# summarised under profiles/), keyed by (dtype, layout); None where not captured.
+NCU_TRAFFIC_BYTES = {("fp32", "shared"): 119.68e6 + 152.29e6}
+
+
+def launches_per_scan(dtype: str) -> int:
+    """Kernels one channel-shared fused scan call launches: the B/C pre-pass and
+    the scan, plus the bf16 -> fp32 widening of delta and x for bf16 inputs."""
+    return 2 if dtype == "fp32" else 4
+
+
 def run_b200(args, world, rank, local):
     from mambaqc_b200 import _lib
     from mambaqc_b200.kernels import ssm_scan_cayley
@@ -337,7 +349,9 @@ def run_b200(args, world, rank, local):
     tokens = BATCH * SEQ * world
     value = tokens / (ms_step / 1e3)
 
-    # roofline of the dominant (only) kernel: FP32 issue bound, with the HBM view beside it
+    # roofline of the dominant kernel (the packed scan; the step also runs the small
+    # B/C pre-pass, and for bf16 inputs the widening of delta and x, which the
+    # achieved figures include): FP32 bound, with the HBM view beside it
     elems = BATCH * SEQ * CHANNELS * STATE
     flops = elems * FLOPS_PER_ELEM_SREAL
     abytes = algorithmic_bytes(inp, y_bytes)
@@ -347,11 +361,13 @@ def run_b200(args, world, rank, local):
     roofline = {"bound": "fp32", "achieved": flops / sec / 1e12, "peak": fp32_peak,
                 "unit": "TFLOP/s", "frac": flops / sec / 1e12 / fp32_peak,
                 "peak_source": "FP32 FMA probe (mqc_probe_fp32_fma) run by bench.py, same clocks",
-                "algorithmic_flops_per_launch": flops, "traffic": None}
+                "algorithmic_flops_per_launch": flops,
+                "traffic": NCU_TRAFFIC_BYTES.get((args.dtype, args.layout))}
     roofline_hbm = {"bound": "hbm", "achieved": abytes / sec / 1e9, "peak": peaks["hbm_gbs"],
                     "unit": "GB/s", "frac": abytes / sec / 1e9 / peaks["hbm_gbs"],
                     "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
-                    "algorithmic_bytes_per_launch": abytes, "traffic": None}
+                    "algorithmic_bytes_per_launch": abytes,
+                    "traffic": NCU_TRAFFIC_BYTES.get((args.dtype, args.layout))}
 
     e2e = None
     if not args.no_e2e:
@@ -386,7 +402,8 @@ def run_b200(args, world, rank, local):
                        "parallelism": f"dp{world} (batch shards, no data-path collective)",
                        "l2": "inputs larger than L2 (310+ MB per step)"},
             "roofline": roofline, "roofline_hbm": roofline_hbm,
-            "gpu_launches": args.steps, "clocks": clk, "e2e": e2e, "cpu_baseline": cpu,
+            "gpu_launches": args.steps * launches_per_scan(args.dtype), "clocks": clk,
+            "e2e": e2e, "cpu_baseline": cpu,
             **extras,
         }
         print(json.dumps(line), flush=True)
@@ -415,7 +432,7 @@ def run_e2e(args, inp, dev, world, stream, op):
     ms = max_over_ranks(ms, world, dev)
     return {"value": BATCH * SEQ * world / (ms / 1e3), "unit": "tokens/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms,
-            "steps": steps, "gpu_launches_per_step": BATCH,
+            "steps": steps, "gpu_launches_per_step": BATCH * launches_per_scan(args.dtype),
             "path": "mambaqc_b200.kernels.ssm_scan_cayley_from_host: pinned host inputs -> "
                     "device (copy stream), fused scan per batch row, y -> pinned host "
                     "(third stream)"}

@@ -48,19 +48,9 @@ namespace mqc {
 namespace scan {
 namespace {
 
-// MQC_PK_PIPE=1: the readout of step t is reduced and stored during step t+1.
-#ifndef MQC_PK_PIPE
-#define MQC_PK_PIPE 0
-#endif
-// Unroll factor of the time loop.
-#ifndef MQC_PK_UNROLL
-#define MQC_PK_UNROLL 2
-#endif
-constexpr int kPkUnroll = MQC_PK_UNROLL;
-
 constexpr int kRing = 3;
-// CTA size cap: 8 states per lane need ~128 registers per thread (512 threads);
-// 4 states per lane fit in ~80 (768 threads).
+// CTA size cap: 8 states per lane need ~128 registers per thread (512 threads).
+// (4 states per lane with twice the warps measured slower on config 3.)
 __host__ __device__ constexpr int pk_max_threads(int g) { return g == 4 ? 768 : 512; }
 constexpr size_t kPkSmemBudget = 220 * 1024;
 constexpr int kPackThreads = 256;
@@ -136,6 +126,69 @@ __device__ __forceinline__ void qp_set_half(QPair& q, int e, float4 v) {
   } else {
     q.x.y = v.x; q.y.y = v.y; q.z.y = v.z; q.w.y = v.w;
   }
+}
+
+// Predicated scalar store without a branch (no divergence / reconvergence code
+// in the time loop).
+__device__ __forceinline__ void st1_pred(float* p, float v, bool pred) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %2, 0;\n\t@q st.global.f32 [%0], %1;\n\t}" ::"l"(p),
+               "f"(v), "r"(unsigned(pred))
+               : "memory");
+}
+__device__ __forceinline__ void st1_pred(__nv_bfloat16* p, float v, bool pred) {
+  const unsigned short h = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %2, 0;\n\t@q st.global.b16 [%0], %1;\n\t}" ::"l"(p),
+               "h"(h), "r"(unsigned(pred))
+               : "memory");
+}
+
+// reduce_store_y (ssm_scan_common.cuh) with predicated stores: sums the partial
+// readouts `a` over the NG lanes of a channel (reduce-scatter: afterwards lane ng
+// holds component ng & 3), adds dsk * s and stores y[t, c, 0..3].
+template <typename T, int NG>
+__device__ __forceinline__ void reduce_store_y_pk(float4 a, float4 sv, float dsk, int ng,
+                                                  bool active, T* yp) {
+  constexpr unsigned kFull = 0xffffffffu;
+  if constexpr (NG == 1) {
+    st1_pred(yp + 0, fmaf(dsk, sv.x, a.x), active);
+    st1_pred(yp + 1, fmaf(dsk, sv.y, a.y), active);
+    st1_pred(yp + 2, fmaf(dsk, sv.z, a.z), active);
+    st1_pred(yp + 3, fmaf(dsk, sv.w, a.w), active);
+  } else {
+    const bool odd = ng & 1;
+    const float s0 = odd ? a.x : a.y;
+    const float s1 = odd ? a.z : a.w;
+    const float r0 = __shfl_xor_sync(kFull, s0, 1);
+    const float r1 = __shfl_xor_sync(kFull, s1, 1);
+    const float k0 = (odd ? a.y : a.x) + r0;  // component (odd)
+    const float k1 = (odd ? a.w : a.z) + r1;  // component (odd + 2)
+    if constexpr (NG == 2) {
+      const int c0 = odd ? 1 : 0;
+      st1_pred(yp + c0, fmaf(dsk, f4_get(sv, c0), k0), active);
+      st1_pred(yp + c0 + 2, fmaf(dsk, f4_get(sv, c0 + 2), k1), active);
+    } else {
+      const bool hi = (ng >> 1) & 1;
+      const float snd = hi ? k0 : k1;
+      const float r = __shfl_xor_sync(kFull, snd, 2);
+      float v = (hi ? k1 : k0) + r;
+#pragma unroll
+      for (int m = 4; m < NG; m <<= 1) v += __shfl_xor_sync(kFull, v, m);
+      const int comp = ng & 3;
+      st1_pred(yp + comp, fmaf(dsk, f4_get(sv, comp), v), active && ng < 4);
+    }
+  }
+}
+
+// Bounded wait for a thread off the critical path (the producer, which runs
+// chunks ahead of the consumers): sleeps between polls so that its polling
+// does not take issue slots from the consumer warps on its sub-partition.
+__device__ __forceinline__ bool mbar_wait_bounded_backoff(uint64_t* bar, uint32_t parity,
+                                                          long long limit) {
+  for (long long i = 0; i < limit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    __nanosleep(200);
+  }
+  return false;
 }
 
 // ------------------------------------------------------------ B/C pre-pass
@@ -227,8 +280,8 @@ __host__ __device__ inline PkLayout pk_layout(int tc, int np, int warps, int cpw
 
 // p.Bm / p.Cm point at the packed rows and p.delta / p.s at fp32 data here; T is
 // the type of y. CKPT: p.ckpt is set (the forward of a training step stores
-// states for the backward).
-template <typename T, int G, int NG, bool S_REAL, bool CKPT>
+// states for the backward). DT: the skip weight varies over time (p.dst != 0).
+template <typename T, int G, int NG, bool S_REAL, bool CKPT, bool DT>
 __global__ void __launch_bounds__(pk_max_threads(G), 1)
     scan_fwd_packed_kernel(const FwdParams p) {
   static_assert(G % 2 == 0, "states are processed in pairs");
@@ -277,7 +330,8 @@ __global__ void __launch_bounds__(pk_max_threads(G), 1)
       for (int k = 0; k < nchunks; ++k) {
         const int st = k % kRing;
         if (k >= kRing) {
-          ok = mbar_wait_bounded(&empty[st], uint32_t(((k / kRing) - 1) & 1), p.wait_limit);
+          ok = mbar_wait_bounded_backoff(&empty[st], uint32_t(((k / kRing) - 1) & 1),
+                                         p.wait_limit);
           if (!ok) break;
         }
         if (*abort_flag) break;
@@ -330,7 +384,6 @@ __global__ void __launch_bounds__(pk_max_threads(G), 1)
                     make_float2(k2[0].lj, k2[1].lj), make_float2(k2[0].lk, k2[1].lk),
                     make_float2(k2[0].m, k2[1].m)};
   }
-  const bool d_const = p.dst == 0;
   const float dsk0 = active ? __ldg(p.dskip + int64_t(b) * p.dsb + int64_t(c) * p.dsd) : 0.f;
 
   // warp-private staging of delta and s: [2][tc][CPW] (+ [SW] for s)
@@ -360,14 +413,6 @@ __global__ void __launch_bounds__(pk_max_threads(G), 1)
 
   const float eps = p.eps;
   T* yb = static_cast<T*>(p.y) + (int64_t(b) * T_ * D + c) * 4;
-  // The readout of step t is reduced over the NG lanes and stored while step
-  // t+1 runs (software pipelining): its three dependent shuffle rounds then
-  // overlap the next step's FP32 work instead of stalling the warp. `pend_*`
-  // carries the pending step; `pend_on` is false until the first step.
-  float4 pend_y = f4_zero(), pend_s = f4_zero();
-  float pend_d = 0.f;
-  int pend_t = 0;
-  bool pend_on = false;
   for (int k = 0; k < nchunks; ++k) {
     const int st = k % kRing;
     const int buf = k & 1;
@@ -391,9 +436,10 @@ __global__ void __launch_bounds__(pk_max_threads(G), 1)
     const float* rowC = sC + int64_t(st) * tc * NP * 4 + ng * 8;
     // unrolled by two so the loop-carried states alternate between two register
     // sets instead of being copied back at every step
-#pragma unroll kPkUnroll
-    for (int tt = 0; tt < len; ++tt) {
-      const int t = t0 + tt;
+    T* yrow = yb + int64_t(t0) * D * 4;
+    const int64_t ystep = int64_t(D) * 4;
+#pragma unroll 2
+    for (int tt = 0; tt < len; ++tt, yrow += ystep) {
       const float dl = cdel[tt * CPW + lc_ch];
       const float dl2 = dl * dl;
       float4 sv;
@@ -422,32 +468,29 @@ __global__ void __launch_bounds__(pk_max_threads(G), 1)
         }
         h[j] = qp_mul_acc(qv, h[j], inj);
         ya = qp_mul_acc(Cq, h[j], ya);
-        if (MQC_PK_PIPE && j == G2 / 2 - 1)  // previous step's readout, mid-step
-          reduce_store_y<T, NG>(pend_y, pend_s, pend_d, ng, active && pend_on,
-                                yb + int64_t(pend_t) * D * 4);
       }
       // even states + odd states, as the scalar kernel's two accumulators
-      pend_y = make_float4(ya.x.x + ya.x.y, ya.y.x + ya.y.y, ya.z.x + ya.z.y, ya.w.x + ya.w.y);
-      pend_s = sv;
-      pend_d = dsk0;
-      if (!d_const)
-        pend_d = (active && ng < 4)
-                     ? __ldg(p.dskip + int64_t(b) * p.dsb + int64_t(t) * p.dst + int64_t(c) * p.dsd)
-                     : 0.f;
-      pend_t = t;
-      pend_on = true;
-      if (!MQC_PK_PIPE)
-        reduce_store_y<T, NG>(pend_y, pend_s, pend_d, ng, active, yb + int64_t(t) * D * 4);
-      if (CKPT && active && (t + 1) % p.ckpt_every == 0 && t + 1 < T_) {
-        float* base =
-            p.ckpt + ((int64_t(b) * p.nck + (t + 1) / p.ckpt_every - 1) * D + c) * int64_t(N) * 4;
+      const float4 yv =
+          make_float4(ya.x.x + ya.x.y, ya.y.x + ya.y.y, ya.z.x + ya.z.y, ya.w.x + ya.w.y);
+      float dsk = dsk0;
+      if constexpr (DT)
+        dsk = (active && ng < 4) ? __ldg(p.dskip + int64_t(b) * p.dsb +
+                                         int64_t(t0 + tt) * p.dst + int64_t(c) * p.dsd)
+                                 : 0.f;
+      reduce_store_y_pk<T, NG>(yv, sv, dsk, ng, active, yrow);
+      if constexpr (CKPT) {
+        const int t = t0 + tt;
+        if (active && (t + 1) % p.ckpt_every == 0 && t + 1 < T_) {
+          float* base = p.ckpt +
+                        ((int64_t(b) * p.nck + (t + 1) / p.ckpt_every - 1) * D + c) * int64_t(N) * 4;
 #pragma unroll
-        for (int j = 0; j < G2; ++j)
+          for (int j = 0; j < G2; ++j)
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int n = ng + NG * (2 * j + e);
-            if (n < N) QIO<float>::st(base + int64_t(n) * 4, qp_half(h[j], e));
-          }
+            for (int e = 0; e < 2; ++e) {
+              const int n = ng + NG * (2 * j + e);
+              if (n < N) QIO<float>::st(base + int64_t(n) * 4, qp_half(h[j], e));
+            }
+        }
       }
     }
     __syncwarp();
@@ -457,10 +500,6 @@ __global__ void __launch_bounds__(pk_max_threads(G), 1)
       __syncwarp();
     }
   }
-  if (MQC_PK_PIPE)
-    reduce_store_y<T, NG>(pend_y, pend_s, pend_d, ng, active && pend_on,
-                          yb + int64_t(pend_t) * D * 4);
-
   if (p.hT != nullptr && active) {
 #pragma unroll
     for (int j = 0; j < G2; ++j)
@@ -538,8 +577,11 @@ int launch_packed(FwdParams p, cudaStream_t st) {
     p.nb = nb;
     p.cpb = cpb;
     p.tc = tc;
-    auto kern = p.ckpt != nullptr ? scan_fwd_packed_kernel<T, G, NG, S_REAL, true>
-                                  : scan_fwd_packed_kernel<T, G, NG, S_REAL, false>;
+    const bool ck = p.ckpt != nullptr, dt = p.dst != 0;
+    auto kern = ck ? (dt ? scan_fwd_packed_kernel<T, G, NG, S_REAL, true, true>
+                         : scan_fwd_packed_kernel<T, G, NG, S_REAL, true, false>)
+                   : (dt ? scan_fwd_packed_kernel<T, G, NG, S_REAL, false, true>
+                         : scan_fwd_packed_kernel<T, G, NG, S_REAL, false, false>);
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) {
       rc = fail(MQC_ERR_CUDA, "mqc_ssm_scan_fwd: smem attribute (%zu B): %s", smem,
@@ -573,19 +615,8 @@ int dispatch_packed_g(const FwdParams& p, cudaStream_t st) {
   }
 }
 
-// States per lane: 8 by default; MQC_SCAN_G=4 selects 4 (twice the warps, about
-// 80 registers per thread) for tuning comparisons.
-int pk_states_per_lane() {
-  static const int g = [] {
-    const char* v = getenv("MQC_SCAN_G");
-    return (v != nullptr && v[0] == '4' && v[1] == '\0') ? 4 : 8;
-  }();
-  return g;
-}
-
 template <typename T, bool S_REAL>
 int dispatch_packed_t(const FwdParams& p, cudaStream_t st) {
-  if (pk_states_per_lane() == 4 && p.N <= 128) return dispatch_packed_g<T, 4, S_REAL>(p, st);
   return dispatch_packed_g<T, 8, S_REAL>(p, st);
 }
 
