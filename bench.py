@@ -63,7 +63,7 @@ def parse_args():
                     help="skip the forward+backward and per-channel-layout sub-measurements")
     ap.add_argument("--only", choices=["fwd_bwd", "perchannel"], default=None,
                     help="run only this sub-measurement and print it (profiling aid)")
-    ap.add_argument("--workload", choices=["config3", "config5"], default="config3",
+    ap.add_argument("--workload", choices=["config3", "config5", "config2"], default="config3",
                     help="config5: B=1, T=65536, D=1536, N=64, bf16, channel-sharded over the "
                          "GPUs with an NCCL all-gather of y (strong scaling)")
     return ap.parse_args()
@@ -556,6 +556,98 @@ def run_config5(args, world, rank, local):
     return 0
 
 
+def run_config2(args, world, rank, local):
+    """Config 2: the quaternion primitives on their own, each timed with one pair
+    of CUDA events around K back-to-back launches (replays of a CUDA graph of the
+    public calls, so host call overhead is not in the kernel figures). Primitives
+    whose data fit in L2 rotate over enough independent input/output sets
+    (together larger than L2) that every launch reads its input from HBM. Reported against the measured
+    HBM bandwidth, with algorithmic bytes = inputs read once + outputs written once."""
+    from mambaqc_b200.kernels import (cayley_discretization_fused, parallel_scan_quaternion,
+                                      quaternion_layer_norm_fused, quaternion_multiply)
+
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    peaks, peak_kind = measured_peaks()
+    hbm = peaks["hbm_gbs"]
+    g = torch.Generator(device=dev).manual_seed(0)
+    steps = max(8, min(args.steps, 64))
+    l2_bytes = 126 << 20
+
+    def time_rotating(fns):
+        # the launches are captured once in a CUDA graph and the graph is replayed,
+        # so the kernels run back to back without waiting on the Python call path
+        k = len(fns)
+        for f in fns:
+            f()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for f in fns:
+                f()
+        reps = max(1, steps // k)
+        ms = timed(graph.replay, reps, 3, world, stream)
+        del graph
+        return max_over_ranks(ms / (reps * k), world, dev)
+
+    def sets_for(bytes_per_set):
+        return max(1, -(-2 * l2_bytes // bytes_per_set))  # > 2x L2 in total
+
+    res = {}
+    with torch.no_grad():
+        p = torch.randn(1 << 26, 4, generator=g, device=dev)
+        q = torch.randn(1 << 26, 4, generator=g, device=dev)
+        ms = time_rotating([lambda: quaternion_multiply(p, q)])
+        res["qmul"] = {"shape": [1 << 26, 4], "ms": ms, "bytes": 3 * p.numel() * 4, "sets": 1}
+        del p, q
+        zs = []
+        nz = sets_for(2 * 2 * 16 * 768 * 64 * 16)
+        for _ in range(nz):
+            z = torch.randn(2, 16, 768, 64, 4, generator=g, device=dev)
+            z[..., 0] = -z[..., 0].abs()
+            zs.append(z)
+        ms = time_rotating([(lambda z=z: cayley_discretization_fused(z)) for z in zs])
+        res["cayley"] = {"shape": list(zs[0].shape), "ms": ms, "bytes": 2 * zs[0].numel() * 4,
+                         "sets": nz}
+        del zs
+        u = torch.randn(2, 256, 768, 64, 4, generator=g, device=dev)
+        r = torch.rand(2, 256, 768, 64, 1, generator=g, device=dev) * 0.099 + 0.9
+        qs = u / torch.linalg.vector_norm(u, dim=-1, keepdim=True) * r
+        del u, r
+        ms = time_rotating([lambda: parallel_scan_quaternion(qs)])
+        res["prefix_scan"] = {"shape": list(qs.shape), "ms": ms, "bytes": 2 * qs.numel() * 4,
+                              "sets": 1}
+        del qs
+        gamma = torch.ones(768, device=dev)
+        beta = torch.zeros(768, 4, device=dev)
+        nx = sets_for(2 * 4 * 2048 * 768 * 16)
+        xs = [torch.randn(4, 2048, 768, 4, generator=g, device=dev) for _ in range(nx)]
+        ms = time_rotating([(lambda x=x: quaternion_layer_norm_fused(x, gamma, beta)) for x in xs])
+        res["layer_norm"] = {"shape": list(xs[0].shape), "ms": ms, "sets": nx,
+                             "bytes": 2 * xs[0].numel() * 4 + gamma.numel() * 4 + beta.numel() * 4}
+        del xs
+    for v in res.values():
+        v["gbps"] = v["bytes"] / (v["ms"] / 1e3) / 1e9
+        v["frac_of_hbm"] = v["gbps"] / hbm
+    if rank == 0:
+        geo = math.exp(sum(math.log(v["frac_of_hbm"]) for v in res.values()) / len(res))
+        line = {
+            "metric": "config2 quaternion primitives, HBM bandwidth (geometric mean fraction of "
+                      "measured HBM over qmul, Cayley, prefix scan, LayerNorm)",
+            "value": geo, "unit": "fraction of measured HBM GB/s", "n_gpus": world,
+            "steps": steps, "warmup": 3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config-2 shapes)",
+            "config": {"workload": "config2_primitives",
+                       "l2": "Cayley and LayerNorm rotate over input/output sets totalling "
+                             "more than 2x L2; qmul and prefix scan inputs exceed L2"},
+            "hbm_peak_gbs": hbm, "hbm_peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+            "primitives": res, "gpu_launches": steps * len(res),
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse_args()
     world, rank, local = dist_setup(args)
@@ -564,6 +656,8 @@ def main():
             return run_reference(args, world, rank)
         if args.workload == "config5":
             return run_config5(args, world, rank, local)
+        if args.workload == "config2":
+            return run_config2(args, world, rank, local)
         return run_b200(args, world, rank, local)
     finally:
         if dist.is_initialized():

@@ -96,7 +96,9 @@ MQC_API int mqc_cayley_bwd(const void* z, const void* dq, void* dz, int64_t n, f
 MQC_API int mqc_prefix_prod(const void* q, void* out, int64_t batch, int64_t seq_len, int64_t lanes,
                     int dtype, void* stream);
 
-/* Same result as mqc_prefix_prod, allocating nothing. No counterpart in the
+/* Same result as mqc_prefix_prod (up to rounding: it splits time into chunks
+ * whenever the lanes give fewer than 1024 threads per SM, a more eager split
+ * than mqc_prefix_prod's), allocating nothing. No counterpart in the
  * reference. For callers that cannot allocate device memory while they run --
  * e.g. a server that gives all device memory to its own allocator at start-up,
  * or a process on a fixed device-memory budget where an allocation failing

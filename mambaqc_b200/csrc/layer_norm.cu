@@ -72,23 +72,25 @@ __global__ void __launch_bounds__(kMaxRowThreads) qln_fwd_kernel(
   if (pad_lanes) tot2 += float(pad_lanes) * (pad_norm - mu) * (pad_norm - mu);
   const float var = tot2 / float(D);
   const float sd = sqrtf(var + eps);
+  const float rsd = 1.f / sd;
   if (threadIdx.x == 0) {
     if (mean_out) mean_out[row] = mu;
-    if (rstd_out) rstd_out[row] = 1.f / sd;
+    if (rstd_out) rstd_out[row] = rsd;
   }
+  // one reciprocal per quaternion (and one per row) instead of a division per
+  // component: out = gamma * nh * q / (n + eps) + beta
 #pragma unroll
   for (int j = 0; j < kVpt; ++j) {
     const int d = threadIdx.x + j * blockDim.x;
     if (d < D) {
-      const float nh = (nrm[j] - mu) / sd;
-      const float g = __ldg(gamma + d) * nh;
-      const float dn = nrm[j] + eps;
+      const float nh = (nrm[j] - mu) * rsd;
+      const float g = __ldg(gamma + d) * nh * (1.f / (nrm[j] + eps));
       const float4 bt = QIO<float>::ld(beta + d * 4);
       float4 o;
-      o.x = fmaf(g, v[j].x / dn, bt.x);
-      o.y = fmaf(g, v[j].y / dn, bt.y);
-      o.z = fmaf(g, v[j].z / dn, bt.z);
-      o.w = fmaf(g, v[j].w / dn, bt.w);
+      o.x = fmaf(g, v[j].x, bt.x);
+      o.y = fmaf(g, v[j].y, bt.y);
+      o.z = fmaf(g, v[j].z, bt.z);
+      o.w = fmaf(g, v[j].w, bt.w);
       QIO<T>::st_stream(orow + d * 4, o);
     }
   }

@@ -3,6 +3,7 @@
 
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 namespace mqc {
 
@@ -41,6 +42,50 @@ int num_sms() {
   }
   return g_sm_count[dev];
 }
+
+namespace {
+std::mutex g_pool_mu;
+cudaMemPool_t g_pool[kMaxDevices] = {};
+
+cudaError_t scratch_pool(cudaMemPool_t* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_pool_mu);
+  if (g_pool[dev] == nullptr) {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t pool = nullptr;
+    e = cudaMemPoolCreate(&pool, &props);
+    if (e != cudaSuccess) return e;
+    uint64_t keep = kScratchKeepBytes;
+    e = cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    if (e != cudaSuccess) {
+      cudaMemPoolDestroy(pool);
+      return e;
+    }
+    g_pool[dev] = pool;
+  }
+  *out = g_pool[dev];
+  return cudaSuccess;
+}
+}  // namespace
+
+cudaError_t scratch_alloc(void** p, size_t bytes, cudaStream_t st) {
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(st, &cap);
+  if (e != cudaSuccess) return e;
+  if (cap != cudaStreamCaptureStatusNone) return cudaMallocAsync(p, bytes, st);
+  cudaMemPool_t pool = nullptr;
+  e = scratch_pool(&pool);
+  if (e != cudaSuccess) return e;
+  return cudaMallocFromPoolAsync(p, bytes, pool, st);
+}
+
+cudaError_t scratch_free(void* p, cudaStream_t st) { return cudaFreeAsync(p, st); }
 
 }  // namespace mqc
 

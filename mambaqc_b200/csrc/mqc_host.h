@@ -19,6 +19,15 @@ void clear_error();
 int check_launch(const char* what);
 // Number of SMs of the current device (cached per device).
 int num_sms();
+// Stream-ordered scratch for the entry points that need it (current device).
+// Memory comes from a pool private to the library, one per device, that keeps
+// up to kScratchKeepBytes cached across synchronisations instead of handing it
+// back to the driver after every synchronize (what the default pool does), so
+// repeated calls do not re-map their scratch. While `st` is being captured into
+// a CUDA graph the default pool is used (the allocation becomes a graph node).
+constexpr uint64_t kScratchKeepBytes = uint64_t(8) << 30;
+cudaError_t scratch_alloc(void** p, size_t bytes, cudaStream_t st);
+cudaError_t scratch_free(void* p, cudaStream_t st);
 
 inline bool aligned(const void* p, uintptr_t a) {
   return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;

@@ -23,20 +23,31 @@ constexpr int kThreads = 256;
 constexpr int kUnroll = 8;
 
 // Runs steps [t0, t1) of lane (b, l) starting from `acc`; optionally stores each
-// prefix to `out`, returns the final accumulator.
+// prefix to `out`, returns the final accumulator. Loads are double-buffered: the
+// next kUnroll steps are requested before the current ones are multiplied and
+// stored, so every thread always has loads in flight.
 template <typename T, bool STORE>
 __device__ __forceinline__ float4 run_chain(const T* __restrict__ q, T* __restrict__ out,
                                             int64_t row_stride, int64_t off, int64_t t0,
                                             int64_t t1, float4 acc) {
   int64_t t = t0;
-  for (; t + kUnroll <= t1; t += kUnroll) {
-    float4 v[kUnroll];
+  if (t + kUnroll <= t1) {
+    float4 cur[kUnroll];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) v[u] = QIO<T>::ld_stream(q + off + (t + u) * row_stride);
+    for (int u = 0; u < kUnroll; ++u) cur[u] = QIO<T>::ld_stream(q + off + (t + u) * row_stride);
+    for (; t + kUnroll <= t1; t += kUnroll) {
+      float4 nxt[kUnroll];
+      const bool more = t + 2 * kUnroll <= t1;
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      acc = qmul(v[u], acc);
-      if (STORE) QIO<T>::st_stream(out + off + (t + u) * row_stride, acc);
+      for (int u = 0; u < kUnroll; ++u)
+        nxt[u] = more ? QIO<T>::ld_stream(q + off + (t + kUnroll + u) * row_stride) : cur[u];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        acc = qmul(cur[u], acc);
+        if (STORE) QIO<T>::st_stream(out + off + (t + u) * row_stride, acc);
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) cur[u] = nxt[u];
     }
   }
   for (; t < t1; ++t) {
@@ -97,7 +108,9 @@ int launch(const void* qv, void* outv, int64_t batch, int64_t seq_len, int64_t l
   const T* q = static_cast<const T*>(qv);
   T* out = static_cast<T*>(outv);
   const int64_t lane_blocks = (lanes + kThreads - 1) / kThreads;
-  const int64_t want_threads = int64_t(num_sms()) * 1024;
+  // a single streaming pass needs only a few hundred threads per SM (each keeps
+  // 2 x kUnroll loads in flight); chunk time only below that
+  const int64_t want_threads = int64_t(num_sms()) * 256;
   const int64_t have = batch * lanes;
   int64_t nchunks = 1;
   if (have < want_threads && seq_len >= 64) {
@@ -120,7 +133,7 @@ int launch(const void* qv, void* outv, int64_t batch, int64_t seq_len, int64_t l
   // stream right after pass 2, so the memory pool recycles it).
   float* P = nullptr;
   const size_t bytes = size_t(batch) * size_t(nchunks) * size_t(lanes) * 16;
-  cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&P), bytes, st);
+  cudaError_t e = scratch_alloc(reinterpret_cast<void**>(&P), bytes, st);
   if (e != cudaSuccess)
     return fail(MQC_ERR_CUDA, "mqc_prefix_prod: scratch allocation of %zu bytes: %s", bytes,
                 cudaGetErrorString(e));
@@ -128,7 +141,7 @@ int launch(const void* qv, void* outv, int64_t batch, int64_t seq_len, int64_t l
   prefix_chunk_total_kernel<T><<<grid, kThreads, 0, st>>>(q, P, seq_len, lanes, chunk);
   prefix_chunk_apply_kernel<T><<<grid, kThreads, 0, st>>>(q, P, out, seq_len, lanes, chunk);
   int rc = check_launch("mqc_prefix_prod(chunked)");
-  cudaFreeAsync(P, st);
+  scratch_free(P, st);
   return rc;
 }
 
@@ -205,7 +218,9 @@ int launch_noalloc(const void* qv, void* outv, int64_t batch, int64_t seq_len, i
   MQC_REQUIRE(lane_blocks <= 0x7fffffff && batch <= 65535, MQC_ERR_UNSUPPORTED,
               "mqc_prefix_prod_noalloc: grid too large (batch=%lld lanes=%lld)", (long long)batch,
               (long long)lanes);
-  // same time-chunk choice as mqc_prefix_prod
+  // time chunks whenever the lanes give fewer than 1024 threads per SM (a more
+  // eager split than mqc_prefix_prod's, kept so that the chunk scratch, and with
+  // it the sizes this entry point rejects, stay as documented)
   const int64_t want_threads = int64_t(num_sms()) * 1024;
   const int64_t have = batch * lanes;
   int64_t nchunks = 1;

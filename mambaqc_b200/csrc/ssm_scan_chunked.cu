@@ -12,6 +12,8 @@
 //   pass 2  the regular fused scan of every chunk from H_{c-1} -> y
 // Pass 2 is the same kernel as the unchunked scan; the extra work is pass 1
 // (a scan without readout) and the carry (3 x 16 B per chunk and lane).
+#include <cstdlib>
+
 #include "ssm_scan_common.cuh"
 
 namespace mqc {
@@ -97,7 +99,10 @@ extern "C" int mqc_ssm_scan_fwd_chunked(const mqc_ssm_scan_args* a, int64_t nchu
   p1.y = nullptr;
   p1.ckpt = nullptr;
   p1.nck = 0;
-  rc = dispatch_state_only(p1, a->dtype, s_real, shared, st);
+  const char* impl = getenv("MQC_SCAN_IMPL");
+  const bool packed = shared && (impl == nullptr || impl[0] == '\0');
+  rc = packed ? dispatch_state_only_packed(p1, a->dtype, s_real, st)
+              : dispatch_state_only(p1, a->dtype, s_real, shared, st);
   if (rc != MQC_OK) return rc;
 
   // carry: start state of every chunk, and the final state

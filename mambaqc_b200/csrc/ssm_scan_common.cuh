@@ -209,6 +209,8 @@ int dispatch_shared(const FwdParams& p, int dtype, bool s_real, cudaStream_t st)
 // The same with packed two-lane FP32 arithmetic over pair-interleaved B/C rows
 // (ssm_scan_fwd_packed.cu).
 int dispatch_shared_packed(const FwdParams& p, int dtype, bool s_real, cudaStream_t st);
+// Pass 1 of the time-chunked scan on the packed kernel (channel-shared B/C).
+int dispatch_state_only_packed(const FwdParams& p, int dtype, bool s_real, cudaStream_t st);
 // Streaming kernel for per-channel B/C and explicit q (ssm_scan_fwd_stream.cu).
 int dispatch_stream(const FwdParams& p, int dtype, bool s_real, bool q_given, cudaStream_t st);
 // Pass 1 of the time-chunked scan: final state + operator product, no readout.

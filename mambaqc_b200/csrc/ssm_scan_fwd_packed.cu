@@ -105,14 +105,17 @@ struct LamPair {
   float2 lr, li, lj, lk, m;
 };
 
-// cayley_from_const (ssm_scan_common.cuh) for both halves.
-__device__ __forceinline__ QPair cayley_pair(float dl, float dl2, const LamPair& c, float eps) {
+// cayley_from_const (ssm_scan_common.cuh) for both halves; *s_out (if given)
+// receives delta / den, the factor of Im Lambda in q.
+__device__ __forceinline__ QPair cayley_pair(float dl, float dl2, const LamPair& c, float eps,
+                                             float2* s_out = nullptr) {
   const float2 P = mul2(bc2(dl2), c.m);
   float2 den = fma2(bc2(-dl), c.lr, add2(bc2(1.f), P));
   den.x = fmaxf(den.x, eps);
   den.y = fmaxf(den.y, eps);
   const float2 inv = rcp_nr2(den);
   const float2 s = mul2(bc2(dl), inv);
+  if (s_out != nullptr) *s_out = s;
   return QPair{fma2(neg2(P), inv, inv), mul2(s, c.li), mul2(s, c.lj), mul2(s, c.lk)};
 }
 
@@ -212,14 +215,16 @@ __global__ void __launch_bounds__(kPackThreads)
     const int64_t base = row * N;
     const float4 b0 = n0 < N ? QIO<T>::ld(Bm + (base + n0) * 4) : f4_zero();
     const float4 b1 = n1 < N ? QIO<T>::ld(Bm + (base + n1) * 4) : f4_zero();
-    const float4 c0 = n0 < N ? QIO<T>::ld(Cm + (base + n0) * 4) : f4_zero();
-    const float4 c1 = n1 < N ? QIO<T>::ld(Cm + (base + n1) * 4) : f4_zero();
     float4* ob = reinterpret_cast<float4*>(Bp + idx * 8);
-    float4* oc = reinterpret_cast<float4*>(Cp + idx * 8);
     ob[0] = make_float4(b0.x, b1.x, b0.y, b1.y);
     ob[1] = make_float4(b0.z, b1.z, b0.w, b1.w);
-    oc[0] = make_float4(c0.x, c1.x, c0.y, c1.y);
-    oc[1] = make_float4(c0.z, c1.z, c0.w, c1.w);
+    if (Cm != nullptr) {  // C is not needed by the state-only pass
+      const float4 c0 = n0 < N ? QIO<T>::ld(Cm + (base + n0) * 4) : f4_zero();
+      const float4 c1 = n1 < N ? QIO<T>::ld(Cm + (base + n1) * 4) : f4_zero();
+      float4* oc = reinterpret_cast<float4*>(Cp + idx * 8);
+      oc[0] = make_float4(c0.x, c1.x, c0.y, c1.y);
+      oc[1] = make_float4(c0.z, c1.z, c0.w, c1.w);
+    }
   }
 }
 
@@ -281,7 +286,13 @@ __host__ __device__ inline PkLayout pk_layout(int tc, int np, int warps, int cpw
 // p.Bm / p.Cm point at the packed rows and p.delta / p.s at fp32 data here; T is
 // the type of y. CKPT: p.ckpt is set (the forward of a training step stores
 // states for the backward). DT: the skip weight varies over time (p.dst != 0).
-template <typename T, int G, int NG, bool S_REAL, bool CKPT, bool DT>
+// SO (state only, pass 1 of the time-chunked scan): no readout and no C; the
+// kernel writes the final state to p.hT and the product of the step operators
+// P = q_{T-1} (x) ... (x) q_0 to p.pout. All q_t of a lane lie in the plane
+// span{1, u}, u = Im Lambda / |Im Lambda|, where quaternions commute and
+// multiply like complex numbers, so P is kept as (Pa, Pb) with P = Pa + Pb u:
+// 4 operations per step instead of a 16-term Hamilton product.
+template <typename T, int G, int NG, bool S_REAL, bool CKPT, bool DT, bool SO>
 __global__ void __launch_bounds__(pk_max_threads(G), 1)
     scan_fwd_packed_kernel(const FwdParams p) {
   static_assert(G % 2 == 0, "states are processed in pairs");
@@ -338,10 +349,10 @@ __global__ void __launch_bounds__(pk_max_threads(G), 1)
         const int t0 = k * tc;
         const int len = min(tc, T_ - t0);
         const uint32_t bytes = uint32_t(len) * row_bytes;
-        mbar_arrive_expect_tx(&full[st], 2u * bytes);
+        mbar_arrive_expect_tx(&full[st], (SO ? 1u : 2u) * bytes);
         const int64_t g0 = (int64_t(b) * T_ + t0) * NP * 4;
         bulk_g2s(sB + int64_t(st) * tc * NP * 4, gB + g0, bytes, &full[st]);
-        bulk_g2s(sC + int64_t(st) * tc * NP * 4, gC + g0, bytes, &full[st]);
+        if (!SO) bulk_g2s(sC + int64_t(st) * tc * NP * 4, gC + g0, bytes, &full[st]);
         issued = k + 1;
       }
       if (!ok) {
@@ -384,6 +395,18 @@ __global__ void __launch_bounds__(pk_max_threads(G), 1)
                     make_float2(k2[0].lj, k2[1].lj), make_float2(k2[0].lk, k2[1].lk),
                     make_float2(k2[0].m, k2[1].m)};
   }
+  // SO: |Im Lambda| per state and the operator product (Pa, Pb), P = Pa + Pb u
+  float2 nim[SO ? G2 : 1], Pa[SO ? G2 : 1], Pb[SO ? G2 : 1];
+  if constexpr (SO) {
+#pragma unroll
+    for (int j = 0; j < G2; ++j) {
+      const LamPair& l = lc[j];
+      nim[j] = make_float2(sqrtf(fmaf(l.li.x, l.li.x, fmaf(l.lj.x, l.lj.x, l.lk.x * l.lk.x))),
+                           sqrtf(fmaf(l.li.y, l.li.y, fmaf(l.lj.y, l.lj.y, l.lk.y * l.lk.y))));
+      Pa[j] = bc2(1.f);
+      Pb[j] = bc2(0.f);
+    }
+  }
   const float dsk0 = active ? __ldg(p.dskip + int64_t(b) * p.dsb + int64_t(c) * p.dsd) : 0.f;
 
   // warp-private staging of delta and s: [2][tc][CPW] (+ [SW] for s)
@@ -412,7 +435,7 @@ __global__ void __launch_bounds__(pk_max_threads(G), 1)
   __syncwarp();
 
   const float eps = p.eps;
-  T* yb = static_cast<T*>(p.y) + (int64_t(b) * T_ * D + c) * 4;
+  T* yb = SO ? nullptr : static_cast<T*>(p.y) + (int64_t(b) * T_ * D + c) * 4;
   for (int k = 0; k < nchunks; ++k) {
     const int st = k % kRing;
     const int buf = k & 1;
@@ -449,16 +472,12 @@ __global__ void __launch_bounds__(pk_max_threads(G), 1)
 #pragma unroll
       for (int j = 0; j < G2; ++j) {
         const float* pb = rowB + tt * NP * 4 + j * NG * 8;
-        const float* pc = rowC + tt * NP * 4 + j * NG * 8;
         const float4 b01 = *reinterpret_cast<const float4*>(pb);
         const float4 b23 = *reinterpret_cast<const float4*>(pb + 4);
-        const float4 c01 = *reinterpret_cast<const float4*>(pc);
-        const float4 c23 = *reinterpret_cast<const float4*>(pc + 4);
         const QPair Bq{make_float2(b01.x, b01.y), make_float2(b01.z, b01.w),
                        make_float2(b23.x, b23.y), make_float2(b23.z, b23.w)};
-        const QPair Cq{make_float2(c01.x, c01.y), make_float2(c01.z, c01.w),
-                       make_float2(c23.x, c23.y), make_float2(c23.z, c23.w)};
-        const QPair qv = cayley_pair(dl, dl2, lc[j], eps);
+        float2 sq;
+        const QPair qv = cayley_pair(dl, dl2, lc[j], eps, &sq);
         QPair inj;
         if (S_REAL) {
           const float2 s2 = bc2(sv.x);
@@ -467,17 +486,32 @@ __global__ void __launch_bounds__(pk_max_threads(G), 1)
           inj = qp_mul_bcast(Bq, sv);
         }
         h[j] = qp_mul_acc(qv, h[j], inj);
-        ya = qp_mul_acc(Cq, h[j], ya);
+        if constexpr (SO) {
+          // q = qa + qb u with qa = q.x, qb = (delta / den) |Im Lambda|; P <- q P
+          const float2 qb = mul2(sq, nim[j]);
+          const float2 pa = fma2(qv.x, Pa[j], neg2(mul2(qb, Pb[j])));
+          Pb[j] = fma2(qv.x, Pb[j], mul2(qb, Pa[j]));
+          Pa[j] = pa;
+        } else {
+          const float* pc = rowC + tt * NP * 4 + j * NG * 8;
+          const float4 c01 = *reinterpret_cast<const float4*>(pc);
+          const float4 c23 = *reinterpret_cast<const float4*>(pc + 4);
+          const QPair Cq{make_float2(c01.x, c01.y), make_float2(c01.z, c01.w),
+                         make_float2(c23.x, c23.y), make_float2(c23.z, c23.w)};
+          ya = qp_mul_acc(Cq, h[j], ya);
+        }
       }
-      // even states + odd states, as the scalar kernel's two accumulators
-      const float4 yv =
-          make_float4(ya.x.x + ya.x.y, ya.y.x + ya.y.y, ya.z.x + ya.z.y, ya.w.x + ya.w.y);
-      float dsk = dsk0;
-      if constexpr (DT)
-        dsk = (active && ng < 4) ? __ldg(p.dskip + int64_t(b) * p.dsb +
-                                         int64_t(t0 + tt) * p.dst + int64_t(c) * p.dsd)
-                                 : 0.f;
-      reduce_store_y_pk<T, NG>(yv, sv, dsk, ng, active, yrow);
+      if constexpr (!SO) {
+        // even states + odd states, as the scalar kernel's two accumulators
+        const float4 yv =
+            make_float4(ya.x.x + ya.x.y, ya.y.x + ya.y.y, ya.z.x + ya.z.y, ya.w.x + ya.w.y);
+        float dsk = dsk0;
+        if constexpr (DT)
+          dsk = (active && ng < 4) ? __ldg(p.dskip + int64_t(b) * p.dsb +
+                                           int64_t(t0 + tt) * p.dst + int64_t(c) * p.dsd)
+                                   : 0.f;
+        reduce_store_y_pk<T, NG>(yv, sv, dsk, ng, active, yrow);
+      }
       if constexpr (CKPT) {
         const int t = t0 + tt;
         if (active && (t + 1) % p.ckpt_every == 0 && t + 1 < T_) {
@@ -509,10 +543,29 @@ __global__ void __launch_bounds__(pk_max_threads(G), 1)
         if (n < N) QIO<float>::st(p.hT + ((int64_t(b) * D + c) * N + n) * 4, qp_half(h[j], e));
       }
   }
+  if constexpr (SO) {
+    if (active) {
+#pragma unroll
+      for (int j = 0; j < G2; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int n = ng + NG * (2 * j + e);
+          if (n < N) {
+            const float nm = e ? nim[j].y : nim[j].x;
+            const float pa = e ? Pa[j].y : Pa[j].x;
+            const float pbu = (nm > 0.f ? (e ? Pb[j].y : Pb[j].x) / nm : 0.f);
+            const LamPair& l = lc[j];
+            const float4 P4 = make_float4(pa, pbu * (e ? l.li.y : l.li.x),
+                                          pbu * (e ? l.lj.y : l.lj.x), pbu * (e ? l.lk.y : l.lk.x));
+            QIO<float>::st(p.pout + ((int64_t(b) * D + c) * N + n) * 4, P4);
+          }
+        }
+    }
+  }
 }
 
 template <typename T, int G, int NG, bool S_REAL>
-int launch_packed(FwdParams p, cudaStream_t st) {
+int launch_packed(FwdParams p, bool state_only, cudaStream_t st) {
   constexpr int CPW = 32 / NG;
   constexpr int NP = NG * G;
   const int sw = S_REAL ? 1 : 4;
@@ -548,7 +601,7 @@ int launch_packed(FwdParams p, cudaStream_t st) {
   const int64_t n_s = n_delta * (S_REAL ? 1 : 4);
   const size_t bytes = 2 * plane + (kWiden ? size_t(n_delta + n_s) * sizeof(float) : 0);
   float* ws = nullptr;
-  cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&ws), bytes, st);
+  cudaError_t e = scratch_alloc(reinterpret_cast<void**>(&ws), bytes, st);
   if (e != cudaSuccess)
     return fail(MQC_ERR_CUDA, "mqc_ssm_scan_fwd: scratch allocation of %zu bytes: %s", bytes,
                 cudaGetErrorString(e));
@@ -559,9 +612,9 @@ int launch_packed(FwdParams p, cudaStream_t st) {
   const int64_t items = rows * (G / 2) * NG;
   const int64_t want = (items + kPackThreads - 1) / kPackThreads;
   const int pgrid = int(want < int64_t(sms) * 16 ? want : int64_t(sms) * 16);
-  pack_bc_kernel<T><<<pgrid, kPackThreads, 0, st>>>(static_cast<const T*>(p.Bm),
-                                                     static_cast<const T*>(p.Cm), Bp, Cp, rows,
-                                                     p.N, ng_log2, G / 2);
+  pack_bc_kernel<T><<<pgrid, kPackThreads, 0, st>>>(
+      static_cast<const T*>(p.Bm), state_only ? nullptr : static_cast<const T*>(p.Cm), Bp, Cp,
+      rows, p.N, ng_log2, G / 2);
   int rc = check_launch("mqc_ssm_scan_fwd(pack)");
   if (kWiden && rc == MQC_OK) {
     float* dw = Cp + plane / sizeof(float);
@@ -578,10 +631,11 @@ int launch_packed(FwdParams p, cudaStream_t st) {
     p.cpb = cpb;
     p.tc = tc;
     const bool ck = p.ckpt != nullptr, dt = p.dst != 0;
-    auto kern = ck ? (dt ? scan_fwd_packed_kernel<T, G, NG, S_REAL, true, true>
-                         : scan_fwd_packed_kernel<T, G, NG, S_REAL, true, false>)
-                   : (dt ? scan_fwd_packed_kernel<T, G, NG, S_REAL, false, true>
-                         : scan_fwd_packed_kernel<T, G, NG, S_REAL, false, false>);
+    auto kern = state_only ? scan_fwd_packed_kernel<T, G, NG, S_REAL, false, false, true>
+                : ck ? (dt ? scan_fwd_packed_kernel<T, G, NG, S_REAL, true, true, false>
+                           : scan_fwd_packed_kernel<T, G, NG, S_REAL, true, false, false>)
+                     : (dt ? scan_fwd_packed_kernel<T, G, NG, S_REAL, false, true, false>
+                           : scan_fwd_packed_kernel<T, G, NG, S_REAL, false, false, false>);
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) {
       rc = fail(MQC_ERR_CUDA, "mqc_ssm_scan_fwd: smem attribute (%zu B): %s", smem,
@@ -592,23 +646,23 @@ int launch_packed(FwdParams p, cudaStream_t st) {
       rc = check_launch("mqc_ssm_scan_fwd(packed)");
     }
   }
-  cudaFreeAsync(ws, st);
+  scratch_free(ws, st);
   return rc;
 }
 
 template <typename T, int G, bool S_REAL>
-int dispatch_packed_g(const FwdParams& p, cudaStream_t st) {
+int dispatch_packed_g(const FwdParams& p, bool so, cudaStream_t st) {
   // NG = lanes per channel, the power of two covering ceil(N / G), at most 32
   const int need = (p.N + G - 1) / G;
   int ng = 1;
   while (ng < need) ng <<= 1;
   switch (ng) {
-    case 1: return launch_packed<T, G, 1, S_REAL>(p, st);
-    case 2: return launch_packed<T, G, 2, S_REAL>(p, st);
-    case 4: return launch_packed<T, G, 4, S_REAL>(p, st);
-    case 8: return launch_packed<T, G, 8, S_REAL>(p, st);
-    case 16: return launch_packed<T, G, 16, S_REAL>(p, st);
-    case 32: return launch_packed<T, G, 32, S_REAL>(p, st);
+    case 1: return launch_packed<T, G, 1, S_REAL>(p, so, st);
+    case 2: return launch_packed<T, G, 2, S_REAL>(p, so, st);
+    case 4: return launch_packed<T, G, 4, S_REAL>(p, so, st);
+    case 8: return launch_packed<T, G, 8, S_REAL>(p, so, st);
+    case 16: return launch_packed<T, G, 16, S_REAL>(p, so, st);
+    case 32: return launch_packed<T, G, 32, S_REAL>(p, so, st);
     default:
       return fail(MQC_ERR_UNSUPPORTED, "mqc_ssm_scan_fwd: d_state=%d (supported 1..%d)", p.N,
                   32 * G);
@@ -616,17 +670,26 @@ int dispatch_packed_g(const FwdParams& p, cudaStream_t st) {
 }
 
 template <typename T, bool S_REAL>
-int dispatch_packed_t(const FwdParams& p, cudaStream_t st) {
-  return dispatch_packed_g<T, 8, S_REAL>(p, st);
+int dispatch_packed_t(const FwdParams& p, bool so, cudaStream_t st) {
+  return dispatch_packed_g<T, 8, S_REAL>(p, so, st);
+}
+
+int dispatch_packed(const FwdParams& p, int dtype, bool s_real, bool so, cudaStream_t st) {
+  if (dtype == MQC_DTYPE_F32)
+    return s_real ? dispatch_packed_t<float, true>(p, so, st)
+                  : dispatch_packed_t<float, false>(p, so, st);
+  return s_real ? dispatch_packed_t<__nv_bfloat16, true>(p, so, st)
+                : dispatch_packed_t<__nv_bfloat16, false>(p, so, st);
 }
 
 }  // namespace
 
 int dispatch_shared_packed(const FwdParams& p, int dtype, bool s_real, cudaStream_t st) {
-  if (dtype == MQC_DTYPE_F32)
-    return s_real ? dispatch_packed_t<float, true>(p, st) : dispatch_packed_t<float, false>(p, st);
-  return s_real ? dispatch_packed_t<__nv_bfloat16, true>(p, st)
-                : dispatch_packed_t<__nv_bfloat16, false>(p, st);
+  return dispatch_packed(p, dtype, s_real, false, st);
+}
+
+int dispatch_state_only_packed(const FwdParams& p, int dtype, bool s_real, cudaStream_t st) {
+  return dispatch_packed(p, dtype, s_real, true, st);
 }
 
 }  // namespace scan
