@@ -3,9 +3,8 @@
 //
 // Reference: quaternion_layer_norm_fused / quaternion_layer_norm_reference,
 // mambaqc/kernels/quaternion_norm.py:119-174 and :219-245. One CTA owns one row
-// of d_model quaternions; each thread keeps VPT quaternions of the row in
-// registers (16-byte coalesced loads), so the row is read from HBM once and
-// written once. Mean and variance of the norms are two-pass over registers
+// of d_model quaternions, staged in shared memory by cp.async (16-byte coalesced
+// copies), so the row is read from HBM once and written once. Mean and variance of the norms are two-pass over registers
 // (mean first, then centred squares), with warp-shuffle + shared-memory sums.
 #include "mqc_common.cuh"
 #include "mqc_host.h"
@@ -31,26 +30,41 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return s;
 }
 
+// 8-byte asynchronous global -> shared copy (one bf16 quaternion).
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_addr(dst)), "l"(src)
+               : "memory");
+}
+
+// The row is staged in shared memory with cp.async (no registers held while it
+// is in flight), so many rows per SM are in flight at once; each thread then
+// works on quaternions d = threadIdx.x + j * blockDim.x of the staged row.
 template <typename T>
 __global__ void __launch_bounds__(kMaxRowThreads) qln_fwd_kernel(
     const T* __restrict__ q, const float* __restrict__ gamma, const float* __restrict__ beta,
     T* __restrict__ out, float* __restrict__ mean_out, float* __restrict__ rstd_out, int D,
     float eps, int pad_lanes) {
   __shared__ float red[32];
+  extern __shared__ __align__(16) unsigned char srow_raw[];
+  T* srow = reinterpret_cast<T*>(srow_raw);
   const int64_t row = blockIdx.x;
   const T* qr = q + row * D * 4;
   T* orow = out + row * D * 4;
-  float4 v[kVpt];
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    if constexpr (sizeof(T) == 4) cp_async16(srow + d * 4, qr + d * 4, true);
+    else cp_async8(srow + d * 4, qr + d * 4);
+  }
+  cp_async_commit();
+  cp_async_wait_all();
+  __syncthreads();
   float nrm[kVpt];
   float s = 0.f;
 #pragma unroll
   for (int j = 0; j < kVpt; ++j) {
     const int d = threadIdx.x + j * blockDim.x;
-    v[j] = f4_zero();
     nrm[j] = 0.f;
     if (d < D) {
-      v[j] = QIO<T>::ld_stream(qr + d * 4);
-      const float4 a = v[j];
+      const float4 a = QIO<T>::lds(srow + d * 4);
       nrm[j] = sqrtf(fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, a.w * a.w))) + eps);
       s += nrm[j];
     }
@@ -86,11 +100,12 @@ __global__ void __launch_bounds__(kMaxRowThreads) qln_fwd_kernel(
       const float nh = (nrm[j] - mu) * rsd;
       const float g = __ldg(gamma + d) * nh * (1.f / (nrm[j] + eps));
       const float4 bt = QIO<float>::ld(beta + d * 4);
+      const float4 v = QIO<T>::lds(srow + d * 4);
       float4 o;
-      o.x = fmaf(g, v[j].x, bt.x);
-      o.y = fmaf(g, v[j].y, bt.y);
-      o.z = fmaf(g, v[j].z, bt.z);
-      o.w = fmaf(g, v[j].w, bt.w);
+      o.x = fmaf(g, v.x, bt.x);
+      o.y = fmaf(g, v.y, bt.y);
+      o.z = fmaf(g, v.z, bt.z);
+      o.w = fmaf(g, v.w, bt.w);
       QIO<T>::st_stream(orow + d * 4, o);
     }
   }
@@ -251,12 +266,25 @@ extern "C" int mqc_qln_fwd(const void* q, const float* gamma, const float* beta,
     pad = block - D;
   }
   cudaStream_t st = as_stream(stream);
+  const size_t srow_bytes = size_t(D) * 4 * (dtype == MQC_DTYPE_F32 ? 4 : 2);
+  if (srow_bytes > 48 * 1024) {
+    cudaError_t e = dtype == MQC_DTYPE_F32
+                        ? cudaFuncSetAttribute(qln_fwd_kernel<float>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               int(srow_bytes))
+                        : cudaFuncSetAttribute(qln_fwd_kernel<__nv_bfloat16>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               int(srow_bytes));
+    if (e != cudaSuccess)
+      return fail(MQC_ERR_CUDA, "mqc_qln_fwd: smem attribute (%zu B): %s", srow_bytes,
+                  cudaGetErrorString(e));
+  }
   if (dtype == MQC_DTYPE_F32) {
-    qln_fwd_kernel<float><<<unsigned(rows), threads, 0, st>>>(
+    qln_fwd_kernel<float><<<unsigned(rows), threads, srow_bytes, st>>>(
         static_cast<const float*>(q), gamma, beta, static_cast<float*>(out), mean, rstd, D, eps,
         pad);
   } else {
-    qln_fwd_kernel<__nv_bfloat16><<<unsigned(rows), threads, 0, st>>>(
+    qln_fwd_kernel<__nv_bfloat16><<<unsigned(rows), threads, srow_bytes, st>>>(
         static_cast<const __nv_bfloat16*>(q), gamma, beta, static_cast<__nv_bfloat16*>(out), mean,
         rstd, D, eps, pad);
   }
