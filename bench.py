@@ -63,6 +63,9 @@ def parse_args():
                     help="skip the forward+backward and per-channel-layout sub-measurements")
     ap.add_argument("--only", choices=["fwd_bwd", "perchannel"], default=None,
                     help="run only this sub-measurement and print it (profiling aid)")
+    ap.add_argument("--segments", type=int, default=4,
+                    help="config5 on >1 GPU: time segments whose all-gather overlaps the "
+                         "scan of the next segment")
     ap.add_argument("--workload", choices=["config3", "config5", "config2"], default="config3",
                     help="config5: B=1, T=65536, D=1536, N=64, bf16, channel-sharded over the "
                          "GPUs with an NCCL all-gather of y (strong scaling)")
@@ -517,11 +520,13 @@ def run_config5(args, world, rank, local):
     lam[..., 1:] = 0.5 * torch.randn(dl, STATE, 3, generator=g, device=dev)
     Dk = torch.ones(dl, device=dev)
     nc = auto_time_chunks(1, C5_SEQ, dl, STATE, dev)
+    segs = args.segments if world > 1 else 1
     stream = torch.cuda.current_stream(dev)
     out = {}
 
     def step():
-        out["y"] = ssm_scan_cayley_channel_sharded(delta, lam, Bm, Cm, x, Dk, time_chunks=nc)
+        out["y"] = ssm_scan_cayley_channel_sharded(
+            delta, lam, Bm, Cm, x, Dk, time_chunks="auto" if segs > 1 else nc, segments=segs)
 
     def scan_only():
         out["yl"] = ssm_scan_cayley(delta, lam, Bm, Cm, x, Dk, time_chunks=nc)
@@ -546,8 +551,10 @@ def run_config5(args, world, rank, local):
             "dtype": "bf16 inputs, f32 state", "data": "synthetic (seeded, config-3 distributions)",
             "config": {"workload": "config5_channel_sharded", "batch": 1, "seq_len": C5_SEQ,
                        "d_inner": CHANNELS, "d_state": STATE, "channels_per_gpu": dl,
-                       "time_chunks": nc, "parallelism": f"channel shards x{world}, "
-                                                         "NCCL all_gather_into_tensor of y"},
+                       "time_chunks": nc, "segments": segs,
+                       "parallelism": f"channel shards x{world}, NCCL all_gather_into_tensor "
+                                      f"of y per time segment ({segs}), overlapped with the "
+                                      "scan of the next segment"},
             "scan_only_ms": ms_scan_max,
             "gather_and_reassembly_ms": ms_max - ms_scan_max,
             "scan_fp32_tflops_per_gpu": elems / world * FLOPS_PER_ELEM_SREAL / (ms_scan_max / 1e3) / 1e12,

@@ -28,8 +28,8 @@ def _inputs():
     return [t.double() for t in (delta, lam, Bm, Cm, x, Dk)]
 
 
-def _oracle_scan(d, L, Bm, Cm, s, Dk):
-    return ref.ssm_scan_cayley(d, L, Bm, Cm, s, Dk)[0]
+def _oracle_scan(d, L, Bm, Cm, s, Dk, h0=None):
+    return ref.ssm_scan_cayley(d, L, Bm, Cm, s, Dk, h0=h0)
 
 
 def _worker(rank, port, q):
@@ -37,11 +37,12 @@ def _worker(rank, port, q):
     dist.init_process_group("gloo", rank=rank, world_size=WORLD)
     try:
         delta, lam, Bm, Cm, x, Dk = _inputs()
-        y = ssm_scan_cayley_channel_sharded(
-            channel_shard(delta, rank, WORLD, 2), channel_shard(lam, rank, WORLD, 0), Bm, Cm,
-            channel_shard(x, rank, WORLD, 2), channel_shard(Dk, rank, WORLD, 0),
-            scan_fn=_oracle_scan)
-        q.put((rank, y))
+        shard = (channel_shard(delta, rank, WORLD, 2), channel_shard(lam, rank, WORLD, 0), Bm, Cm,
+                 channel_shard(x, rank, WORLD, 2), channel_shard(Dk, rank, WORLD, 0))
+        y1 = ssm_scan_cayley_channel_sharded(*shard, scan_fn=_oracle_scan)
+        # three time segments, each scanned from the previous one's final state
+        y3 = ssm_scan_cayley_channel_sharded(*shard, scan_fn=_oracle_scan, segments=3)
+        q.put((rank, (y1, y3)))
     finally:
         dist.destroy_process_group()
 
@@ -63,9 +64,11 @@ def test_channel_sharded_scan_matches_unsharded():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    full = _oracle_scan(*_inputs())
+    full = _oracle_scan(*_inputs())[0]
     for r in range(WORLD):
-        assert torch.equal(results[r], full)
+        y1, y3 = results[r]
+        assert torch.equal(y1, full)
+        assert torch.allclose(y3, full, rtol=1e-12, atol=1e-12)
 
 
 def test_channel_shard_rejects_uneven_split():
