@@ -19,8 +19,10 @@
 // a per-warp shared-memory slice, the slices are summed over the CTA's warps in a
 // fixed order at the end of each sub-block, and the CTA's sum is added to global
 // fp32 accumulators with one vector atomic per (t, n, tensor).
+#include <cstdlib>
 #include <type_traits>
 
+#include "packed_math.cuh"
 #include "ssm_scan_common.cuh"
 
 namespace mqc {
@@ -469,6 +471,373 @@ __global__ void __launch_bounds__(32 * bwd_warps(G))
   }
 }
 
+// ---------------------------------------------------------------------------
+// Packed backward: channel-shared B/C with d_state <= 2*NG, G = 2 states per lane
+// forming one pair (ng, ng + NG), on packed two-lane FP32 (packed_math.cuh).
+// Same algorithm as ssm_scan_bwd_kernel:
+//  * B/C come from the pair-interleaved pre-pass (pack_bc_pairs);
+//  * delta, x (or S) and dy are fp32 (bf16 inputs widened first);
+//  * all inputs of a sub-block are staged one sub-block ahead with cp.async;
+//  * the per-warp dB/dC slices are pair-interleaved and are un-interleaved only
+//    in the per-CTA summation.
+constexpr int kPbWarps = 8;
+
+struct PbLayout {
+  size_t slices, bc, dl, sx, gy, hst, stage, total;
+};
+
+// [slices: warps x kSub x 2 x NG pairs x 8 f32] then 2 stages of
+// [bc: kSub x 2 x NG x 8 f32 | dl: kSub x cpb f32 | sx: kSub x cpb x sw f32 |
+//  gy: kSub x cpb x 4 f32 | hst: warps x 32 lanes x 8 f32]; stage offsets are
+// relative to the stage.
+__host__ __device__ inline PbLayout pb_layout(int NG, int cpb, bool s_real) {
+  PbLayout L;
+  L.slices = size_t(kPbWarps) * kSub * 2 * NG * 32;
+  L.bc = 0;
+  size_t o = size_t(kSub) * 2 * NG * 32;
+  L.dl = o;
+  o = align_up(o + size_t(kSub) * cpb * 4, 16);
+  L.sx = o;
+  o = align_up(o + size_t(kSub) * cpb * (s_real ? 4 : 16), 16);
+  L.gy = o;
+  o += size_t(kSub) * cpb * 16;
+  L.hst = o;
+  o += size_t(kPbWarps) * 32 * 32;
+  L.stage = o;
+  L.total = L.slices + 2 * o;
+  return L;
+}
+
+template <typename T, int NG, bool S_REAL>
+__global__ void __launch_bounds__(32 * kPbWarps)
+    ssm_scan_bwd_packed_kernel(const BwdParams p, const float* __restrict__ Bp,
+                               const float* __restrict__ Cp, const float* __restrict__ dlf,
+                               const float* __restrict__ sf, const float* __restrict__ dyf) {
+  using namespace ::mqc::pk;
+  constexpr int CPW = 32 / NG;
+  constexpr int NV = S_REAL ? 2 : 8;  // per-(t, channel) sums: ddelta, dS (padded)
+  constexpr int V = kSub * NV;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int cpb = p.cpb;
+  const PbLayout L = pb_layout(NG, cpb, S_REAL);
+  float* slices = reinterpret_cast<float*>(smem_raw);
+  unsigned char* stage_base = smem_raw + L.slices;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ng = lane % NG;
+  const int cl = warp * CPW + lane / NG;
+  const int b = blockIdx.y;
+  const int c_raw = blockIdx.x * cpb + cl;
+  const bool active = cl < cpb && c_raw < p.D;
+  const int c = active ? c_raw : 0;
+  const int T_ = p.T, D = p.D, N = p.N;
+  const int n0 = ng, n1 = ng + NG;
+  const bool ok0 = active && n0 < N, ok1 = active && n1 < N;
+  float* slice = slices + size_t(warp) * kSub * 2 * NG * 8;
+
+  LamPair lc;
+  QPair carry, dlam = qp_zero();
+  {
+    LamConst k0{0.f, 0.f, 0.f, 0.f, 0.f}, k1{0.f, 0.f, 0.f, 0.f, 0.f};
+    float4 c0 = f4_zero(), c1 = f4_zero();
+    if (ok0) {
+      k0 = make_lam_const(QIO<float>::ld(p.lam + (int64_t(c) * N + n0) * 4));
+      if (p.dhT != nullptr) c0 = QIO<float>::ld(p.dhT + ((int64_t(b) * D + c) * N + n0) * 4);
+    }
+    if (ok1) {
+      k1 = make_lam_const(QIO<float>::ld(p.lam + (int64_t(c) * N + n1) * 4));
+      if (p.dhT != nullptr) c1 = QIO<float>::ld(p.dhT + ((int64_t(b) * D + c) * N + n1) * 4);
+    }
+    lc = LamPair{make_float2(k0.lr, k1.lr), make_float2(k0.li, k1.li),
+                 make_float2(k0.lj, k1.lj), make_float2(k0.lk, k1.lk), make_float2(k0.m, k1.m)};
+    carry = qp_from(c0, c1);  // conj(q_{t+1}) (x) lambda_{t+1}
+  }
+  const QPair lq{lc.lr, lc.li, lc.lj, lc.lk};
+  const float eps = p.eps;
+
+  auto issue_stage = [&](int sb, int buf) {
+    unsigned char* st = stage_base + size_t(buf) * L.stage;
+    const int t0 = sb * kSub;
+    const int len = min(kSub, T_ - t0);
+    float* sbc = reinterpret_cast<float*>(st + L.bc);
+    // packed rows: per step and matrix NG pairs x 8 floats = 2*NG chunks of 16 B
+    for (int e = threadIdx.x; e < len * 4 * NG; e += blockDim.x) {
+      const int tt = e / (4 * NG), r = e % (4 * NG), which = r / (2 * NG), k = r % (2 * NG);
+      const float* src = (which ? Cp : Bp) + (int64_t(b) * T_ + t0 + tt) * NG * 8 + k * 4;
+      cp_async16(sbc + (tt * 2 + which) * NG * 8 + k * 4, src, true);
+    }
+    float* sdl = reinterpret_cast<float*>(st + L.dl);
+    float* ssx = reinterpret_cast<float*>(st + L.sx);
+    float* sgy = reinterpret_cast<float*>(st + L.gy);
+    for (int e = threadIdx.x; e < len * cpb; e += blockDim.x) {
+      const int tt = e / cpb, cc = e % cpb;
+      const int ch = blockIdx.x * cpb + cc;
+      const bool v = ch < D;
+      const int64_t row = v ? (int64_t(b) * T_ + t0 + tt) * D + ch : 0;
+      cp_async4(sdl + e, dlf + row, v);
+      if (S_REAL) cp_async4(ssx + e, sf + row, v);
+      else cp_async16(ssx + e * 4, sf + row * 4, v);
+      cp_async16(sgy + e * 4, dyf + row * 4, v);
+    }
+    // the lane's two start states (checkpoint, h0 or zero), state-wise
+    float* shst = reinterpret_cast<float*>(st + L.hst) + (warp * 32 + lane) * 8;
+#pragma unroll
+    for (int e2 = 0; e2 < 2; ++e2) {
+      const int n = e2 ? n1 : n0;
+      const bool ok = e2 ? ok1 : ok0;
+      const bool v = ok && (sb > 0 || p.h0 != nullptr);
+      const float* src = p.lam;
+      if (v)
+        src = sb > 0 ? p.ckpt + ((int64_t(b) * p.nck + (sb - 1)) * D + c) * int64_t(N) * 4 +
+                           int64_t(n) * 4
+                     : p.h0 + ((int64_t(b) * D + c) * N + n) * 4;
+      cp_async16(shst + e2 * 4, src, v);
+    }
+    cp_async_commit();
+  };
+
+  const int nsub = (T_ + kSub - 1) / kSub;
+  issue_stage(nsub - 1, 0);
+  cp_async_wait_all();
+  __syncthreads();
+  for (int sb = nsub - 1; sb >= 0; --sb) {
+    const int t0 = sb * kSub;
+    const int len = min(kSub, T_ - t0);
+    const int64_t row0 = (int64_t(b) * T_ + t0) * D + c;  // (b, t0, c) in [B,T,D]
+    const int buf = (nsub - 1 - sb) & 1;
+    const unsigned char* stg = stage_base + size_t(buf) * L.stage;
+    const float* sbc = reinterpret_cast<const float*>(stg + L.bc) + ng * 8;
+    const float* sdl = reinterpret_cast<const float*>(stg + L.dl) + cl;
+    const float* ssx = reinterpret_cast<const float*>(stg + L.sx);
+    const float4* sgy = reinterpret_cast<const float4*>(stg + L.gy) + cl;
+    if (sb > 0) issue_stage(sb - 1, buf ^ 1);
+    auto ld_pair = [&](int tt, int which) -> QPair {
+      const float* q = sbc + (tt * 2 + which) * NG * 8;
+      const float4 u = *reinterpret_cast<const float4*>(q);
+      const float4 w = *reinterpret_cast<const float4*>(q + 4);
+      return QPair{make_float2(u.x, u.y), make_float2(u.z, u.w), make_float2(w.x, w.y),
+                   make_float2(w.z, w.w)};
+    };
+    auto in_s = [&](int tt) -> float4 {
+      if (S_REAL) return make_float4(ssx[tt * cpb + cl], 0.f, 0.f, 0.f);
+      return reinterpret_cast<const float4*>(ssx)[tt * cpb + cl];
+    };
+    const float* shst = reinterpret_cast<const float*>(stg + L.hst) + (warp * 32 + lane) * 8;
+    const QPair hstart = qp_from(*reinterpret_cast<const float4*>(shst),
+                                 *reinterpret_cast<const float4*>(shst + 4));
+    // ---- recompute the sub-block's states forward (registers)
+    QPair hs[kSub];
+    {
+      QPair h = hstart;
+#pragma unroll
+      for (int tt = 0; tt < kSub; ++tt) {
+        if (tt < len) {
+          const float dl = sdl[tt * cpb];
+          const float4 sv = in_s(tt);
+          const QPair Bq = ld_pair(tt, 0);
+          const QPair qv = cayley_pair(dl, dl * dl, lc, eps);
+          QPair inj;
+          if (S_REAL) {
+            const float2 s2 = bc2(sv.x);
+            inj = QPair{mul2(s2, Bq.x), mul2(s2, Bq.y), mul2(s2, Bq.z), mul2(s2, Bq.w)};
+          } else {
+            inj = qp_mul_bcast(Bq, sv);
+          }
+          h = qp_mul_acc(qv, h, inj);
+        }
+        hs[tt] = h;
+      }
+    }
+    // ---- adjoint, backwards over the sub-block
+    float part[V];
+#pragma unroll
+    for (int e = 0; e < V; ++e) part[e] = 0.f;
+#pragma unroll
+    for (int tt = kSub - 1; tt >= 0; --tt) {
+      if (tt < len) {
+        const int t = t0 + tt;
+        const float dl = sdl[tt * cpb];
+        const float4 sv = in_s(tt);
+        const float4 gy = sgy[tt * cpb];
+        float4 psum = f4_zero();
+        if (ng == 0 && active) {  // skip term D * dy, counted once per channel
+          const float dsk = __ldg(p.dskip + int64_t(b) * p.dsb + int64_t(t) * p.dst +
+                                  int64_t(c) * p.dsd);
+          psum = make_float4(dsk * gy.x, dsk * gy.y, dsk * gy.z, dsk * gy.w);
+        }
+        const QPair Bq = ld_pair(tt, 0), Cq = ld_pair(tt, 1);
+        const QPair hcur = hs[tt];
+        const QPair hprev = tt > 0 ? hs[tt > 0 ? tt - 1 : 0] : hstart;
+        // lambda_t = conj(C_t) (x) dy_t + conj(q_{t+1}) (x) lambda_{t+1}
+        const QPair cg = qp_mul_bcast(qp_conj(Cq), gy);
+        const QPair lam{add2(cg.x, carry.x), add2(cg.y, carry.y), add2(cg.z, carry.z),
+                        add2(cg.w, carry.w)};
+        const QPair qv = cayley_pair(dl, dl * dl, lc, eps);
+        const QPair dq = qp_mul_acc(lam, qp_conj(hprev), qp_zero());
+        const float2 d2 = bc2(dl);
+        const QPair z{mul2(d2, lq.x), mul2(d2, lq.y), mul2(d2, lq.z), mul2(d2, lq.w)};
+        const QPair dz = cayley_vjp_pair(z, dq, eps);
+        const float2 pdp = qp_dot(dz, lq);
+        dlam = QPair{fma2(d2, dz.x, dlam.x), fma2(d2, dz.y, dlam.y), fma2(d2, dz.z, dlam.z),
+                     fma2(d2, dz.w, dlam.w)};
+        QPair dB;
+        if (S_REAL) {
+          const float2 s2 = bc2(sv.x);
+          dB = QPair{mul2(s2, lam.x), mul2(s2, lam.y), mul2(s2, lam.z), mul2(s2, lam.w)};
+          const float2 bl = qp_dot(Bq, lam);
+          psum.x += bl.x + bl.y;
+        } else {
+          dB = qp_mul_bcast(lam, qconj(sv));
+          const QPair pl = qp_mul_acc(qp_conj(Bq), lam, qp_zero());
+          psum.x += pl.x.x + pl.x.y;
+          psum.y += pl.y.x + pl.y.y;
+          psum.z += pl.z.x + pl.z.y;
+          psum.w += pl.w.x + pl.w.y;
+        }
+        QPair dC = qp_bmul(gy, qp_conj(hcur));
+        // sum over the CPW channels of this warp (lanes ng + NG*k hold the same states)
+#pragma unroll
+        for (int m = NG; m < 32; m <<= 1) {
+          float* fb = reinterpret_cast<float*>(&dB);
+          float* fc = reinterpret_cast<float*>(&dC);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            fb[k] += __shfl_xor_sync(0xffffffffu, fb[k], m);
+            fc[k] += __shfl_xor_sync(0xffffffffu, fc[k], m);
+          }
+        }
+        // the warp's first channel lanes write every (tt, pair) slot, so the slice
+        // needs no clearing
+        if (lane < NG) {
+          float4* sbw = reinterpret_cast<float4*>(slice + ((tt * 2) * NG + ng) * 8);
+          sbw[0] = make_float4(dB.x.x, dB.x.y, dB.y.x, dB.y.y);
+          sbw[1] = make_float4(dB.z.x, dB.z.y, dB.w.x, dB.w.y);
+          float4* scw = reinterpret_cast<float4*>(slice + ((tt * 2 + 1) * NG + ng) * 8);
+          scw[0] = make_float4(dC.x.x, dC.x.y, dC.y.x, dC.y.y);
+          scw[1] = make_float4(dC.z.x, dC.z.y, dC.w.x, dC.w.y);
+        }
+        carry = qp_mul_acc(qp_conj(qv), lam, qp_zero());
+        part[tt * NV + 0] = pdp.x + pdp.y;
+        part[tt * NV + 1] = psum.x;
+        if (!S_REAL) {
+          part[tt * NV + 2] = psum.y;
+          part[tt * NV + 3] = psum.z;
+          part[tt * NV + 4] = psum.w;
+        }
+      }
+    }
+    // ---- per-(t, channel) sums over the NG lanes of the channel, then stores
+    {
+      const int base = reduce_scatter<V, NG>(part, ng);
+      constexpr int W = (V / NG) > 0 ? (V / NG) : 1;
+      constexpr int kLogV = (V >= 64) ? 6 : (V >= 32 ? 5 : (V >= 16 ? 4 : (V >= 8 ? 3 : 1)));
+      const bool writer = active && (NG <= V || (ng >> kLogV) == 0);
+#pragma unroll
+      for (int j = 0; j < W; ++j) {
+        const int idx = base + j;
+        const int tt = idx / NV, k = idx % NV;
+        if (writer && tt < len) {
+          const int64_t row = row0 + int64_t(tt) * D;
+          if (k == 0) {
+            QIO<T>::st1(static_cast<T*>(p.ddelta) + row, part[j]);
+          } else if (S_REAL) {
+            QIO<T>::st1(static_cast<T*>(p.ds) + row, part[j]);
+          } else if (k <= 4) {
+            QIO<T>::st1(static_cast<T*>(p.ds) + row * 4 + (k - 1), part[j]);
+          }
+        }
+      }
+    }
+    // ---- sum the warps' slices (fixed order) and add the CTA's share to global
+    __syncthreads();
+    float* dBg = static_cast<float*>(p.dB);
+    float* dCg = static_cast<float*>(p.dC);
+    for (int e = threadIdx.x; e < len * 2 * NG; e += blockDim.x) {
+      const int pg = e % NG, tw = e / NG;  // tw = tt * 2 + which
+      const float* s0 = slices + size_t(tw * NG + pg) * 8;
+      float4 u = *reinterpret_cast<const float4*>(s0);
+      float4 w = *reinterpret_cast<const float4*>(s0 + 4);
+      for (int k = 1; k < kPbWarps; ++k) {
+        const float* sk = s0 + size_t(k) * kSub * 2 * NG * 8;
+        const float4 a = *reinterpret_cast<const float4*>(sk);
+        const float4 a2 = *reinterpret_cast<const float4*>(sk + 4);
+        u.x += a.x; u.y += a.y; u.z += a.z; u.w += a.w;
+        w.x += a2.x; w.y += a2.y; w.z += a2.z; w.w += a2.w;
+      }
+      // u = (x0, x1, y0, y1), w = (z0, z1, w0, w1): states pg and pg + NG
+      float* dst = ((tw & 1) ? dCg : dBg) + (int64_t(b) * T_ + t0 + (tw >> 1)) * N * 4;
+      if (pg < N) atomicAdd(reinterpret_cast<float4*>(dst + pg * 4), make_float4(u.x, u.z, w.x, w.z));
+      if (pg + NG < N)
+        atomicAdd(reinterpret_cast<float4*>(dst + (pg + NG) * 4), make_float4(u.y, u.w, w.y, w.w));
+    }
+    cp_async_wait_all();
+    __syncthreads();  // slices free; next stage visible
+  }
+
+  if (ok0) {
+    const int64_t off = ((int64_t(b) * D + c) * N + n0) * 4;
+    QIO<float>::st(p.dlam_part + off, qp_half(dlam, 0));
+    if (p.dh0 != nullptr) QIO<float>::st(p.dh0 + off, qp_half(carry, 0));
+  }
+  if (ok1) {
+    const int64_t off = ((int64_t(b) * D + c) * N + n1) * 4;
+    QIO<float>::st(p.dlam_part + off, qp_half(dlam, 1));
+    if (p.dh0 != nullptr) QIO<float>::st(p.dh0 + off, qp_half(carry, 1));
+  }
+}
+
+template <typename T, int NG, bool S_REAL>
+int launch_bwd_packed(BwdParams p, cudaStream_t st) {
+  constexpr int CPW = 32 / NG;
+  constexpr int SW = S_REAL ? 1 : 4;
+  p.cpb = kPbWarps * CPW;
+  const PbLayout L = pb_layout(NG, p.cpb, S_REAL);
+  if (L.total > size_t(kMaxBwdSmem))
+    return fail(MQC_ERR_UNSUPPORTED, "mqc_ssm_scan_bwd: packed staging does not fit");
+  constexpr bool kWiden = !std::is_same<T, float>::value;
+  const int64_t rows = int64_t(p.B) * p.T;
+  const size_t plane = size_t(rows) * NG * 8 * sizeof(float);
+  const int64_t n_delta = rows * p.D;
+  const size_t bytes = 2 * plane + (kWiden ? size_t(n_delta) * (1 + SW + 4) * sizeof(float) : 0);
+  float* ws = nullptr;
+  cudaError_t e = scratch_alloc(reinterpret_cast<void**>(&ws), bytes, st);
+  if (e != cudaSuccess)
+    return fail(MQC_ERR_CUDA, "mqc_ssm_scan_bwd: scratch allocation of %zu bytes: %s", bytes,
+                cudaGetErrorString(e));
+  float* Bp = ws;
+  float* Cp = ws + plane / sizeof(float);
+  const float* dlf = static_cast<const float*>(p.delta);
+  const float* sf = static_cast<const float*>(p.s);
+  const float* dyf = static_cast<const float*>(p.dy);
+  int rc = pack_bc_pairs(p.Bm, p.Cm, Bp, Cp, rows, p.N, NG, 2,
+                         kWiden ? MQC_DTYPE_BF16 : MQC_DTYPE_F32, st);
+  if (kWiden && rc == MQC_OK) {
+    float* w0 = Cp + plane / sizeof(float);
+    float* w1 = w0 + n_delta;
+    float* w2 = w1 + n_delta * SW;
+    rc = widen_bf16_to_f32(p.delta, w0, n_delta, st);
+    if (rc == MQC_OK) rc = widen_bf16_to_f32(p.s, w1, n_delta * SW, st);
+    if (rc == MQC_OK) rc = widen_bf16_to_f32(p.dy, w2, n_delta * 4, st);
+    dlf = w0;
+    sf = w1;
+    dyf = w2;
+  }
+  if (rc == MQC_OK) {
+    auto kern = ssm_scan_bwd_packed_kernel<T, NG, S_REAL>;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L.total));
+    if (e != cudaSuccess) {
+      rc = fail(MQC_ERR_CUDA, "mqc_ssm_scan_bwd: smem attribute (%zu B): %s", L.total,
+                cudaGetErrorString(e));
+    } else {
+      dim3 grid{unsigned((p.D + p.cpb - 1) / p.cpb), unsigned(p.B), 1u};
+      kern<<<grid, 32 * kPbWarps, L.total, st>>>(p, Bp, Cp, dlf, sf, dyf);
+      rc = check_launch("mqc_ssm_scan_bwd(packed)");
+    }
+  }
+  scratch_free(ws, st);
+  return rc;
+}
+
 template <typename T, int G, int NG, bool BC_SHARED, bool S_REAL>
 int launch_bwd(BwdParams p, cudaStream_t st) {
   constexpr int kBwdWarps = bwd_warps(G);
@@ -494,6 +863,16 @@ int launch_bwd(BwdParams p, cudaStream_t st) {
   return check_launch("mqc_ssm_scan_bwd");
 }
 
+// The packed kernel serves channel-shared B/C up to N = 64 unless MQC_SCAN_IMPL
+// selects another implementation (the unpacked kernel is then used).
+inline bool use_packed_bwd() {
+  static const bool packed = [] {
+    const char* v = getenv("MQC_SCAN_IMPL");
+    return v == nullptr || v[0] == '\0';
+  }();
+  return packed;
+}
+
 template <typename T, bool BC_SHARED, bool S_REAL>
 int dispatch_bwd_ng(const BwdParams& p, cudaStream_t st) {
   // G = 2 states per lane up to N = 64 (NG <= 32), then G = 4 / 8
@@ -501,6 +880,16 @@ int dispatch_bwd_ng(const BwdParams& p, cudaStream_t st) {
     const int need = (p.N + 1) / 2;
     int ng = 1;
     while (ng < need) ng <<= 1;
+    if (BC_SHARED && use_packed_bwd()) {
+      switch (ng) {
+        case 1: return launch_bwd_packed<T, 1, S_REAL>(p, st);
+        case 2: return launch_bwd_packed<T, 2, S_REAL>(p, st);
+        case 4: return launch_bwd_packed<T, 4, S_REAL>(p, st);
+        case 8: return launch_bwd_packed<T, 8, S_REAL>(p, st);
+        case 16: return launch_bwd_packed<T, 16, S_REAL>(p, st);
+        default: return launch_bwd_packed<T, 32, S_REAL>(p, st);
+      }
+    }
     switch (ng) {
       case 1: return launch_bwd<T, 2, 1, BC_SHARED, S_REAL>(p, st);
       case 2: return launch_bwd<T, 2, 2, BC_SHARED, S_REAL>(p, st);

@@ -209,6 +209,13 @@ int dispatch_shared(const FwdParams& p, int dtype, bool s_real, cudaStream_t st)
 // The same with packed two-lane FP32 arithmetic over pair-interleaved B/C rows
 // (ssm_scan_fwd_packed.cu).
 int dispatch_shared_packed(const FwdParams& p, int dtype, bool s_real, cudaStream_t st);
+// Rewrites channel-shared B and C [rows, N, 4] (dtype) into fp32 pair-interleaved
+// rows of NG*G states, [pair j][lane ng][component][half] with state
+// n = ng + NG*(2j + half), zero-padded above N (Cm may be null: C skipped).
+int pack_bc_pairs(const void* Bm, const void* Cm, float* Bp, float* Cp, int64_t rows, int N,
+                  int NG, int G, int dtype, cudaStream_t st);
+// bf16 -> fp32, n elements.
+int widen_bf16_to_f32(const void* in, float* out, int64_t n, cudaStream_t st);
 // Pass 1 of the time-chunked scan on the packed kernel (channel-shared B/C).
 int dispatch_state_only_packed(const FwdParams& p, int dtype, bool s_real, cudaStream_t st);
 // Streaming kernel for per-channel B/C and explicit q (ssm_scan_fwd_stream.cu).

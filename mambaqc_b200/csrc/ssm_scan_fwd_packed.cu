@@ -42,11 +42,14 @@
 #include <cstdlib>
 #include <type_traits>
 
+#include "packed_math.cuh"
 #include "ssm_scan_common.cuh"
 
 namespace mqc {
 namespace scan {
 namespace {
+
+using namespace ::mqc::pk;
 
 constexpr int kRing = 3;
 // CTA size cap: 8 states per lane need ~128 registers per thread (512 threads).
@@ -54,82 +57,6 @@ constexpr int kRing = 3;
 __host__ __device__ constexpr int pk_max_threads(int g) { return g == 4 ? 768 : 512; }
 constexpr size_t kPkSmemBudget = 220 * 1024;
 constexpr int kPackThreads = 256;
-
-// ------------------------------------------------------------ packed helpers
-__device__ __forceinline__ float2 bc2(float a) { return make_float2(a, a); }
-__device__ __forceinline__ float2 neg2(float2 a) { return make_float2(-a.x, -a.y); }
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
-__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
-__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
-
-// Two quaternions, component-interleaved: x = (q0.x, q1.x), ...
-struct QPair {
-  float2 x, y, z, w;
-};
-
-__device__ __forceinline__ QPair qp_zero() {
-  const float2 z = make_float2(0.f, 0.f);
-  return QPair{z, z, z, z};
-}
-
-// p (x) h + acc for both halves (the scalar qmul_acc, one packed op per FMA).
-__device__ __forceinline__ QPair qp_mul_acc(const QPair& p, const QPair& h, const QPair& a) {
-  QPair r;
-  r.x = fma2(p.x, h.x, fma2(neg2(p.y), h.y, fma2(neg2(p.z), h.z, fma2(neg2(p.w), h.w, a.x))));
-  r.y = fma2(p.x, h.y, fma2(p.y, h.x, fma2(p.z, h.w, fma2(neg2(p.w), h.z, a.y))));
-  r.z = fma2(p.x, h.z, fma2(neg2(p.y), h.w, fma2(p.z, h.x, fma2(p.w, h.y, a.z))));
-  r.w = fma2(p.x, h.w, fma2(p.y, h.z, fma2(neg2(p.z), h.y, fma2(p.w, h.x, a.w))));
-  return r;
-}
-
-// p (x) s with s the same quaternion for both halves (the scalar qmul).
-__device__ __forceinline__ QPair qp_mul_bcast(const QPair& p, float4 s) {
-  QPair r;
-  r.x = fma2(p.x, bc2(s.x), fma2(neg2(p.y), bc2(s.y), fma2(neg2(p.z), bc2(s.z), mul2(neg2(p.w), bc2(s.w)))));
-  r.y = fma2(p.x, bc2(s.y), fma2(p.y, bc2(s.x), fma2(p.z, bc2(s.w), mul2(neg2(p.w), bc2(s.z)))));
-  r.z = fma2(p.x, bc2(s.z), fma2(neg2(p.y), bc2(s.w), fma2(p.z, bc2(s.x), mul2(p.w, bc2(s.y)))));
-  r.w = fma2(p.x, bc2(s.w), fma2(p.y, bc2(s.z), fma2(neg2(p.z), bc2(s.y), mul2(p.w, bc2(s.x)))));
-  return r;
-}
-
-__device__ __forceinline__ float2 rcp_nr2(float2 d) {
-  float2 r;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r.x) : "f"(d.x));
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r.y) : "f"(d.y));
-  const float2 e = fma2(neg2(d), r, bc2(1.f));
-  return fma2(r, e, r);
-}
-
-// Per-(d, n) Cayley constants of a state pair (lr, Im Lambda, m = |Lambda|^2 / 4).
-struct LamPair {
-  float2 lr, li, lj, lk, m;
-};
-
-// cayley_from_const (ssm_scan_common.cuh) for both halves; *s_out (if given)
-// receives delta / den, the factor of Im Lambda in q.
-__device__ __forceinline__ QPair cayley_pair(float dl, float dl2, const LamPair& c, float eps,
-                                             float2* s_out = nullptr) {
-  const float2 P = mul2(bc2(dl2), c.m);
-  float2 den = fma2(bc2(-dl), c.lr, add2(bc2(1.f), P));
-  den.x = fmaxf(den.x, eps);
-  den.y = fmaxf(den.y, eps);
-  const float2 inv = rcp_nr2(den);
-  const float2 s = mul2(bc2(dl), inv);
-  if (s_out != nullptr) *s_out = s;
-  return QPair{fma2(neg2(P), inv, inv), mul2(s, c.li), mul2(s, c.lj), mul2(s, c.lk)};
-}
-
-__device__ __forceinline__ float4 qp_half(const QPair& q, int e) {
-  return e == 0 ? make_float4(q.x.x, q.y.x, q.z.x, q.w.x) : make_float4(q.x.y, q.y.y, q.z.y, q.w.y);
-}
-
-__device__ __forceinline__ void qp_set_half(QPair& q, int e, float4 v) {
-  if (e == 0) {
-    q.x.x = v.x; q.y.x = v.y; q.z.x = v.z; q.w.x = v.w;
-  } else {
-    q.x.y = v.x; q.y.y = v.y; q.z.y = v.z; q.w.y = v.w;
-  }
-}
 
 // Predicated scalar store without a branch (no divergence / reconvergence code
 // in the time loop).
@@ -683,6 +610,29 @@ int dispatch_packed(const FwdParams& p, int dtype, bool s_real, bool so, cudaStr
 }
 
 }  // namespace
+
+int pack_bc_pairs(const void* Bm, const void* Cm, float* Bp, float* Cp, int64_t rows, int N,
+                  int NG, int G, int dtype, cudaStream_t st) {
+  int ng_log2 = 0;
+  while ((1 << ng_log2) < NG) ++ng_log2;
+  const int64_t items = rows * (G / 2) * NG;
+  const int64_t want = (items + kPackThreads - 1) / kPackThreads;
+  const int64_t cap = int64_t(num_sms()) * 16;
+  const int grid = int(want < cap ? (want > 0 ? want : 1) : cap);
+  if (dtype == MQC_DTYPE_F32)
+    pack_bc_kernel<float><<<grid, kPackThreads, 0, st>>>(
+        static_cast<const float*>(Bm), static_cast<const float*>(Cm), Bp, Cp, rows, N, ng_log2,
+        G / 2);
+  else
+    pack_bc_kernel<__nv_bfloat16><<<grid, kPackThreads, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(Bm), static_cast<const __nv_bfloat16*>(Cm), Bp, Cp,
+        rows, N, ng_log2, G / 2);
+  return check_launch("pack_bc_pairs");
+}
+
+int widen_bf16_to_f32(const void* in, float* out, int64_t n, cudaStream_t st) {
+  return launch_widen(in, out, n, st);
+}
 
 int dispatch_shared_packed(const FwdParams& p, int dtype, bool s_real, cudaStream_t st) {
   return dispatch_packed(p, dtype, s_real, false, st);
