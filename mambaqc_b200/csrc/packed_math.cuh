@@ -39,13 +39,16 @@ __device__ __forceinline__ QPair qp_mul_acc(const QPair& p, const QPair& h, cons
   return r;
 }
 
-// p (x) s with s the same quaternion for both halves (the scalar qmul).
+// p (x) s with s the same quaternion for both halves (the scalar qmul). The
+// broadcast scalar is the first multiplicand of every packed op (the operand
+// slot where a broadcast is free); a*b == b*a exactly, so the rounding is that
+// of the scalar formula.
 __device__ __forceinline__ QPair qp_mul_bcast(const QPair& p, float4 s) {
   QPair r;
-  r.x = fma2(p.x, bc2(s.x), fma2(neg2(p.y), bc2(s.y), fma2(neg2(p.z), bc2(s.z), mul2(neg2(p.w), bc2(s.w)))));
-  r.y = fma2(p.x, bc2(s.y), fma2(p.y, bc2(s.x), fma2(p.z, bc2(s.w), mul2(neg2(p.w), bc2(s.z)))));
-  r.z = fma2(p.x, bc2(s.z), fma2(neg2(p.y), bc2(s.w), fma2(p.z, bc2(s.x), mul2(p.w, bc2(s.y)))));
-  r.w = fma2(p.x, bc2(s.w), fma2(p.y, bc2(s.z), fma2(neg2(p.z), bc2(s.y), mul2(p.w, bc2(s.x)))));
+  r.x = fma2(bc2(s.x), p.x, fma2(bc2(-s.y), p.y, fma2(bc2(-s.z), p.z, mul2(bc2(-s.w), p.w))));
+  r.y = fma2(bc2(s.y), p.x, fma2(bc2(s.x), p.y, fma2(bc2(s.w), p.z, mul2(bc2(-s.z), p.w))));
+  r.z = fma2(bc2(s.z), p.x, fma2(bc2(-s.w), p.y, fma2(bc2(s.x), p.z, mul2(bc2(s.y), p.w))));
+  r.w = fma2(bc2(s.w), p.x, fma2(bc2(s.z), p.y, fma2(bc2(-s.y), p.z, mul2(bc2(s.x), p.w))));
   return r;
 }
 

@@ -625,13 +625,18 @@ __global__ void __launch_bounds__(32 * kPbWarps)
     const float* shst = reinterpret_cast<const float*>(stg + L.hst) + (warp * 32 + lane) * 8;
     const QPair hstart = qp_from(*reinterpret_cast<const float4*>(shst),
                                  *reinterpret_cast<const float4*>(shst + 4));
-    // ---- recompute the sub-block's states forward (registers)
+    // ---- recompute + adjoint of the sub-block; FULL (len == kSub, every
+    // sub-block but possibly the last) compiles without per-step guards, so the
+    // loop-carried values need no conditional merges
+    float part[V];
+    auto run_sub = [&](auto full_tag) {
+    constexpr bool FULL = decltype(full_tag)::value;
     QPair hs[kSub];
     {
       QPair h = hstart;
 #pragma unroll
       for (int tt = 0; tt < kSub; ++tt) {
-        if (tt < len) {
+        if (FULL || tt < len) {
           const float dl = sdl[tt * cpb];
           const float4 sv = in_s(tt);
           const QPair Bq = ld_pair(tt, 0);
@@ -649,12 +654,11 @@ __global__ void __launch_bounds__(32 * kPbWarps)
       }
     }
     // ---- adjoint, backwards over the sub-block
-    float part[V];
 #pragma unroll
     for (int e = 0; e < V; ++e) part[e] = 0.f;
 #pragma unroll
     for (int tt = kSub - 1; tt >= 0; --tt) {
-      if (tt < len) {
+      if (FULL || tt < len) {
         const int t = t0 + tt;
         const float dl = sdl[tt * cpb];
         const float4 sv = in_s(tt);
@@ -708,13 +712,17 @@ __global__ void __launch_bounds__(32 * kPbWarps)
         }
         // the warp's first channel lanes write every (tt, pair) slot, so the slice
         // needs no clearing
-        if (lane < NG) {
-          float4* sbw = reinterpret_cast<float4*>(slice + ((tt * 2) * NG + ng) * 8);
-          sbw[0] = make_float4(dB.x.x, dB.x.y, dB.y.x, dB.y.y);
-          sbw[1] = make_float4(dB.z.x, dB.z.y, dB.w.x, dB.w.y);
-          float4* scw = reinterpret_cast<float4*>(slice + ((tt * 2 + 1) * NG + ng) * 8);
-          scw[0] = make_float4(dC.x.x, dC.x.y, dC.y.x, dC.y.y);
-          scw[1] = make_float4(dC.z.x, dC.z.y, dC.w.x, dC.w.y);
+        if (lane < NG) {  // one 8-byte store per pair: no register assembly
+          float2* sbw = reinterpret_cast<float2*>(slice + ((tt * 2) * NG + ng) * 8);
+          sbw[0] = dB.x;
+          sbw[1] = dB.y;
+          sbw[2] = dB.z;
+          sbw[3] = dB.w;
+          float2* scw = reinterpret_cast<float2*>(slice + ((tt * 2 + 1) * NG + ng) * 8);
+          scw[0] = dC.x;
+          scw[1] = dC.y;
+          scw[2] = dC.z;
+          scw[3] = dC.w;
         }
         carry = qp_mul_acc(qp_conj(qv), lam, qp_zero());
         part[tt * NV + 0] = pdp.x + pdp.y;
@@ -726,6 +734,9 @@ __global__ void __launch_bounds__(32 * kPbWarps)
         }
       }
     }
+    };
+    if (len == kSub) run_sub(std::true_type{});
+    else run_sub(std::false_type{});
     // ---- per-(t, channel) sums over the NG lanes of the channel, then stores
     {
       const int base = reduce_scatter<V, NG>(part, ng);
@@ -755,15 +766,18 @@ __global__ void __launch_bounds__(32 * kPbWarps)
     for (int e = threadIdx.x; e < len * 2 * NG; e += blockDim.x) {
       const int pg = e % NG, tw = e / NG;  // tw = tt * 2 + which
       const float* s0 = slices + size_t(tw * NG + pg) * 8;
-      float4 u = *reinterpret_cast<const float4*>(s0);
-      float4 w = *reinterpret_cast<const float4*>(s0 + 4);
+      const float2* p0 = reinterpret_cast<const float2*>(s0);
+      float2 px = p0[0], py = p0[1], pz = p0[2], pw = p0[3];
+#pragma unroll
       for (int k = 1; k < kPbWarps; ++k) {
-        const float* sk = s0 + size_t(k) * kSub * 2 * NG * 8;
-        const float4 a = *reinterpret_cast<const float4*>(sk);
-        const float4 a2 = *reinterpret_cast<const float4*>(sk + 4);
-        u.x += a.x; u.y += a.y; u.z += a.z; u.w += a.w;
-        w.x += a2.x; w.y += a2.y; w.z += a2.z; w.w += a2.w;
+        const float2* pk2 = reinterpret_cast<const float2*>(s0 + size_t(k) * kSub * 2 * NG * 8);
+        px = add2(px, pk2[0]);
+        py = add2(py, pk2[1]);
+        pz = add2(pz, pk2[2]);
+        pw = add2(pw, pk2[3]);
       }
+      const float4 u = make_float4(px.x, px.y, py.x, py.y);
+      const float4 w = make_float4(pz.x, pz.y, pw.x, pw.y);
       // u = (x0, x1, y0, y1), w = (z0, z1, w0, w1): states pg and pg + NG
       float* dst = ((tw & 1) ? dCg : dBg) + (int64_t(b) * T_ + t0 + (tw >> 1)) * N * 4;
       if (pg < N) atomicAdd(reinterpret_cast<float4*>(dst + pg * 4), make_float4(u.x, u.z, w.x, w.z));
