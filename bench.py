@@ -417,7 +417,8 @@ def run_e2e(args, inp, dev, world, stream, op):
     """Same metric through the public API with host buffers: every step hands the
     inputs in pinned host memory to ``ssm_scan_cayley_from_host`` and gets y back
     in pinned host memory -- all host<->device copies inside the timed region
-    (pipelined over batch rows by the API)."""
+    (pipelined over time segments by the API)."""
+    from mambaqc_b200.kernels.ssm_fused import _host_segments
     from mambaqc_b200.kernels import ssm_scan_cayley_from_host
 
     host = {k: v.cpu().pin_memory() for k, v in inp.items()}
@@ -435,10 +436,12 @@ def run_e2e(args, inp, dev, world, stream, op):
     ms = max_over_ranks(ms, world, dev)
     return {"value": BATCH * SEQ * world / (ms / 1e3), "unit": "tokens/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms,
-            "steps": steps, "gpu_launches_per_step": BATCH * launches_per_scan(args.dtype),
+            "steps": steps,
+            "gpu_launches_per_step": _host_segments(SEQ) * launches_per_scan(args.dtype),
             "path": "mambaqc_b200.kernels.ssm_scan_cayley_from_host: pinned host inputs -> "
-                    "device (copy stream), fused scan per batch row, y -> pinned host "
-                    "(third stream)"}
+                    "device (copy stream), fused scan per time segment of the whole batch "
+                    f"({_host_segments(SEQ)} segments chained through the final state), "
+                    "y -> pinned host (third stream)"}
 
 
 def run_fwd_bwd(args, inp, dev, world, stream, op):

@@ -184,6 +184,23 @@ MQC_API int mqc_ssm_scan_fwd(const mqc_ssm_scan_args* args, void* stream);
  * only time-parallel primitive is parallel_scan_quaternion (parallel_scan.py:171),
  * which the model never calls; this is the scan of ssm_forward_fused
  * (ssm_fused.py:340-401) made time-parallel. */
+/* mqc_ssm_scan_fwd (fused Cayley form, no checkpoints) on HOST buffers:
+ * delta, Lambda, Bm, Cm, s, dskip, h0 (optional) are read from host memory and
+ * y, hT (optional) are written to host memory; `status` stays a device pointer
+ * or NULL. The skip weight must be per channel (dskip_sb = dskip_st = 0). The
+ * sequence is cut into time segments (seq_len % segments == 0; with
+ * s = seq_len / segments even and segments >= 2 the pieces are s/2, s, ..., s,
+ * s/2, which halves the pipeline's fill and drain), each holding every batch
+ * row; segment k is copied in on an internal stream
+ * while segment k-1 is scanned on `stream` (from segment k-2's final state) and
+ * segment k-2's y is copied out on a second internal stream. Pinned host memory
+ * makes the copies asynchronous. Returns once everything is enqueued; the host
+ * y and hT are complete when `stream` is. Calls on one device share the two
+ * internal streams: do not overlap two calls on one device. This is the
+ * host-facing form of QuaternionMamba2Block._ssm_forward lines
+ * models/quaternion_mamba2_block.py:214-228, with the transfers inside the call. */
+MQC_API int mqc_ssm_scan_fwd_host(const mqc_ssm_scan_args* args, int64_t segments, void* stream);
+
 MQC_API size_t mqc_ssm_scan_fwd_chunked_workspace_size(int64_t batch, int64_t channels,
                                                        int64_t d_state, int64_t nchunks);
 MQC_API int mqc_ssm_scan_fwd_chunked(const mqc_ssm_scan_args* args, int64_t nchunks,

@@ -82,6 +82,7 @@ _SIGNATURES = {
     "mqc_prefix_prod": [_c_void_p, _c_void_p, _i64, _i64, _i64, _i32, _c_void_p],
     "mqc_prefix_prod_noalloc": [_c_void_p, _c_void_p, _i64, _i64, _i64, _i32, _c_void_p],
     "mqc_ssm_scan_fwd": [ctypes.POINTER(SsmScanArgs), _c_void_p],
+    "mqc_ssm_scan_fwd_host": [ctypes.POINTER(SsmScanArgs), _i64, _c_void_p],
     "mqc_ssm_scan_bwd": [ctypes.POINTER(SsmScanBwdArgs), _c_void_p],
     "mqc_ssm_scan_fwd_chunked": [ctypes.POINTER(SsmScanArgs), _i64, _c_void_p, ctypes.c_size_t,
                                  _c_void_p],

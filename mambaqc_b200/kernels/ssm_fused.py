@@ -326,67 +326,64 @@ def ssm_step_fused(q: torch.Tensor, B: torch.Tensor, S: torch.Tensor, C: torch.T
     return h_new.to(h_prev.dtype), y
 
 
+def _host_segments(seqlen: int) -> int:
+    """Time segments for the host pipeline: up to 8, each >= 128 steps."""
+    n = 8
+    while n > 1 and (seqlen % n or seqlen // n < 128):
+        n //= 2
+    return n
+
+
 def ssm_scan_cayley_from_host(delta: torch.Tensor, Lambda: torch.Tensor, B: torch.Tensor,
                               C: torch.Tensor, S: torch.Tensor, D: torch.Tensor,
                               device: torch.device | str | None = None,
                               out: torch.Tensor | None = None, eps: float = 1e-6,
+                              segments: int | str = "auto",
                               _bufs: dict | None = None) -> torch.Tensor:
-    """``ssm_scan_cayley`` on host (CPU) tensors, pipelined over the batch.
+    """``ssm_scan_cayley`` on host (CPU) tensors, through ``mqc_ssm_scan_fwd_host``.
 
-    For inputs that live in host memory: batch row b is copied to the GPU on one
-    stream while row b-1 is scanned on another and row b-2's output is copied
-    back on a third, so the PCIe transfers in both directions overlap the
-    kernels. Pinned host tensors give asynchronous copies (pageable ones work but
-    serialise). Returns y [B,T,D,4] in host memory (``out`` if given, pinned
-    when allocated here). Forward only (no autograd). ``_bufs`` may hold
-    reusable device buffers between calls (a dict the caller keeps).
+    For inputs that live in host memory: the C entry point cuts the sequence into
+    time segments (all batch rows in each) and pipelines them over three
+    streams: segment k is copied to the GPU (one strided copy per tensor) while
+    segment k-1 is scanned on the current stream (from segment k-2's final
+    state, so every scan keeps the whole batch and fills the GPU) and segment
+    k-2's output is copied back, so the PCIe transfers in both directions overlap
+    the kernels. Pinned host tensors give asynchronous copies (pageable ones work
+    but serialise). Returns y [B,T,D,4] in host memory (``out`` if given, pinned
+    when allocated here), complete when the current stream is. Forward only (no
+    autograd); D is the per-channel skip weight [D]. ``_bufs`` is accepted for
+    compatibility and unused (device scratch comes from the library's pool).
     """
     assert delta.dim() == 3 and S.shape[:3] == delta.shape
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
     bsz, seqlen, dm = delta.shape
     dt = delta.dtype
+    for name, t in (("delta", delta), ("B", B), ("C", C), ("S", S), ("Lambda", Lambda), ("D", D)):
+        if t.device.type != "cpu":
+            raise ValueError(f"ssm_scan_cayley_from_host: {name} must be a host tensor")
+    for name, t in (("B", B), ("C", C), ("S", S)):
+        if t.dtype != dt:
+            raise TypeError(f"{name} dtype {t.dtype} != {dt}")
+    if D.dim() != 1 or D.shape[0] != dm:
+        raise ValueError("ssm_scan_cayley_from_host: D must be the per-channel skip weight [D]")
+    nseg = _host_segments(seqlen) if segments == "auto" else int(segments)
+    if nseg < 1 or seqlen % nseg:
+        raise ValueError(f"seq_len {seqlen} does not split into {nseg} equal segments")
     if out is None:
         out = torch.empty(bsz, seqlen, dm, 4, dtype=dt, pin_memory=True)
-    bufs = _bufs if _bufs is not None else {}
+    assert out.is_contiguous() and out.dtype == dt and tuple(out.shape) == (bsz, seqlen, dm, 4)
+    shared = B.dim() == 4
+    ds = B.shape[2] if shared else B.shape[3]
+    dc, Bc, Cc, Sc = (t.contiguous() for t in (delta, B, C, S))
+    Lc = Lambda.float().contiguous()
+    Dc = D.float().contiguous()
+    flags = (_lib.MQC_SSM_BC_SHARED if shared else 0) | (_lib.MQC_SSM_S_REAL if S.dim() == 3 else 0)
+    a = _lib.SsmScanArgs(
+        batch=bsz, seq_len=seqlen, channels=dm, d_state=ds, dtype=_lib.dtype_code(dc),
+        flags=flags, eps=float(eps), reserved0=0, delta=dc.data_ptr(), lambda_=Lc.data_ptr(),
+        q=None, Bm=Bc.data_ptr(), Cm=Cc.data_ptr(), s=Sc.data_ptr(), dskip=Dc.data_ptr(),
+        dskip_sb=0, dskip_st=0, dskip_sd=1, h0=None, y=out.data_ptr(), hT=None,
+        status=_lib.status_word(dev).data_ptr(), wait_poll_limit=-1, ckpt=None, ckpt_every=0)
     with torch.cuda.device(dev):
-        lam_d = Lambda.to(dev, torch.float32, non_blocking=True)
-        d_d = D.to(dev, non_blocking=True)
-        per_row = (delta, B, C, S)
-        if "streams" not in bufs:
-            bufs["streams"] = [torch.cuda.Stream(dev) for _ in range(3)]
-            bufs["slots"] = [[torch.empty(t.shape[1:], dtype=t.dtype, device=dev) for t in per_row]
-                             for _ in range(2)]
-            bufs["y"] = [torch.empty(seqlen, dm, 4, dtype=dt, device=dev) for _ in range(2)]
-        h2d, comp, d2h = bufs["streams"]
-        slots, ybufs = bufs["slots"], bufs["y"]
-        cur = torch.cuda.current_stream(dev)
-        h2d.wait_stream(cur)
-        comp.wait_stream(cur)
-        done_comp = [None, None]
-        done_d2h = [None, None]
-        for b in range(bsz):
-            k = b % 2
-            with torch.cuda.stream(h2d):
-                if done_comp[k] is not None:
-                    h2d.wait_event(done_comp[k])  # slot k free again
-                for dst, src in zip(slots[k], per_row):
-                    dst.copy_(src[b], non_blocking=True)
-                ready = torch.cuda.Event()
-                ready.record(h2d)
-            with torch.cuda.stream(comp):
-                comp.wait_event(ready)
-                if done_d2h[k] is not None:
-                    comp.wait_event(done_d2h[k])  # y buffer k copied out
-                dl, Bb, Cb, Sb = (t.unsqueeze(0) for t in slots[k])
-                _run_scan(flags=0, delta=dl, Lam=lam_d, B=Bb, C=Cb, S=Sb, D=d_d, eps=eps,
-                          y=ybufs[k].unsqueeze(0))
-                done_comp[k] = torch.cuda.Event()
-                done_comp[k].record(comp)
-            with torch.cuda.stream(d2h):
-                d2h.wait_event(done_comp[k])
-                out[b].copy_(ybufs[k], non_blocking=True)
-                done_d2h[k] = torch.cuda.Event()
-                done_d2h[k].record(d2h)
-        cur.wait_stream(d2h)
-        cur.wait_stream(comp)
+        _lib.call("mqc_ssm_scan_fwd_host", ctypes.byref(a), int(nseg), _lib.stream_ptr(dev))
     return out

@@ -242,9 +242,26 @@ def test_host_buffer_entry_point_matches_device_entry_point():
     y_dev = ssm_scan_cayley(d["delta"], d["Lambda"], d["B"], d["C"], d["S"], d["D"])
     host = {k: v.float().pin_memory() for k, v in inp.items()}
     bufs = {}
-    for _ in range(2):  # reusing the device buffers across calls
+    # one segment, then four time segments chained through the final state, with
+    # the device buffers reused across calls (and rebuilt when the segment changes)
+    for segments in (1, 1, 4, 4):
         y_host = ssm_scan_cayley_from_host(host["delta"], host["Lambda"], host["B"], host["C"],
-                                           host["S"], host["D"], device=DEV, _bufs=bufs)
+                                           host["S"], host["D"], device=DEV, _bufs=bufs,
+                                           segments=segments)
         torch.cuda.synchronize()
         assert y_host.device.type == "cpu"
         assert torch.equal(y_host, y_dev.cpu())
+
+
+@pytest.mark.parametrize("shared,dtype", [(False, torch.float32), (True, torch.bfloat16)])
+def test_host_buffer_entry_point_layouts(shared, dtype):
+    """Per-channel B/C and bf16 through the host-buffer entry point, in segments."""
+    from mambaqc_b200.kernels import ssm_scan_cayley_from_host
+    inp = make_scan_inputs(2, 48, 7, 12, shared=shared, s_real=True, seed=202)
+    d = to_dev(inp, dtype)
+    y_dev = ssm_scan_cayley(d["delta"], d["Lambda"], d["B"], d["C"], d["S"], d["D"])
+    host = {k: v.cpu().pin_memory() for k, v in d.items()}
+    y_host = ssm_scan_cayley_from_host(host["delta"], host["Lambda"], host["B"], host["C"],
+                                       host["S"], host["D"], device=DEV, segments=3)
+    torch.cuda.synchronize()
+    assert torch.equal(y_host, y_dev.cpu())
