@@ -66,7 +66,10 @@ def parse_args():
     ap.add_argument("--segments", type=int, default=4,
                     help="config5 on >1 GPU: time segments whose all-gather overlaps the "
                          "scan of the next segment")
-    ap.add_argument("--workload", choices=["config3", "config5", "config2"], default="config3",
+    ap.add_argument("--decode-batch", type=int, default=4,
+                    help="decode workload: sequences decoded together per GPU")
+    ap.add_argument("--workload", choices=["config3", "config5", "config2", "decode"],
+                    default="config3",
                     help="config5: B=1, T=65536, D=1536, N=64, bf16, channel-sharded over the "
                          "GPUs with an NCCL all-gather of y (strong scaling)")
     return ap.parse_args()
@@ -658,6 +661,68 @@ def run_config2(args, world, rank, local):
     return 0
 
 
+def run_decode(args, world, rank, local):
+    """Single-token decode through the block's SSM: each step advances every
+    sequence of the decode batch by one token (config-3 channel and state sizes),
+    updating the fp32 state cache in place (``ssm_step_cayley``). 64 steps are
+    captured in a CUDA graph and replayed, as a generation loop would run them;
+    the state cache (B*D*N*16 bytes) is read and written every step."""
+    from mambaqc_b200.kernels import ssm_step_cayley
+
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    bsz, K = args.decode_batch, 64
+    g = torch.Generator(device=dev).manual_seed(5 + rank)
+    delta = torch.nn.functional.softplus(torch.randn(K, bsz, CHANNELS, generator=g, device=dev) - 3)
+    x = torch.randn(K, bsz, CHANNELS, generator=g, device=dev)
+    Bm = torch.randn(K, bsz, STATE, 4, generator=g, device=dev) / math.sqrt(STATE)
+    Cm = torch.randn(K, bsz, STATE, 4, generator=g, device=dev) / math.sqrt(STATE)
+    lam = torch.empty(CHANNELS, STATE, 4, device=dev)
+    lam[..., 0] = -torch.exp(torch.rand(CHANNELS, STATE, generator=g, device=dev) *
+                             (math.log(1e-1) - math.log(1e-3)) + math.log(1e-3))
+    lam[..., 1:] = 0.5 * torch.randn(CHANNELS, STATE, 3, generator=g, device=dev)
+    Dk = torch.ones(CHANNELS, device=dev)
+    h = torch.zeros(bsz, CHANNELS, STATE, 4, device=dev)
+    ys = torch.empty(K, bsz, CHANNELS, 4, device=dev)
+
+    def steps():
+        for t in range(K):
+            ssm_step_cayley(delta[t], lam, Bm[t], Cm[t], x[t], Dk, h, out=ys[t])
+
+    steps()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        steps()
+    reps = max(3, min(args.steps, 50))
+    ms = timed(graph.replay, reps, max(3, args.warmup), world, stream) / (reps * K)
+    ms = max_over_ranks(ms, world, dev)
+    # per step: state read + write, y, inputs (delta, x, B, C), Lambda
+    step_bytes = (2 * h.numel() * 4 + bsz * CHANNELS * 16 + bsz * CHANNELS * 8 +
+                  2 * bsz * STATE * 16 + lam.numel() * 4)
+    peaks, peak_kind = measured_peaks()
+    gbps = step_bytes / (ms / 1e3) / 1e9
+    if rank == 0:
+        line = {
+            "metric": "decode tokens/s through the block SSM (one token per sequence per step, "
+                      "fp32 state cache updated in place)",
+            "value": bsz * world / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": reps * K, "warmup": max(3, args.warmup), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded, config-3 distributions)",
+            "config": {"workload": "decode", "decode_batch": bsz, "d_inner": CHANNELS,
+                       "d_state": STATE, "graph_steps": K},
+            "roofline": {"bound": "hbm", "achieved": gbps, "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": gbps / peaks["hbm_gbs"],
+                         "algorithmic_bytes_per_step": step_bytes,
+                         "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},
+            "gpu_launches": reps * K,
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse_args()
     world, rank, local = dist_setup(args)
@@ -668,6 +733,8 @@ def main():
             return run_config5(args, world, rank, local)
         if args.workload == "config2":
             return run_config2(args, world, rank, local)
+        if args.workload == "decode":
+            return run_decode(args, world, rank, local)
         return run_b200(args, world, rank, local)
     finally:
         if dist.is_initialized():

@@ -220,6 +220,11 @@ int widen_bf16_to_f32(const void* in, float* out, int64_t n, cudaStream_t st);
 int dispatch_state_only_packed(const FwdParams& p, int dtype, bool s_real, cudaStream_t st);
 // Streaming kernel for per-channel B/C and explicit q (ssm_scan_fwd_stream.cu).
 int dispatch_stream(const FwdParams& p, int dtype, bool s_real, bool q_given, cudaStream_t st);
+// Streaming kernel for channel-shared B/C (short sequences).
+int dispatch_stream_shared(const FwdParams& p, int dtype, bool s_real, cudaStream_t st);
+// Sequences up to this length with channel-shared B/C skip the packed kernel's
+// pre-pass and producer pipeline and take the streaming kernel.
+constexpr int kShortScan = 8;
 // Pass 1 of the time-chunked scan: final state + operator product, no readout.
 int dispatch_state_only(const FwdParams& p, int dtype, bool s_real, bool bc_shared,
                         cudaStream_t st);

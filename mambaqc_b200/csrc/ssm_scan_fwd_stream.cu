@@ -209,6 +209,14 @@ int dispatch_stream(const FwdParams& p, int dtype, bool s_real, bool q_given, cu
                 : dispatch_stream_t<__nv_bfloat16, false, false, false, false>(p, st);
 }
 
+int dispatch_stream_shared(const FwdParams& p, int dtype, bool s_real, cudaStream_t st) {
+  if (dtype == MQC_DTYPE_F32)
+    return s_real ? dispatch_stream_t<float, true, false, true, false>(p, st)
+                  : dispatch_stream_t<float, false, false, true, false>(p, st);
+  return s_real ? dispatch_stream_t<__nv_bfloat16, true, false, true, false>(p, st)
+                : dispatch_stream_t<__nv_bfloat16, false, false, true, false>(p, st);
+}
+
 int dispatch_state_only(const FwdParams& p, int dtype, bool s_real, bool bc_shared,
                         cudaStream_t st) {
   if (dtype == MQC_DTYPE_F32) {

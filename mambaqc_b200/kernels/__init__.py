@@ -14,7 +14,8 @@ from .quaternion_ops import (
 from .cayley_transform import cayley_discretization_fused
 from .parallel_scan import parallel_scan_quaternion
 from .quaternion_norm import quaternion_layer_norm_fused
-from .ssm_fused import ssm_step_fused, ssm_forward_fused, ssm_scan_cayley, ssm_scan_cayley_from_host
+from .ssm_fused import (ssm_step_fused, ssm_forward_fused, ssm_scan_cayley,
+                        ssm_scan_cayley_from_host, ssm_step_cayley)
 
 # Importing the submodule ``quaternion_norm`` (the LayerNorm file) rebinds the
 # package attribute of that name to the module; bind the function again so that
@@ -34,4 +35,5 @@ __all__ = [
     "ssm_forward_fused",
     "ssm_scan_cayley",
     "ssm_scan_cayley_from_host",
+    "ssm_step_cayley",
 ]

@@ -52,7 +52,8 @@ def _skip_operand(D: torch.Tensor, bsz: int, seqlen: int, dm: int):
 
 
 def _run_scan(*, flags: int, q=None, delta=None, Lam=None, B, C, S, D, h0=None,
-              return_final_state=False, eps=1e-6, wait_poll_limit=-1, ckpt=None, y=None):
+              return_final_state=False, eps=1e-6, wait_poll_limit=-1, ckpt=None, y=None,
+              hT_out=None):
     ref = q if q is not None else delta
     dt = ref.dtype
     bsz, seqlen, dm = ref.shape[0], ref.shape[1], ref.shape[2]
@@ -77,8 +78,13 @@ def _run_scan(*, flags: int, q=None, delta=None, Lam=None, B, C, S, D, h0=None,
     else:
         assert y.is_contiguous() and y.dtype == dt and tuple(y.shape) == (bsz, seqlen, dm, 4)
         assert y.data_ptr() % va == 0
-    hT = (torch.empty(bsz, dm, ds, 4, dtype=torch.float32, device=ref.device)
-          if return_final_state else None)
+    if hT_out is not None:
+        assert hT_out.is_contiguous() and hT_out.dtype == torch.float32
+        assert tuple(hT_out.shape) == (bsz, dm, ds, 4)
+        hT = hT_out
+    else:
+        hT = (torch.empty(bsz, dm, ds, 4, dtype=torch.float32, device=ref.device)
+              if return_final_state else None)
     if shared:
         flags |= _lib.MQC_SSM_BC_SHARED
     if s_real:
@@ -324,6 +330,26 @@ def ssm_step_fused(q: torch.Tensor, B: torch.Tensor, S: torch.Tensor, C: torch.T
                   Dc.data_ptr(), hp.data_ptr(), h_new.data_ptr(), y.data_ptr(), bsz, dm, ds,
                   _lib.dtype_code(qc), _lib.stream_ptr(q.device))
     return h_new.to(h_prev.dtype), y
+
+
+def ssm_step_cayley(delta: torch.Tensor, Lambda: torch.Tensor, B: torch.Tensor,
+                    C: torch.Tensor, S: torch.Tensor, D: torch.Tensor, h: torch.Tensor,
+                    eps: float = 1e-6, out: torch.Tensor | None = None) -> torch.Tensor:
+    """One decode step of the fused Cayley scan with an in-place state cache.
+
+    delta [B,D], Lambda [D,N,4], B/C [B,N,4] (shared by channels) or [B,D,N,4],
+    S real x [B,D] or quaternion [B,D,4], D skip [D], h [B,D,N,4] fp32: the state
+    before the step, overwritten with the state after it. Returns y [B,D,4]
+    (written into ``out`` when given, e.g. a row of a preallocated trajectory).
+    The same step as ``ssm_step_fused`` (ssm_fused.py:258-337 in the reference)
+    with q formed from delta and Lambda inside the kernel. No autograd.
+    """
+    assert delta.dim() == 2 and h.dim() == 4 and h.dtype == torch.float32 and h.is_contiguous()
+    assert B.dim() in (3, 4) and C.dim() == B.dim()
+    y, _ = _run_scan(flags=0, delta=delta.unsqueeze(1), Lam=Lambda, B=B.unsqueeze(1),
+                     C=C.unsqueeze(1), S=S.unsqueeze(1), D=D, h0=h, eps=eps, hT_out=h,
+                     y=None if out is None else out.unsqueeze(1))
+    return y.squeeze(1)
 
 
 def _host_segments(seqlen: int) -> int:
