@@ -120,6 +120,31 @@ def test_scan_argument_validation_without_gpu():
 
 
 @no_gpu
+def test_host_scan_argument_validation_without_gpu():
+    """mqc_ssm_scan_fwd_host rejects bad arguments before any CUDA call."""
+    lib = _lib.load()
+    fake = 0x10000
+    base = dict(batch=2, seq_len=8, channels=4, d_state=16, dtype=0,
+                flags=_lib.MQC_SSM_BC_SHARED | _lib.MQC_SSM_S_REAL, eps=1e-6, reserved0=0,
+                delta=fake, lambda_=fake, q=None, Bm=fake, Cm=fake, s=fake, dskip=fake,
+                dskip_sb=0, dskip_st=0, dskip_sd=1, h0=None, y=fake, hT=None, status=None,
+                wait_poll_limit=-1)
+
+    def call(segments=2, **kw):
+        a = _lib.SsmScanArgs(**{**base, **kw})
+        return lib.mqc_ssm_scan_fwd_host(ctypes.byref(a), segments, None)
+
+    assert call(segments=3) == INVALID  # 8 steps do not split into 3
+    assert b"segments" in lib.mqc_last_error()
+    assert call(segments=0) == INVALID
+    assert call(dskip_st=1) == UNSUPPORTED  # the skip weight must be per channel
+    assert call(flags=_lib.MQC_SSM_Q_GIVEN) == UNSUPPORTED
+    assert call(y=None) == INVALID
+    assert call(dtype=7) == INVALID
+    assert call(batch=0) == 0  # nothing to do
+
+
+@no_gpu
 def test_layernorm_argument_validation_without_gpu():
     lib = _lib.load()
     fake = 0x10000

@@ -1,18 +1,17 @@
-"""Channel-sharded scan (config 5's decomposition) on CPU with 2 gloo ranks: each
+"""Channel-sharded scan (config 5's decomposition) on CPU with 2 and 3 gloo ranks: each
 rank scans its channel shard (the oracle stands in for the GPU scan) and the
 all-gather + reassembly must reproduce the unsharded oracle bit for bit."""
 
 import os
 import socket
 
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from mambaqc_b200.kernels.sharded import channel_shard, ssm_scan_cayley_channel_sharded
 from oracle import ref
-
-WORLD = 2
 
 
 def _inputs():
@@ -32,13 +31,13 @@ def _oracle_scan(d, L, Bm, Cm, s, Dk, h0=None):
     return ref.ssm_scan_cayley(d, L, Bm, Cm, s, Dk, h0=h0)
 
 
-def _worker(rank, port, q):
+def _worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         delta, lam, Bm, Cm, x, Dk = _inputs()
-        shard = (channel_shard(delta, rank, WORLD, 2), channel_shard(lam, rank, WORLD, 0), Bm, Cm,
-                 channel_shard(x, rank, WORLD, 2), channel_shard(Dk, rank, WORLD, 0))
+        shard = (channel_shard(delta, rank, world, 2), channel_shard(lam, rank, world, 0), Bm, Cm,
+                 channel_shard(x, rank, world, 2), channel_shard(Dk, rank, world, 0))
         y1 = ssm_scan_cayley_channel_sharded(*shard, scan_fn=_oracle_scan)
         # three time segments, each scanned from the previous one's final state
         y3 = ssm_scan_cayley_channel_sharded(*shard, scan_fn=_oracle_scan, segments=3)
@@ -53,25 +52,25 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_channel_sharded_scan_matches_unsharded():
+@pytest.mark.parametrize("world", [2, 3])
+def test_channel_sharded_scan_matches_unsharded(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, port, q)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    results = dict(q.get(timeout=120) for _ in range(WORLD))
+    results = dict(q.get(timeout=120) for _ in range(world))
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
     full = _oracle_scan(*_inputs())[0]
-    for r in range(WORLD):
+    for r in range(world):
         y1, y3 = results[r]
         assert torch.equal(y1, full)
         assert torch.allclose(y3, full, rtol=1e-12, atol=1e-12)
 
 
 def test_channel_shard_rejects_uneven_split():
-    import pytest
     with pytest.raises(ValueError):
         channel_shard(torch.zeros(1, 2, 5), 0, 2, 2)
