@@ -243,6 +243,11 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool vali
                "r"(valid ? 16 : 0)
                : "memory");
 }
+// Waits until at most N of this thread's committed cp.async groups are pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() {
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
