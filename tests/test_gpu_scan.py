@@ -296,3 +296,33 @@ def test_decode_step_with_state_cache(shared, dtype):
                                        h0=h0.double().cpu())
     tol = RTOL_F32 if dtype == torch.float32 else RTOL_BF16
     assert rel_l2(ys[0], y_ref[:, 0]) < tol
+
+
+def test_config3_full_size_bf16_channel_sample():
+    """Config 3 at full size with bf16 inputs (fp32 state): the oracle runs in fp64
+    on the bf16-rounded inputs of a channel sample, so h_T differs only by the
+    kernel's fp32 rounding and y by its final bf16 rounding."""
+    bsz, seqlen, dm, ds = 4, 2048, 1536, 64
+    g = gen(5)
+    x = torch.randn(bsz, seqlen, dm, generator=g).bfloat16()
+    delta = torch.nn.functional.softplus(torch.randn(bsz, seqlen, dm, generator=g) - 3.0).bfloat16()
+    lam = torch.empty(dm, ds, 4)
+    lam[..., 0] = -torch.exp(torch.empty(dm, ds).uniform_(math.log(1e-3), math.log(1e-1),
+                                                          generator=g))
+    lam[..., 1:] = 0.5 * torch.randn(dm, ds, 3, generator=g)
+    Bm = (torch.randn(bsz, seqlen, ds, 4, generator=g) / 8).bfloat16()
+    Cm = (torch.randn(bsz, seqlen, ds, 4, generator=g) / 8).bfloat16()
+    Dk = 1.0 + 0.1 * torch.randn(dm, generator=g)
+    y, hT = ssm_scan_cayley(delta.to(DEV), lam.to(DEV), Bm.to(DEV), Cm.to(DEV), x.to(DEV),
+                            Dk.to(DEV), return_final_state=True)
+    torch.cuda.synchronize()
+    _lib.check_device_status(torch.device(DEV))
+    assert y.dtype == torch.bfloat16 and hT.dtype == torch.float32
+    chans = torch.tensor([0, 3, 64, 1000, 1535])
+    for b in (1, 2):
+        y_ref, h_ref = ref.ssm_scan_cayley(
+            delta[b:b + 1, :, chans].double(), lam[chans].double(), Bm[b:b + 1].double(),
+            Cm[b:b + 1].double(), x[b:b + 1, :, chans].double(), Dk[chans].double())
+        assert rel_l2(hT[b:b + 1, chans.to(DEV)], h_ref) < RTOL_F32
+        assert rel_l2(y[b:b + 1, :, chans.to(DEV)], y_ref) < RTOL_BF16
+    assert torch.isfinite(y.float()).all()
