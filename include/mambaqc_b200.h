@@ -291,6 +291,70 @@ MQC_API int mqc_qln_bwd(const void* q, const float* gamma, const void* dout, con
                 size_t workspace_bytes, int64_t rows, int64_t d_model, float eps, int dtype,
                 void* stream);
 
+/* ---- block glue around the scan: models/quaternion_mamba2_block.py --------- */
+
+/* Causal depthwise conv + bias + SiLU of the block's inner signal, in one pass:
+ *   a[b,t,d] = bias[d] + sum_k weight[d,k] * x[b, t-(K-1)+k, d]   (x = 0 before t = 0)
+ *   out[b,t,d] = a * sigmoid(a)
+ * x rows of `channels` elements at a row stride of `x_row_stride` elements (the
+ * first half of the in_proj output [B,T,2*d_inner] is read in place); out
+ * [B,T,channels] contiguous, same dtype. weight [channels, K] fp32 (the
+ * nn.Conv1d weight [channels,1,K]), bias [channels] fp32 or NULL; 1 <= K <= 8.
+ * Replaces CausalConv1d.forward (layers/causal_conv1d.py:68-91) followed by
+ * F.silu, block lines models/quaternion_mamba2_block.py:140-144. */
+MQC_API int mqc_conv_silu_fwd(const void* x, int64_t x_row_stride, const float* weight,
+                              const float* bias, void* out, int64_t batch, int64_t seq_len,
+                              int64_t channels, int64_t kernel_size, int dtype, void* stream);
+
+/* Bytes of workspace mqc_conv_silu_bwd needs (per-block partial sums of the
+ * weight and bias gradients; 0 if nothing to do). */
+MQC_API size_t mqc_conv_silu_bwd_workspace_size(int64_t batch, int64_t seq_len, int64_t channels,
+                                                int64_t kernel_size);
+
+/* Backward of mqc_conv_silu_fwd (the pre-activation is recomputed from x):
+ * dx [B,T,channels] contiguous (dtype); dweight [channels,K] and dbias
+ * [channels] fp32, summed over (b,t) in a fixed order (dbias may be NULL).
+ * `workspace`: caller-owned, 16-byte aligned. The reference has no GPU backward;
+ * this is the gradient autograd takes through conv1d + silu. */
+MQC_API int mqc_conv_silu_bwd(const void* x, int64_t x_row_stride, const float* weight,
+                              const float* bias, const void* dout, void* dx, float* dweight,
+                              float* dbias, int64_t batch, int64_t seq_len, int64_t channels,
+                              int64_t kernel_size, int dtype, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
+/* The scan's inputs from the dt_proj and gate_proj outputs, in one pass:
+ *   delta = softplus(u)  (torch's threshold 20: u above it passes through)
+ *   s     = sigmoid(gate) * x
+ * u, gate: `rows` rows of `channels` at their own row strides (elements); x, delta,
+ * s [rows, channels] contiguous; one dtype. Replaces block lines
+ * models/quaternion_mamba2_block.py:183 and 197-198. */
+MQC_API int mqc_scan_inputs_fwd(const void* u, int64_t u_row_stride, const void* gate,
+                                int64_t gate_row_stride, const void* x, void* delta, void* s,
+                                int64_t rows, int64_t channels, int dtype, void* stream);
+
+/* Backward of mqc_scan_inputs_fwd: du = ddelta * sigmoid(u) (ddelta where u > 20),
+ * dgate = ds * x * sigmoid(gate) * (1 - sigmoid(gate)), dx = ds * sigmoid(gate).
+ * ddelta or ds may be NULL (no gradient: zero). du, dgate, dx [rows, channels]
+ * contiguous. */
+MQC_API int mqc_scan_inputs_bwd(const void* u, int64_t u_row_stride, const void* gate,
+                                int64_t gate_row_stride, const void* x, const void* ddelta,
+                                const void* ds, void* du, void* dgate, void* dx, int64_t rows,
+                                int64_t channels, int dtype, void* stream);
+
+/* Output gate and residual of the block: out = x + sigmoid(z) * y.
+ * x, y, out [rows, cols] contiguous; z `cols` elements per row at a row stride of
+ * `z_row_stride` elements (the second half of the in_proj output, read in place);
+ * one dtype. Replaces block lines models/quaternion_mamba2_block.py:154-164. */
+MQC_API int mqc_gate_residual_fwd(const void* x, const void* z, int64_t z_row_stride,
+                                  const void* y, void* out, int64_t rows, int64_t cols, int dtype,
+                                  void* stream);
+
+/* Backward of mqc_gate_residual_fwd: dz = dout * y * sigmoid(z) * (1 - sigmoid(z)),
+ * dy = dout * sigmoid(z) (dx = dout needs no kernel). dz, dy [rows, cols] contiguous. */
+MQC_API int mqc_gate_residual_bwd(const void* z, int64_t z_row_stride, const void* y,
+                                  const void* dout, void* dz, void* dy, int64_t rows, int64_t cols,
+                                  int dtype, void* stream);
+
 /* ---- diagnostics ---------------------------------------------------------- */
 
 /* Launches a pure FP32 FMA-chain kernel (no memory traffic) that keeps every SM's

@@ -1,7 +1,8 @@
 """GPU kernels of the quaternion SSM hot path (drop-in for ``mambaqc.kernels``).
 
 Same exported names as the reference package (mambaqc/kernels/__init__.py:10-33),
-plus the fused ``ssm_scan_cayley``.
+plus the fused ``ssm_scan_cayley`` and the block's fused glue ops
+(``causal_conv1d_silu``, ``ssm_scan_inputs``, ``gate_residual``).
 """
 
 from .quaternion_ops import (
@@ -16,6 +17,7 @@ from .parallel_scan import parallel_scan_quaternion
 from .quaternion_norm import quaternion_layer_norm_fused
 from .ssm_fused import (ssm_step_fused, ssm_forward_fused, ssm_scan_cayley,
                         ssm_scan_cayley_from_host, ssm_step_cayley)
+from .block_fused import causal_conv1d_silu, gate_residual, ssm_scan_inputs
 
 # Importing the submodule ``quaternion_norm`` (the LayerNorm file) rebinds the
 # package attribute of that name to the module; bind the function again so that
@@ -36,4 +38,7 @@ __all__ = [
     "ssm_scan_cayley",
     "ssm_scan_cayley_from_host",
     "ssm_step_cayley",
+    "causal_conv1d_silu",
+    "ssm_scan_inputs",
+    "gate_residual",
 ]

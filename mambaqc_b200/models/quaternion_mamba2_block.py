@@ -14,8 +14,12 @@ same initial weights. The forward follows :124-230 with two differences:
   for expand_factor != 1; its Lite block slices the same way
   (quaternion_mamba2_lite_block.py:163).
 
-Projections, the causal conv and activations stay dense PyTorch ops (cuBLAS /
-cuDNN); the quaternion path (scan, LayerNorm) runs in ``libmambaqc_b200.so``.
+The projections stay dense PyTorch linears (cuBLAS). Everything between them
+runs in ``libmambaqc_b200.so``:
+* the causal conv + SiLU, read in place from the in_proj output;
+* the step sizes and gated signal (softplus, sigmoid gate);
+* the scan, the quaternion LayerNorm, and the output gate + residual.
+Each has a forward and a backward kernel.
 """
 
 from __future__ import annotations
@@ -24,6 +28,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from mambaqc_b200.kernels.block_fused import causal_conv1d_silu, gate_residual, ssm_scan_inputs
 from mambaqc_b200.kernels.ssm_fused import ssm_scan_cayley
 from mambaqc_b200.layers.causal_conv1d import CausalConv1d
 from mambaqc_b200.layers.quaternion_linear import (
@@ -72,18 +77,18 @@ class QuaternionMamba2Block(nn.Module):
     def forward(self, x: torch.Tensor, return_ssm_state: bool = False):
         xz = self.in_proj(x)
         x_inner, z = xz.chunk(2, dim=-1)
-        x_act = F.silu(self.conv1d(x_inner))
+        conv = self.conv1d.conv
+        x_act = causal_conv1d_silu(x_inner, conv.weight, conv.bias)
         y_quat, h_T = self._ssm_forward(x_act, return_state=True)
         y_real = self.out_proj(self.norm(y_quat))
-        out = x + torch.sigmoid(z[..., : self.d_model]) * y_real
+        out = gate_residual(x, z[..., : self.d_model], y_real)
         return (out, h_T) if return_ssm_state else out
 
     def _ssm_forward(self, x: torch.Tensor, return_state: bool = False):
         bsz, seqlen, d_inner = x.shape
-        delta = F.softplus(self.dt_proj(x))
+        delta, s_real = ssm_scan_inputs(self.dt_proj(x), self.gate_proj(x), x)
         Bq = self.B_proj(x).view(bsz, seqlen, d_inner, self.d_state, 4)
         Cq = self.C_proj(x).view(bsz, seqlen, d_inner, self.d_state, 4)
-        s_real = torch.sigmoid(self.gate_proj(x)) * x
         dt = Bq.dtype
         y, h_T = ssm_scan_cayley(delta.to(dt), self.ssm_lambda(), Bq, Cq.to(dt), s_real.to(dt),
                                  self.D, return_final_state=True)
