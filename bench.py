@@ -68,7 +68,7 @@ def parse_args():
                          "scan of the next segment")
     ap.add_argument("--decode-batch", type=int, default=4,
                     help="decode workload: sequences decoded together per GPU")
-    ap.add_argument("--workload", choices=["config3", "config5", "config2", "decode"],
+    ap.add_argument("--workload", choices=["config3", "config5", "config2", "decode", "block_glue"],
                     default="config3",
                     help="config5: B=1, T=65536, D=1536, N=64, bf16, channel-sharded over the "
                          "GPUs with an NCCL all-gather of y (strong scaling)")
@@ -723,6 +723,149 @@ def run_decode(args, world, rank, local):
     return 0
 
 
+def graph_replay_ms(fns, steps, world, stream, dev):
+    """Mean ms per call of the callables `fns`, captured once in a CUDA graph and
+    replayed (no host call overhead between kernels); max over ranks."""
+    k = len(fns)
+    for f in fns:
+        f()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for f in fns:
+            f()
+    reps = max(1, steps // k)
+    ms = timed(graph.replay, reps, 3, world, stream)
+    del graph
+    return max_over_ranks(ms / (reps * k), world, dev)
+
+
+def run_block_glue(args, world, rank, local):
+    """The block's fused glue kernels at the config-4 block shape (B=4, T=2048,
+    d_model=768, d_inner=1536) in --dtype, forward and backward, against the torch
+    ops of the reference block they replace, timed the same way (CUDA-graph
+    replay, input sets rotating over more than 2x L2). Algorithmic bytes = every
+    operand read once + every result written once."""
+    import torch.nn.functional as F
+
+    from mambaqc_b200.kernels import causal_conv1d_silu, gate_residual, ssm_scan_inputs
+    from mambaqc_b200.kernels.block_fused import _ConvSilu, _GateResidual, _ScanInputs
+
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    peaks, peak_kind = measured_peaks()
+    hbm = peaks["hbm_gbs"]
+    dt = torch.bfloat16 if args.dtype == "bf16" else torch.float32
+    es = 2 if dt == torch.bfloat16 else 4
+    bsz, seqlen, dmod, din, kc = 4, 2048, 768, 1536, 4
+    rows = bsz * seqlen
+    steps = max(8, min(args.steps, 64))
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def rnd(*shape):
+        return torch.randn(*shape, generator=g, device=dev).to(dt)
+
+    def nsets(bytes_per_set):
+        return max(2, -(-2 * (126 << 20) // bytes_per_set))
+
+    w = torch.randn(din, 1, kc, generator=g, device=dev) * 0.5
+    b = torch.randn(din, generator=g, device=dev) * 0.1
+    conv = torch.nn.Conv1d(din, din, kc, groups=din, bias=True).to(dev, dt)
+    with torch.no_grad():
+        conv.weight.copy_(w)
+        conv.bias.copy_(b)
+    res = {}
+    with torch.no_grad():
+        # conv + SiLU: x read in place from the [B,T,2*d_inner] in_proj output
+        n = nsets(rows * din * es * 4)
+        xz = [rnd(bsz, seqlen, 2 * din) for _ in range(n)]
+        fused = [(lambda t=t: causal_conv1d_silu(t[..., :din], w, b)) for t in xz]
+        torch_ops = [(lambda t=t: F.silu(conv(F.pad(t[..., :din].transpose(1, 2), (kc - 1, 0)))
+                                         .transpose(1, 2))) for t in xz]
+        res["conv_silu_fwd"] = {"ms": graph_replay_ms(fused, steps, world, stream, dev),
+                                "torch_ms": graph_replay_ms(torch_ops, steps, world, stream, dev),
+                                "bytes": 2 * rows * din * es}
+        gy = rnd(bsz, seqlen, din)
+
+        class _Ctx:
+            pass
+
+        def conv_bwd(t):
+            c = _Ctx()
+            c.saved_tensors = (t[..., :din], w.reshape(din, kc).contiguous(), b)
+            c.rs, c.shape, c.w_meta, c.b_dtype = 2 * din, (bsz, seqlen, din, kc), (w.shape, w.dtype), b.dtype
+            return _ConvSilu.backward(c, gy)
+        res["conv_silu_bwd"] = {"ms": graph_replay_ms([(lambda t=t: conv_bwd(t)) for t in xz],
+                                                      steps, world, stream, dev),
+                                "bytes": 3 * rows * din * es}
+        del xz
+        # scan inputs: delta = softplus(u), s = sigmoid(gate) * x
+        n = nsets(rows * din * es * 5)
+        sets = [(rnd(bsz, seqlen, din), rnd(bsz, seqlen, din), rnd(bsz, seqlen, din))
+                for _ in range(n)]
+        fused = [(lambda s=s: ssm_scan_inputs(*s)) for s in sets]
+        torch_ops = [(lambda s=s: (F.softplus(s[0]), torch.sigmoid(s[1]) * s[2])) for s in sets]
+        res["scan_inputs_fwd"] = {"ms": graph_replay_ms(fused, steps, world, stream, dev),
+                                  "torch_ms": graph_replay_ms(torch_ops, steps, world, stream, dev),
+                                  "bytes": 5 * rows * din * es}
+        gd, gs = rnd(bsz, seqlen, din), rnd(bsz, seqlen, din)
+
+        def si_bwd(s):
+            c = _Ctx()
+            c.saved_tensors = s
+            c.meta = (din, din, rows, din, dt, dt)
+            return _ScanInputs.backward(c, gd, gs)
+        res["scan_inputs_bwd"] = {"ms": graph_replay_ms([(lambda s=s: si_bwd(s)) for s in sets],
+                                                        steps, world, stream, dev),
+                                  "bytes": 8 * rows * din * es}
+        del sets
+        # output gate + residual, z read in place from the in_proj output
+        n = nsets(rows * dmod * es * 6)
+        sets = [(rnd(bsz, seqlen, dmod), rnd(bsz, seqlen, 2 * din), rnd(bsz, seqlen, dmod))
+                for _ in range(n)]
+        fused = [(lambda s=s: gate_residual(s[0], s[1][..., din:din + dmod], s[2])) for s in sets]
+        torch_ops = [(lambda s=s: s[0] + torch.sigmoid(s[1][..., din:din + dmod]) * s[2])
+                     for s in sets]
+        res["gate_residual_fwd"] = {"ms": graph_replay_ms(fused, steps, world, stream, dev),
+                                    "torch_ms": graph_replay_ms(torch_ops, steps, world, stream,
+                                                                dev),
+                                    "bytes": 4 * rows * dmod * es}
+        go = rnd(bsz, seqlen, dmod)
+
+        def gr_bwd(s):
+            c = _Ctx()
+            c.saved_tensors = (s[1][..., din:din + dmod], s[2])
+            c.meta = (2 * din, rows, dmod, dt, dt, dt)
+            return _GateResidual.backward(c, go)
+        res["gate_residual_bwd"] = {"ms": graph_replay_ms([(lambda s=s: gr_bwd(s)) for s in sets],
+                                                          steps, world, stream, dev),
+                                    "bytes": 5 * rows * dmod * es}
+        del sets
+    for v in res.values():
+        v["gbps"] = v["bytes"] / (v["ms"] / 1e3) / 1e9
+        v["frac_of_hbm"] = v["gbps"] / hbm
+        if "torch_ms" in v:
+            v["speedup_vs_torch_ops"] = v["torch_ms"] / v["ms"]
+    if rank == 0:
+        geo = math.exp(sum(math.log(v["frac_of_hbm"]) for v in res.values()) / len(res))
+        line = {
+            "metric": "block glue kernels (conv+SiLU, scan inputs, gate+residual; forward and "
+                      "backward), geometric mean fraction of measured HBM",
+            "value": geo, "unit": "fraction of measured HBM GB/s", "n_gpus": world,
+            "steps": steps, "warmup": 3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32" if dt == torch.float32 else "bf16",
+            "data": "synthetic (seeded N(0,1))",
+            "config": {"workload": "block_glue_config4_shape", "batch": bsz, "seq_len": seqlen,
+                       "d_model": dmod, "d_inner": din, "d_conv": kc,
+                       "l2": "input sets rotate over more than 2x L2"},
+            "hbm_peak_gbs": hbm, "hbm_peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+            "kernels": res, "gpu_launches": None,
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse_args()
     world, rank, local = dist_setup(args)
@@ -735,6 +878,8 @@ def main():
             return run_config2(args, world, rank, local)
         if args.workload == "decode":
             return run_decode(args, world, rank, local)
+        if args.workload == "block_glue":
+            return run_block_glue(args, world, rank, local)
         return run_b200(args, world, rank, local)
     finally:
         if dist.is_initialized():

@@ -10,11 +10,12 @@
 //   after the scan    gate_residual  out = x + sigmoid(z) * y   (block lines 154-164)
 //
 // Each forward has a backward kernel. All arithmetic is fp32; activations are
-// fp32 or bf16. A thread owns V = 4 adjacent channels (16-byte fp32 / 8-byte
-// bf16 vectors) when the widths and strides allow it, else one channel; warps
-// cover consecutive channel groups of one row, so every row access is
-// coalesced. The conv kernels keep the K-1 preceding inputs in registers and
-// walk a run of time steps, so x is read once plus a (K-1)-row halo per run.
+// fp32 or bf16. A thread owns one 16-byte vector of adjacent channels (4 fp32 or
+// 8 bf16) when the widths, strides and alignment allow it, else one channel;
+// warps cover consecutive channel groups of one row, so every row access is
+// coalesced. The conv kernels walk runs of time steps with the K-1 preceding
+// inputs in registers, so x is read once from HBM (the (K-1)-row halo of each
+// run is an L2 hit).
 #include <initializer_list>
 
 #include "mqc_common.cuh"
@@ -24,46 +25,111 @@ namespace mqc {
 namespace {
 
 constexpr int kMaxK = 8;
-constexpr int kFwdRun = 16;     // time steps per thread, forward conv
-constexpr int kBwdRun = 8;      // time steps per thread, backward conv
-constexpr int kBwdRunsPerCta = 8;
-constexpr int kBwdParts = 64;   // max CTAs along the run axis (rows of partial sums)
+constexpr int kFwdRun = 4;       // time steps per thread, forward conv
+constexpr int kBwdRun = 16;      // time steps per thread, backward conv
+constexpr int kBwdRunsPerCta = 4;
+constexpr int kBwdParts = 128;   // max CTAs along the run axis (rows of partial sums)
+constexpr int kConvThreads = 128;
 constexpr int kEwThreads = 256;
 
+// channels per thread on the 16-byte vector path
+template <typename T>
+constexpr int kVec = 16 / int(sizeof(T));
+
 template <typename T, int V>
-struct VIO {
-  static __device__ __forceinline__ void ld(const T* p, float (&v)[V]) {
-    if constexpr (V == 4) {
-      const float4 a = QIO<T>::ld(p);
-      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-    } else {
-      v[0] = QIO<T>::ld1(p);
-    }
+struct VIO;
+
+template <>
+struct VIO<float, 4> {
+  static __device__ __forceinline__ void ld(const float* p, float (&v)[4]) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
   }
-  static __device__ __forceinline__ void st(T* p, const float (&v)[V]) {
-    if constexpr (V == 4) {
-      QIO<T>::st(p, make_float4(v[0], v[1], v[2], v[3]));
-    } else {
-      QIO<T>::st1(p, v[0]);
-    }
+  static __device__ __forceinline__ void st(float* p, const float (&v)[4]) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
   }
 };
 
-__device__ __forceinline__ float sigmoid_f(float a) { return 1.f / (1.f + expf(-a)); }
+template <>
+struct VIO<__nv_bfloat16, 8> {
+  static __device__ __forceinline__ void ld(const __nv_bfloat16* p, float (&v)[8]) {
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
+    const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[2 * i] = __uint_as_float(w[i] << 16);
+      v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+  static __device__ __forceinline__ void st(__nv_bfloat16* p, const float (&v)[8]) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+};
+
+template <>
+struct VIO<__nv_bfloat16, 4> {
+  static __device__ __forceinline__ void ld(const __nv_bfloat16* p, float (&v)[4]) {
+    const float4 a = QIO<__nv_bfloat16>::ld(p);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  }
+  static __device__ __forceinline__ void st(__nv_bfloat16* p, const float (&v)[4]) {
+    QIO<__nv_bfloat16>::st(p, make_float4(v[0], v[1], v[2], v[3]));
+  }
+};
+
+template <typename T>
+struct VIO<T, 1> {
+  static __device__ __forceinline__ void ld(const T* p, float (&v)[1]) { v[0] = QIO<T>::ld1(p); }
+  static __device__ __forceinline__ void st(T* p, const float (&v)[1]) { QIO<T>::st1(p, v[0]); }
+};
+
+// 1 / (1 + e^-a): the fast exponential (__expf, relative error ~1e-6 over the
+// range where sigmoid is not saturated) and the Newton-refined reciprocal
+// (rcp_nr); 0 as a -> -inf. The accurate expf cost ~8 instructions per element
+// and left these streaming kernels issue-bound.
+__device__ __forceinline__ float sigmoid_f(float a) { return rcp_nr(1.f + __expf(-a)); }
 
 // torch.nn.functional.softplus with beta = 1, threshold = 20
 __device__ __forceinline__ float softplus_f(float u) { return u > 20.f ? u : log1pf(expf(u)); }
 
 // ---------------------------------------------------------------- conv + SiLU
 
-// grid (ceil(groups / blockDim.x), min(runs_total, 65535)); one thread per channel
-// group and run of kFwdRun steps, grid-stride over runs along y.
+// grid (ceil(groups / kConvThreads), ny); one thread per channel group walks
+// runs blockIdx.y, blockIdx.y + ny, ... of kFwdRun steps. The rows of the next
+// run are loaded before the current run is computed and stored, so every warp
+// keeps a run's loads in flight while it works (the kernel is latency-bound
+// without this: one run per thread left DRAM at ~20 % of peak).
 template <typename T, int V, int K>
-__global__ void __launch_bounds__(128)
+__device__ __forceinline__ void conv_fwd_load(const T* __restrict__ x, int64_t x_row, int seq_len,
+                                              int runs_per_seq, int c0, int r,
+                                              float (&xr)[kFwdRun + K - 1][V]) {
+  const int b = r / runs_per_seq;
+  const int t0 = (r - b * runs_per_seq) * kFwdRun;
+  const T* xb = x + int64_t(b) * seq_len * x_row + c0;
+#pragma unroll
+  for (int j = 0; j < kFwdRun + K - 1; ++j) {
+    const int t = t0 - (K - 1) + j;
+    if (t >= 0 && t < seq_len) {
+      VIO<T, V>::ld(xb + int64_t(t) * x_row, xr[j]);
+    } else {
+#pragma unroll
+      for (int v = 0; v < V; ++v) xr[j][v] = 0.f;
+    }
+  }
+}
+
+template <typename T, int V, int K>
+__global__ void __launch_bounds__(kConvThreads)
     conv_silu_fwd_kernel(const T* __restrict__ x, int64_t x_row, const float* __restrict__ w,
                          const float* __restrict__ bias, T* __restrict__ out, int seq_len,
-                         int channels, int runs_per_seq, int64_t runs_total) {
-  const int gi = blockIdx.x * blockDim.x + threadIdx.x;
+                         int channels, int runs_per_seq, int runs_total) {
+  const int gi = blockIdx.x * kConvThreads + threadIdx.x;
   const int c0 = gi * V;
   if (c0 >= channels) return;
   float wk[K][V], bb[V];
@@ -73,23 +139,16 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
     for (int k = 0; k < K; ++k) wk[k][v] = __ldg(w + (c0 + v) * K + k);
   }
-  for (int64_t r = blockIdx.y; r < runs_total; r += gridDim.y) {
-    const int64_t b = r / runs_per_seq;
-    const int t0 = int(r % runs_per_seq) * kFwdRun;
-    const T* xb = x + b * seq_len * x_row + c0;
-    T* ob = out + (b * seq_len) * int64_t(channels) + c0;
-    // rows t0-(K-1) .. t0+kFwdRun-1; rows before 0 or past the end read as 0
-    float xr[kFwdRun + K - 1][V];
-#pragma unroll
-    for (int j = 0; j < kFwdRun + K - 1; ++j) {
-      const int t = t0 - (K - 1) + j;
-      if (t >= 0 && t < seq_len) {
-        VIO<T, V>::ld(xb + int64_t(t) * x_row, xr[j]);
-      } else {
-#pragma unroll
-        for (int v = 0; v < V; ++v) xr[j][v] = 0.f;
-      }
-    }
+  // rows t0-(K-1) .. t0+kFwdRun-1 of a run; rows before 0 or past the end are 0
+  float cur[kFwdRun + K - 1][V], nxt[kFwdRun + K - 1][V];
+  int r = blockIdx.y;
+  if (r < runs_total) conv_fwd_load<T, V, K>(x, x_row, seq_len, runs_per_seq, c0, r, cur);
+  for (; r < runs_total; r += gridDim.y) {
+    const int rn = r + int(gridDim.y);
+    if (rn < runs_total) conv_fwd_load<T, V, K>(x, x_row, seq_len, runs_per_seq, c0, rn, nxt);
+    const int b = r / runs_per_seq;
+    const int t0 = (r - b * runs_per_seq) * kFwdRun;
+    T* ob = out + (int64_t(b) * seq_len) * int64_t(channels) + c0;
 #pragma unroll
     for (int i = 0; i < kFwdRun; ++i) {
       const int t = t0 + i;
@@ -99,26 +158,34 @@ __global__ void __launch_bounds__(128)
         for (int v = 0; v < V; ++v) {
           float a = bb[v];
 #pragma unroll
-          for (int k = 0; k < K; ++k) a = fmaf(wk[k][v], xr[i + k][v], a);
+          for (int k = 0; k < K; ++k) a = fmaf(wk[k][v], cur[i + k][v], a);
           o[v] = a * sigmoid_f(a);
         }
         VIO<T, V>::st(ob + int64_t(t) * channels, o);
       }
     }
+#pragma unroll
+    for (int j = 0; j < kFwdRun + K - 1; ++j)
+#pragma unroll
+      for (int v = 0; v < V; ++v) cur[j][v] = nxt[j][v];
   }
 }
 
 // block (32, kBwdRunsPerCta); grid (ceil(groups / 32), parts). Thread (x, y) owns
-// channel group blockIdx.x*32+x and runs y, y+parts*8, ... of kBwdRun steps; its
-// weight/bias gradient sums are reduced over y in shared memory and written as
-// one row of `part` [parts, channels, K+1] per CTA.
+// channel group blockIdx.x*32+x and runs y, y+parts*kBwdRunsPerCta, ... of
+// kBwdRun steps. A run walks t' = t0 .. t0+kBwdRun+K-2 with two rolling windows
+// of K rows: x rows t'-(K-1)..t' (the pre-activation at t') and pre-activation
+// gradients ga at t'-(K-1)..t'. Once ga(t') is known, dx at t = t'-(K-1) is
+// complete: x_t feeds outputs t..t+K-1, output t+(K-1)-k through weight k.
+// Weight/bias gradient sums over the run's own outputs are reduced over y in
+// shared memory and written as one row of `part` [parts, channels, K+1] per CTA.
 template <typename T, int V, int K>
 __global__ void __launch_bounds__(32 * kBwdRunsPerCta)
     conv_silu_bwd_kernel(const T* __restrict__ x, int64_t x_row, const float* __restrict__ w,
                          const float* __restrict__ bias, const T* __restrict__ dout,
                          T* __restrict__ dx, float* __restrict__ part, int seq_len, int channels,
                          int runs_per_seq, int64_t runs_total) {
-  __shared__ float red[kBwdRunsPerCta][32][(K + 1) * V];
+  __shared__ float red[kBwdRunsPerCta][32][(K + 1) * V + 1];
   const int gi = blockIdx.x * 32 + threadIdx.x;
   const int c0 = gi * V;
   const bool live = c0 < channels;
@@ -142,56 +209,68 @@ __global__ void __launch_bounds__(32 * kBwdRunsPerCta)
       const T* xb = x + b * seq_len * x_row + c0;
       const T* gb = dout + (b * seq_len) * int64_t(channels) + c0;
       T* dxb = dx + (b * seq_len) * int64_t(channels) + c0;
-      // x rows t0-(K-1) .. t0+kBwdRun+K-2, pre-activation gradients for rows
-      // t0 .. t0+kBwdRun+K-2 (the outputs that read this run's inputs)
-      constexpr int NX = kBwdRun + 2 * (K - 1);
-      constexpr int NG = kBwdRun + K - 1;
-      float xr[NX][V], ga[NG][V];
+      // before the first slide the x window holds rows t0-K .. t0-1
+      float xw[K][V], gw[K][V];
 #pragma unroll
-      for (int j = 0; j < NX; ++j) {
-        const int t = t0 - (K - 1) + j;
-        if (t >= 0 && t < seq_len) {
-          VIO<T, V>::ld(xb + int64_t(t) * x_row, xr[j]);
+      for (int j = 0; j < K; ++j) {
+        const int t = t0 - K + j;
+        if (t >= 0) {
+          VIO<T, V>::ld(xb + int64_t(t) * x_row, xw[j]);
         } else {
 #pragma unroll
-          for (int v = 0; v < V; ++v) xr[j][v] = 0.f;
+          for (int v = 0; v < V; ++v) xw[j][v] = 0.f;
         }
+#pragma unroll
+        for (int v = 0; v < V; ++v) gw[j][v] = 0.f;
       }
 #pragma unroll
-      for (int j = 0; j < NG; ++j) {
-        const int t = t0 + j;
-        if (t < seq_len) {
+      for (int j = 0; j < kBwdRun + K - 1; ++j) {
+        const int tp = t0 + j;
+        // slide both windows by one row
+#pragma unroll
+        for (int m = 0; m < K - 1; ++m)
+#pragma unroll
+          for (int v = 0; v < V; ++v) {
+            xw[m][v] = xw[m + 1][v];
+            gw[m][v] = gw[m + 1][v];
+          }
+        if (tp < seq_len) {
           float g[V];
-          VIO<T, V>::ld(gb + int64_t(t) * channels, g);
+          VIO<T, V>::ld(xb + int64_t(tp) * x_row, xw[K - 1]);
+          VIO<T, V>::ld(gb + int64_t(tp) * channels, g);
 #pragma unroll
           for (int v = 0; v < V; ++v) {
             float a = bb[v];
 #pragma unroll
-            for (int k = 0; k < K; ++k) a = fmaf(wk[k][v], xr[j + k][v], a);
+            for (int k = 0; k < K; ++k) a = fmaf(wk[k][v], xw[k][v], a);
             const float s = sigmoid_f(a);
-            ga[j][v] = g[v] * s * fmaf(a, 1.f - s, 1.f);
+            gw[K - 1][v] = g[v] * s * fmaf(a, 1.f - s, 1.f);
           }
         } else {
 #pragma unroll
-          for (int v = 0; v < V; ++v) ga[j][v] = 0.f;
+          for (int v = 0; v < V; ++v) {
+            xw[K - 1][v] = 0.f;
+            gw[K - 1][v] = 0.f;
+          }
         }
-      }
+        if (j < kBwdRun) {
+          // output t' is this run's: weight k met input t'-(K-1)+k
 #pragma unroll
-      for (int i = 0; i < kBwdRun; ++i) {
-        const int t = t0 + i;
-        if (t < seq_len) {
+          for (int v = 0; v < V; ++v) {
+#pragma unroll
+            for (int k = 0; k < K; ++k) acc[k][v] = fmaf(gw[K - 1][v], xw[k][v], acc[k][v]);
+            acc[K][v] += gw[K - 1][v];
+          }
+        }
+        const int t = tp - (K - 1);
+        if (j >= K - 1 && t < seq_len) {
           float o[V];
 #pragma unroll
           for (int v = 0; v < V; ++v) {
-            // x_t feeds output t + (K-1) - k through weight k
             float s = 0.f;
 #pragma unroll
-            for (int k = 0; k < K; ++k) s = fmaf(wk[k][v], ga[i + (K - 1) - k][v], s);
+            for (int k = 0; k < K; ++k) s = fmaf(wk[k][v], gw[K - 1 - k][v], s);
             o[v] = s;
-            // this run's outputs t: weight k met input t-(K-1)+k
-#pragma unroll
-            for (int k = 0; k < K; ++k) acc[k][v] = fmaf(ga[i][v], xr[i + k][v], acc[k][v]);
-            acc[K][v] += ga[i][v];
           }
           VIO<T, V>::st(dxb + int64_t(t) * channels, o);
         }
@@ -354,17 +433,22 @@ __global__ void __launch_bounds__(kEwThreads)
 
 // ---------------------------------------------------------------- host side
 
-// 4 channels per thread when every row start is 4-element aligned in memory
-bool vec4_ok(int64_t channels, int dtype, std::initializer_list<const void*> ptrs,
-             std::initializer_list<int64_t> strides) {
-  if (channels % 4 != 0) return false;
-  const uintptr_t al = uintptr_t(dtype_size(dtype)) * 4;
+// V channels per thread when the channel count, the strides (elements) and the
+// pointers allow V-element vectors: the elementwise kernels use 16-byte vectors
+// (4 fp32 / 8 bf16), the conv kernels 4 channels in both dtypes (their rolling
+// windows hold K rows of V values per thread).
+bool vec_ok(int64_t channels, int64_t V, int dtype, std::initializer_list<const void*> ptrs,
+            std::initializer_list<int64_t> strides) {
+  if (channels % V != 0) return false;
+  const uintptr_t al = uintptr_t(V) * uintptr_t(dtype_size(dtype));
   for (const void* p : ptrs)
     if (p != nullptr && !aligned(p, al)) return false;
   for (int64_t s : strides)
-    if (s % 4 != 0) return false;
+    if (s % V != 0) return false;
   return true;
 }
+
+int ew_vec(int dtype) { return 16 / dtype_size(dtype); }
 
 int ck_zero(float* p, size_t bytes, cudaStream_t st) {
   const cudaError_t e = cudaMemsetAsync(p, 0, bytes, st);
@@ -383,12 +467,22 @@ void launch_conv_fwd(const void* x, int64_t x_row, const float* w, const float* 
                      int64_t B, int64_t T_, int64_t D, cudaStream_t st) {
   const int groups = int(D / V);
   const int runs_per_seq = int((T_ + kFwdRun - 1) / kFwdRun);
-  const int64_t runs_total = B * runs_per_seq;
-  const unsigned gy = unsigned(runs_total < 65535 ? runs_total : 65535);
-  dim3 grid{unsigned((groups + 127) / 128), gy, 1u};
-  conv_silu_fwd_kernel<T, V, K><<<grid, 128, 0, st>>>(
+  const int64_t runs_total = B * runs_per_seq;  // <= INT32_MAX, checked by the entry point
+  // one wave of resident CTAs, each thread walking several runs
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, conv_silu_fwd_kernel<T, V, K>,
+                                                    kConvThreads, 0) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  const int gx = (groups + kConvThreads - 1) / kConvThreads;
+  int64_t gy = int64_t(num_sms()) * per_sm / gx;
+  if (gy < 1) gy = 1;
+  if (gy > runs_total) gy = runs_total;
+  if (gy > 65535) gy = 65535;
+  dim3 grid{unsigned(gx), unsigned(gy), 1u};
+  conv_silu_fwd_kernel<T, V, K><<<grid, kConvThreads, 0, st>>>(
       static_cast<const T*>(x), x_row, w, bias, static_cast<T*>(out), int(T_), int(D),
-      runs_per_seq, runs_total);
+      runs_per_seq, int(runs_total));
 }
 
 template <typename T, int V, int K>
@@ -453,8 +547,8 @@ int check_conv(const void* x, int64_t x_row, const float* w, int64_t B, int64_t 
               (long long)x_row, (long long)D);
   MQC_REQUIRE(B * T_ * D == 0 || (x != nullptr && w != nullptr), MQC_ERR_INVALID_VALUE,
               "%s: null pointer", name);
-  MQC_REQUIRE(T_ <= INT32_MAX && D <= INT32_MAX, MQC_ERR_UNSUPPORTED, "%s: sizes too large",
-              name);
+  MQC_REQUIRE(T_ <= INT32_MAX && D <= INT32_MAX && B * ((T_ + kFwdRun - 1) / kFwdRun) <= INT32_MAX,
+              MQC_ERR_UNSUPPORTED, "%s: sizes too large", name);
   return MQC_OK;
 }
 
@@ -482,7 +576,7 @@ extern "C" int mqc_conv_silu_fwd(const void* x, int64_t x_row_stride, const floa
   int rc = check_conv(x, x_row_stride, weight, batch, seq_len, channels, kernel_size, dtype, name);
   if (rc != MQC_OK || batch * seq_len * channels == 0) return rc;
   MQC_REQUIRE(out != nullptr, MQC_ERR_INVALID_VALUE, "%s: null out", name);
-  const bool v4 = vec4_ok(channels, dtype, {x, out}, {x_row_stride});
+  const bool v4 = vec_ok(channels, 4, dtype, {x, out}, {x_row_stride});
   rc = dispatch_conv<ConvFwd>(dtype, v4, kernel_size, x, x_row_stride, weight, bias, out, batch,
                               seq_len, channels, as_stream(stream));
   if (rc != MQC_OK) return rc;
@@ -520,7 +614,7 @@ extern "C" int mqc_conv_silu_bwd(const void* x, int64_t x_row_stride, const floa
               need);
   const int parts = conv_parts(batch, seq_len);
   float* part = static_cast<float*>(workspace);
-  const bool v4 = vec4_ok(channels, dtype, {x, dout, dx}, {x_row_stride});
+  const bool v4 = vec_ok(channels, 4, dtype, {x, dout, dx}, {x_row_stride});
   rc = dispatch_conv<ConvBwd>(dtype, v4, kernel_size, x, x_row_stride, weight, bias, dout, dx,
                               part, parts, batch, seq_len, channels, st);
   if (rc != MQC_OK) return rc;
@@ -541,8 +635,8 @@ extern "C" int mqc_scan_inputs_fwd(const void* u, int64_t u_row_stride, const vo
   if (rc != MQC_OK || rows * channels == 0) return rc;
   MQC_REQUIRE(u_row_stride >= channels && gate_row_stride >= channels, MQC_ERR_INVALID_VALUE,
               "%s: row stride below channels", name);
-  const bool v4 = vec4_ok(channels, dtype, {u, gate, x, delta, s}, {u_row_stride, gate_row_stride});
-  const int V = v4 ? 4 : 1;
+  const bool v4 = vec_ok(channels, ew_vec(dtype), dtype, {u, gate, x, delta, s}, {u_row_stride, gate_row_stride});
+  const int V = v4 ? ew_vec(dtype) : 1;
   const int g = ew_grid(rows * (channels / V));
   cudaStream_t st = as_stream(stream);
 #define MQC_SI_FWD(TT, VV)                                                                 \
@@ -553,7 +647,7 @@ extern "C" int mqc_scan_inputs_fwd(const void* u, int64_t u_row_stride, const vo
   if (dtype == MQC_DTYPE_F32) {
     if (v4) MQC_SI_FWD(float, 4); else MQC_SI_FWD(float, 1);
   } else {
-    if (v4) MQC_SI_FWD(__nv_bfloat16, 4); else MQC_SI_FWD(__nv_bfloat16, 1);
+    if (v4) MQC_SI_FWD(__nv_bfloat16, 8); else MQC_SI_FWD(__nv_bfloat16, 1);
   }
 #undef MQC_SI_FWD
   return check_launch(name);
@@ -569,9 +663,9 @@ extern "C" int mqc_scan_inputs_bwd(const void* u, int64_t u_row_stride, const vo
   if (rc != MQC_OK || rows * channels == 0) return rc;
   MQC_REQUIRE(u_row_stride >= channels && gate_row_stride >= channels, MQC_ERR_INVALID_VALUE,
               "%s: row stride below channels", name);
-  const bool v4 = vec4_ok(channels, dtype, {u, gate, x, ddelta, ds, du, dgate, dx},
+  const bool v4 = vec_ok(channels, ew_vec(dtype), dtype, {u, gate, x, ddelta, ds, du, dgate, dx},
                           {u_row_stride, gate_row_stride});
-  const int V = v4 ? 4 : 1;
+  const int V = v4 ? ew_vec(dtype) : 1;
   const int g = ew_grid(rows * (channels / V));
   cudaStream_t st = as_stream(stream);
 #define MQC_SI_BWD(TT, VV)                                                                    \
@@ -583,7 +677,7 @@ extern "C" int mqc_scan_inputs_bwd(const void* u, int64_t u_row_stride, const vo
   if (dtype == MQC_DTYPE_F32) {
     if (v4) MQC_SI_BWD(float, 4); else MQC_SI_BWD(float, 1);
   } else {
-    if (v4) MQC_SI_BWD(__nv_bfloat16, 4); else MQC_SI_BWD(__nv_bfloat16, 1);
+    if (v4) MQC_SI_BWD(__nv_bfloat16, 8); else MQC_SI_BWD(__nv_bfloat16, 1);
   }
 #undef MQC_SI_BWD
   return check_launch(name);
@@ -597,8 +691,8 @@ extern "C" int mqc_gate_residual_fwd(const void* x, const void* z, int64_t z_row
   int rc = check_ew(rows, cols, dtype, name, {x, z, y, out});
   if (rc != MQC_OK || rows * cols == 0) return rc;
   MQC_REQUIRE(z_row_stride >= cols, MQC_ERR_INVALID_VALUE, "%s: row stride below cols", name);
-  const bool v4 = vec4_ok(cols, dtype, {x, z, y, out}, {z_row_stride});
-  const int V = v4 ? 4 : 1;
+  const bool v4 = vec_ok(cols, ew_vec(dtype), dtype, {x, z, y, out}, {z_row_stride});
+  const int V = v4 ? ew_vec(dtype) : 1;
   const int g = ew_grid(rows * (cols / V));
   cudaStream_t st = as_stream(stream);
 #define MQC_GR_FWD(TT, VV)                                                                \
@@ -608,7 +702,7 @@ extern "C" int mqc_gate_residual_fwd(const void* x, const void* z, int64_t z_row
   if (dtype == MQC_DTYPE_F32) {
     if (v4) MQC_GR_FWD(float, 4); else MQC_GR_FWD(float, 1);
   } else {
-    if (v4) MQC_GR_FWD(__nv_bfloat16, 4); else MQC_GR_FWD(__nv_bfloat16, 1);
+    if (v4) MQC_GR_FWD(__nv_bfloat16, 8); else MQC_GR_FWD(__nv_bfloat16, 1);
   }
 #undef MQC_GR_FWD
   return check_launch(name);
@@ -622,8 +716,8 @@ extern "C" int mqc_gate_residual_bwd(const void* z, int64_t z_row_stride, const 
   int rc = check_ew(rows, cols, dtype, name, {z, y, dout, dz, dy});
   if (rc != MQC_OK || rows * cols == 0) return rc;
   MQC_REQUIRE(z_row_stride >= cols, MQC_ERR_INVALID_VALUE, "%s: row stride below cols", name);
-  const bool v4 = vec4_ok(cols, dtype, {z, y, dout, dz, dy}, {z_row_stride});
-  const int V = v4 ? 4 : 1;
+  const bool v4 = vec_ok(cols, ew_vec(dtype), dtype, {z, y, dout, dz, dy}, {z_row_stride});
+  const int V = v4 ? ew_vec(dtype) : 1;
   const int g = ew_grid(rows * (cols / V));
   cudaStream_t st = as_stream(stream);
 #define MQC_GR_BWD(TT, VV)                                                                 \
@@ -634,7 +728,7 @@ extern "C" int mqc_gate_residual_bwd(const void* z, int64_t z_row_stride, const 
   if (dtype == MQC_DTYPE_F32) {
     if (v4) MQC_GR_BWD(float, 4); else MQC_GR_BWD(float, 1);
   } else {
-    if (v4) MQC_GR_BWD(__nv_bfloat16, 4); else MQC_GR_BWD(__nv_bfloat16, 1);
+    if (v4) MQC_GR_BWD(__nv_bfloat16, 8); else MQC_GR_BWD(__nv_bfloat16, 1);
   }
 #undef MQC_GR_BWD
   return check_launch(name);
