@@ -68,6 +68,9 @@ def parse_args():
                          "scan of the next segment")
     ap.add_argument("--decode-batch", type=int, default=4,
                     help="decode workload: sequences decoded together per GPU")
+    ap.add_argument("--shard", choices=["channel", "time"], default="channel",
+                    help="config5 on >1 GPU: channel shards with y all-gathered, or time "
+                         "shards exchanging range summaries (y then all-gathered too)")
     ap.add_argument("--workload", choices=["config3", "config5", "config2", "decode", "block_glue"],
                     default="config3",
                     help="config5: B=1, T=65536, D=1536, N=64, bf16, channel-sharded over the "
@@ -569,6 +572,74 @@ def run_config5(args, world, rank, local):
     return 0
 
 
+def run_config5_time(args, world, rank, local):
+    """Config 5 split by time: rank r holds steps [r*T/G, (r+1)*T/G) of all D
+    channels. One step = range summary (state-only pass) + all-gather of the
+    summaries + carry + scan of the range from its start state, then an NCCL
+    all-gather of y so that every rank holds y [1, T, D, 4], as in the
+    channel-sharded form; the time without that gather is reported beside it."""
+    from mambaqc_b200.kernels.sharded import ssm_scan_cayley_time_sharded
+
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    if C5_SEQ % world:
+        raise SystemExit(f"{C5_SEQ} steps do not split over {world} GPUs")
+    tl = C5_SEQ // world
+    g = torch.Generator(device=dev).manual_seed(77)
+    bf = torch.bfloat16
+    Bm = (torch.randn(1, tl, STATE, 4, generator=g, device=dev) / math.sqrt(STATE)).to(bf)
+    Cm = (torch.randn(1, tl, STATE, 4, generator=g, device=dev) / math.sqrt(STATE)).to(bf)
+    g.manual_seed(1000 + rank)
+    x = torch.randn(1, tl, CHANNELS, generator=g, device=dev).to(bf)
+    delta = torch.nn.functional.softplus(
+        torch.randn(1, tl, CHANNELS, generator=g, device=dev) - 3.0).to(bf)
+    g.manual_seed(99)  # Lambda is the same on every rank
+    lam = torch.empty(CHANNELS, STATE, 4, device=dev)
+    u = torch.rand(CHANNELS, STATE, generator=g, device=dev)
+    lam[..., 0] = -torch.exp(u * (math.log(1e-1) - math.log(1e-3)) + math.log(1e-3))
+    lam[..., 1:] = 0.5 * torch.randn(CHANNELS, STATE, 3, generator=g, device=dev)
+    Dk = torch.ones(CHANNELS, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    y_full = torch.empty(world, tl, CHANNELS, 4, dtype=bf, device=dev)
+    out = {}
+
+    def scan_only():
+        out["y"], out["hT"] = ssm_scan_cayley_time_sharded(delta, lam, Bm, Cm, x, Dk)
+
+    def step():
+        scan_only()
+        if world > 1:
+            dist.all_gather_into_tensor(y_full, out["y"][0])
+        else:
+            y_full[0].copy_(out["y"][0])
+
+    with torch.no_grad():
+        step()
+        torch.cuda.synchronize()
+        steps = max(3, min(args.steps, 20))
+        ms_max = max_over_ranks(timed(step, steps, max(3, args.warmup), world, stream) / steps,
+                                world, dev)
+        ms_scan_max = max_over_ranks(timed(scan_only, steps, 3, world, stream) / steps, world,
+                                     dev)
+    if rank == 0:
+        line = {
+            "metric": "config5 long-sequence scan forward tokens/s (B=1, T=65536, D=1536, N=64, "
+                      "time-sharded, y all-gathered)",
+            "value": C5_SEQ / (ms_max / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": steps, "warmup": max(3, args.warmup), "ms_per_step": ms_max,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16 inputs, f32 state", "data": "synthetic (seeded, config-3 distributions)",
+            "config": {"workload": "config5_time_sharded", "batch": 1, "seq_len": C5_SEQ,
+                       "d_inner": CHANNELS, "d_state": STATE, "steps_per_gpu": tl,
+                       "parallelism": f"time shards x{world}: range summary, NCCL all-gather of "
+                                      "the summaries (P, E), carry, range scan; then an NCCL "
+                                      "all-gather of y"},
+            "without_y_gather_ms": ms_scan_max,
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_config2(args, world, rank, local):
     """Config 2: the quaternion primitives on their own, each timed with one pair
     of CUDA events around K back-to-back launches (replays of a CUDA graph of the
@@ -872,6 +943,8 @@ def main():
     try:
         if args.impl == "reference":
             return run_reference(args, world, rank)
+        if args.workload == "config5" and args.shard == "time":
+            return run_config5_time(args, world, rank, local)
         if args.workload == "config5":
             return run_config5(args, world, rank, local)
         if args.workload == "config2":

@@ -206,6 +206,34 @@ MQC_API size_t mqc_ssm_scan_fwd_chunked_workspace_size(int64_t batch, int64_t ch
 MQC_API int mqc_ssm_scan_fwd_chunked(const mqc_ssm_scan_args* args, int64_t nchunks,
                                      void* workspace, size_t workspace_bytes, void* stream);
 
+/* Summary of a time range for a time-sharded scan. The scan is affine in the
+ * state, so over the steps in `args` it is h -> P (x) h + E, where
+ *   P = q_{T-1} (x) ... (x) q_0 (the step operators, later on the left);
+ *   E = the final state reached from h = 0.
+ * Writes P and E [B, D, N, 4] fp32 and no y. args->h0, hT and ckpt must be NULL;
+ * args->y is ignored. With nchunks > 1 the range is scanned in nchunks
+ * time-parallel chunks whose summaries are then composed; that needs a
+ * caller-owned workspace of mqc_ssm_scan_fwd_summary_workspace_size(...)
+ * bytes. No counterpart in the reference, which has no multi-GPU path; it is
+ * the exchange step of the time-sharded scan of QuaternionMamba2Block._ssm_forward
+ * (models/quaternion_mamba2_block.py:214-228). */
+MQC_API size_t mqc_ssm_scan_fwd_summary_workspace_size(int64_t batch, int64_t channels,
+                                                       int64_t d_state, int64_t nchunks);
+MQC_API int mqc_ssm_scan_fwd_summary(const mqc_ssm_scan_args* args, int64_t nchunks, float* P,
+                                     float* E, void* workspace, size_t workspace_bytes,
+                                     void* stream);
+
+/* Start states of consecutive time segments from their summaries
+ * (mqc_ssm_scan_fwd_summary):
+ *   H_0 = h0 (zero if NULL);  H_{s+1} = P_s (x) H_s + E_s;
+ *   hin[s] = H_s;  hT = H_segments.
+ * P, E, hin [segments, batch, lanes, 4] fp32 (segment-major, as an all-gather
+ * of per-rank summaries lays them out); h0, hT [batch, lanes, 4] fp32; hin or
+ * hT may be NULL. No counterpart in the reference. */
+MQC_API int mqc_ssm_scan_carry(const float* P, const float* E, const float* h0, float* hin,
+                               float* hT, int64_t segments, int64_t batch, int64_t lanes,
+                               void* stream);
+
 /*
  * Backward of mqc_ssm_scan_fwd without Q_GIVEN (the fused Cayley form). The
  * reference has no GPU backward (its Triton kernels are not differentiable);

@@ -109,10 +109,15 @@ _SIGNATURES.update({
                               _i32, _c_void_p],
     "mqc_gate_residual_bwd": [_c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                               _i64, _i64, _i32, _c_void_p],
+    "mqc_ssm_scan_fwd_summary": [ctypes.POINTER(SsmScanArgs), _i64, _c_void_p, _c_void_p,
+                                 _c_void_p, ctypes.c_size_t, _c_void_p],
+    "mqc_ssm_scan_carry": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64,
+                           _i64, _c_void_p],
 })
 _SIZE_FUNCS = {"mqc_qln_bwd_workspace_size": [_i64, _i64],
                "mqc_ssm_scan_fwd_chunked_workspace_size": [_i64, _i64, _i64, _i64],
-               "mqc_conv_silu_bwd_workspace_size": [_i64, _i64, _i64, _i64]}
+               "mqc_conv_silu_bwd_workspace_size": [_i64, _i64, _i64, _i64],
+               "mqc_ssm_scan_fwd_summary_workspace_size": [_i64, _i64, _i64, _i64]}
 _STR_FUNCS = {"mqc_version": [], "mqc_status_string": [_i32], "mqc_last_error": []}
 
 _lock = threading.Lock()

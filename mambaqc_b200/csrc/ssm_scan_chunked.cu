@@ -39,6 +39,47 @@ __global__ void __launch_bounds__(kCarryThreads)
   if (hT != nullptr) QIO<float>::st(hT + (b * lanes + l) * 4, H);
 }
 
+// Composition of chunk summaries into one: over c = 0 .. nc-1,
+// Q <- P_c (x) Q (Q = 1 at first), E <- P_c (x) E + hloc_c (E = 0 at first).
+// grid (ceil(lanes / 256), batch); P, hloc: [batch, nc, lanes, 4]; Pout, Eout: [batch, lanes, 4]
+__global__ void __launch_bounds__(kCarryThreads)
+    chunk_compose_kernel(const float* __restrict__ P, const float* __restrict__ hloc,
+                         float* __restrict__ Pout, float* __restrict__ Eout, int nc,
+                         int64_t lanes) {
+  const int64_t l = int64_t(blockIdx.x) * kCarryThreads + threadIdx.x;
+  if (l >= lanes) return;
+  const int64_t b = blockIdx.y;
+  float4 Q = make_float4(1.f, 0.f, 0.f, 0.f);
+  float4 E = f4_zero();
+  for (int c = 0; c < nc; ++c) {
+    const int64_t idx = ((b * nc + c) * lanes + l) * 4;
+    const float4 Pc = QIO<float>::ld(P + idx);
+    E = qmul_acc(Pc, E, QIO<float>::ld(hloc + idx));
+    Q = qmul(Pc, Q);
+  }
+  QIO<float>::st(Pout + (b * lanes + l) * 4, Q);
+  QIO<float>::st(Eout + (b * lanes + l) * 4, E);
+}
+
+// Start states of consecutive time segments from their summaries:
+// H_0 = h0 (or 0), H_{s+1} = P_s (x) H_s + E_s; hin[s] = H_s, hT = H_S.
+// grid (ceil(lanes / 256), batch); P, E, hin: [segments, batch, lanes, 4]
+__global__ void __launch_bounds__(kCarryThreads)
+    segment_carry_kernel(const float* __restrict__ P, const float* __restrict__ E,
+                         const float* __restrict__ h0, float* __restrict__ hin,
+                         float* __restrict__ hT, int segments, int batch, int64_t lanes) {
+  const int64_t l = int64_t(blockIdx.x) * kCarryThreads + threadIdx.x;
+  if (l >= lanes) return;
+  const int64_t b = blockIdx.y;
+  float4 H = h0 != nullptr ? QIO<float>::ld(h0 + (b * lanes + l) * 4) : f4_zero();
+  for (int sg = 0; sg < segments; ++sg) {
+    const int64_t idx = ((int64_t(sg) * batch + b) * lanes + l) * 4;
+    if (hin != nullptr) QIO<float>::st(hin + idx, H);
+    H = qmul_acc(QIO<float>::ld(P + idx), H, QIO<float>::ld(E + idx));
+  }
+  if (hT != nullptr) QIO<float>::st(hT + (b * lanes + l) * 4, H);
+}
+
 size_t chunked_workspace(int64_t batch, int64_t nchunks, int64_t lanes) {
   return size_t(3) * size_t(batch) * size_t(nchunks) * size_t(lanes) * 16;
 }
@@ -119,4 +160,95 @@ extern "C" int mqc_ssm_scan_fwd_chunked(const mqc_ssm_scan_args* a, int64_t nchu
   a2.h0 = hin;
   a2.hT = nullptr;
   return mqc_ssm_scan_fwd(&a2, stream);
+}
+
+extern "C" size_t mqc_ssm_scan_fwd_summary_workspace_size(int64_t batch, int64_t channels,
+                                                          int64_t d_state, int64_t nchunks) {
+  if (batch <= 0 || channels <= 0 || d_state <= 0 || nchunks <= 1) return 0;
+  return size_t(2) * size_t(batch) * size_t(nchunks) * size_t(channels * d_state) * 16;
+}
+
+extern "C" int mqc_ssm_scan_fwd_summary(const mqc_ssm_scan_args* a, int64_t nchunks, float* P,
+                                        float* E, void* workspace, size_t workspace_bytes,
+                                        void* stream) {
+  clear_error();
+  const char* name = "mqc_ssm_scan_fwd_summary";
+  MQC_REQUIRE(a != nullptr, MQC_ERR_INVALID_VALUE, "%s: null args", name);
+  MQC_REQUIRE(!(a->flags & MQC_SSM_Q_GIVEN), MQC_ERR_UNSUPPORTED,
+              "%s: explicit q is not supported (use the fused form)", name);
+  MQC_REQUIRE(a->ckpt == nullptr && a->h0 == nullptr && a->hT == nullptr,
+              MQC_ERR_INVALID_VALUE, "%s: h0, hT and ckpt must be NULL (the summary is the map "
+              "from the zero state)", name);
+  MQC_REQUIRE(nchunks >= 1, MQC_ERR_INVALID_VALUE, "%s: nchunks must be >= 1", name);
+  MQC_REQUIRE(P != nullptr && E != nullptr && aligned(P, 16) && aligned(E, 16),
+              MQC_ERR_INVALID_VALUE, "%s: P and E must be 16-byte aligned device buffers", name);
+  // y is not written; the caller's y (or P, when it has none) only passes the checks
+  mqc_ssm_scan_args av = *a;
+  if (av.y == nullptr) av.y = P;
+  FwdParams p{};
+  int rc = validate_and_fill(&av, &p, name);
+  if (rc != MQC_OK || p.B == 0 || p.D == 0) return rc;
+  cudaStream_t st = as_stream(stream);
+  const int64_t lanes = int64_t(p.D) * p.N;
+  if (p.T == 0) {
+    // empty sequence: the identity map
+    dim3 grid{unsigned((lanes + kCarryThreads - 1) / kCarryThreads), unsigned(p.B), 1u};
+    chunk_compose_kernel<<<grid, kCarryThreads, 0, st>>>(P, E, P, E, 0, lanes);
+    return check_launch(name);
+  }
+  MQC_REQUIRE(p.T % nchunks == 0, MQC_ERR_INVALID_VALUE, "%s: seq_len %d not divisible by %lld",
+              name, p.T, (long long)nchunks);
+  MQC_REQUIRE(int64_t(p.B) * nchunks <= 65535, MQC_ERR_UNSUPPORTED,
+              "%s: batch * nchunks must be <= 65535", name);
+  const bool s_real = a->flags & MQC_SSM_S_REAL;
+  const bool shared = a->flags & MQC_SSM_BC_SHARED;
+  float* Pc = P;
+  float* Ec = E;
+  if (nchunks > 1) {
+    const size_t need = mqc_ssm_scan_fwd_summary_workspace_size(p.B, p.D, p.N, nchunks);
+    MQC_REQUIRE(workspace != nullptr && workspace_bytes >= need && aligned(workspace, 16),
+                MQC_ERR_INVALID_VALUE, "%s: 16-byte aligned workspace of %zu bytes required",
+                name, need);
+    Pc = static_cast<float*>(workspace);
+    Ec = Pc + size_t(p.B) * nchunks * lanes * 4;
+  }
+  FwdParams p1 = p;
+  p1.B = int(int64_t(p.B) * nchunks);
+  p1.T = int(p.T / nchunks);
+  p1.h0 = nullptr;
+  p1.hT = Ec;
+  p1.pout = Pc;
+  p1.y = nullptr;
+  p1.ckpt = nullptr;
+  p1.nck = 0;
+  const char* impl = getenv("MQC_SCAN_IMPL");
+  const bool packed = shared && (impl == nullptr || impl[0] == '\0');
+  rc = packed ? dispatch_state_only_packed(p1, a->dtype, s_real, st)
+              : dispatch_state_only(p1, a->dtype, s_real, shared, st);
+  if (rc != MQC_OK || nchunks == 1) return rc;
+  dim3 grid{unsigned((lanes + kCarryThreads - 1) / kCarryThreads), unsigned(p.B), 1u};
+  chunk_compose_kernel<<<grid, kCarryThreads, 0, st>>>(Pc, Ec, P, E, int(nchunks), lanes);
+  return check_launch(name);
+}
+
+extern "C" int mqc_ssm_scan_carry(const float* P, const float* E, const float* h0, float* hin,
+                                  float* hT, int64_t segments, int64_t batch, int64_t lanes,
+                                  void* stream) {
+  clear_error();
+  const char* name = "mqc_ssm_scan_carry";
+  MQC_REQUIRE(segments >= 0 && batch >= 0 && lanes >= 0, MQC_ERR_INVALID_VALUE,
+              "%s: negative size", name);
+  MQC_REQUIRE(segments <= INT32_MAX && batch <= 65535, MQC_ERR_UNSUPPORTED,
+              "%s: sizes too large", name);
+  if (batch == 0 || lanes == 0) return MQC_OK;
+  MQC_REQUIRE(segments == 0 || (P != nullptr && E != nullptr), MQC_ERR_INVALID_VALUE,
+              "%s: null P or E", name);
+  MQC_REQUIRE((P == nullptr || aligned(P, 16)) && (E == nullptr || aligned(E, 16)) &&
+                  (h0 == nullptr || aligned(h0, 16)) && (hin == nullptr || aligned(hin, 16)) &&
+                  (hT == nullptr || aligned(hT, 16)),
+              MQC_ERR_MISALIGNED, "%s: buffers must be 16-byte aligned", name);
+  dim3 grid{unsigned((lanes + kCarryThreads - 1) / kCarryThreads), unsigned(batch), 1u};
+  segment_carry_kernel<<<grid, kCarryThreads, 0, as_stream(stream)>>>(
+      P, E, h0, hin, hT, int(segments), int(batch), lanes);
+  return check_launch(name);
 }

@@ -1,4 +1,4 @@
-"""Channel-sharded scan across GPUs (one process per GPU, NCCL over NVLink).
+"""Channel- and time-sharded scans across GPUs (one process per GPU, NCCL over NVLink).
 
 Every (batch, channel) recurrence of the scan is independent, so a long
 sequence is split over GPUs by channel: rank r holds channels
@@ -6,6 +6,14 @@ sequence is split over GPUs by channel: rank r holds channels
 locally (time-parallel when the shard is too narrow to fill the GPU), and one
 all-gather over the process group returns the full output to every rank. There
 is no exchange inside the scan; the all-gather is the only collective.
+
+A sequence can also be split by time (``ssm_scan_cayley_time_sharded``): rank r
+holds time range r of every input. The scan is affine in the state, so each
+rank first summarises its range as h -> P (x) h + E (a state-only pass from
+zero), the ranks all-gather the summaries (2 x B*D*N quaternions each, a few
+MB), every rank folds the summaries of the ranks before it into its start
+state, and then scans its range from that state. y stays time-sharded; the
+final state of the whole sequence is known on every rank.
 """
 
 from __future__ import annotations
@@ -15,7 +23,8 @@ from typing import Callable
 import torch
 import torch.distributed as dist
 
-__all__ = ["channel_shard", "ssm_scan_cayley_channel_sharded"]
+__all__ = ["channel_shard", "time_shard", "ssm_scan_cayley_channel_sharded",
+           "ssm_scan_cayley_time_sharded"]
 
 
 def channel_shard(t: torch.Tensor, rank: int, world: int, dim: int) -> torch.Tensor:
@@ -25,6 +34,11 @@ def channel_shard(t: torch.Tensor, rank: int, world: int, dim: int) -> torch.Ten
         raise ValueError(f"{n} channels do not split evenly over {world} ranks")
     k = n // world
     return t.narrow(dim, rank * k, k)
+
+
+def time_shard(t: torch.Tensor, rank: int, world: int, dim: int = 1) -> torch.Tensor:
+    """The rank's equal slice of ``t`` along the time dimension ``dim``."""
+    return channel_shard(t, rank, world, dim)
 
 
 _side_streams: dict[int, torch.cuda.Stream] = {}
@@ -107,3 +121,59 @@ def ssm_scan_cayley_channel_sharded(delta: torch.Tensor, Lambda: torch.Tensor, B
             b.record_stream(comm)
         compute.wait_stream(comm)
     return y
+
+
+def ssm_scan_cayley_time_sharded(delta: torch.Tensor, Lambda: torch.Tensor, B: torch.Tensor,
+                                 C: torch.Tensor, S: torch.Tensor, D: torch.Tensor,
+                                 h0: torch.Tensor | None = None, group=None,
+                                 time_chunks: int | str = "auto",
+                                 summary_fn: Callable | None = None,
+                                 carry_fn: Callable | None = None,
+                                 scan_fn: Callable | None = None):
+    """Scan this rank's time range of a sequence split by time over ``group``.
+
+    The inputs are time shards: delta [B, T/world, D], B/C [B, T/world, N, 4] (or
+    per-channel), S [B, T/world, D(,4)], in rank order = time order. Lambda
+    [D, N, 4] and the skip D [D] are the full tensors, held on every rank.
+    h0 [B, D, N, 4] is the state before step 0, or None.
+
+    Returns (y, h_T):
+    - y [B, T/world, D, 4] is this rank's time range of the output;
+    - h_T is the state after the last step of the whole sequence, the same on
+      every rank.
+
+    The only collective is one all-gather each of the range summaries P and E,
+    fp32 [B, D, N, 4] per rank.
+
+    ``summary_fn(delta, Lambda, B, C, S, D) -> (P, E)``,
+    ``carry_fn(P_all, E_all, h0) -> (hin, h_T)`` and
+    ``scan_fn(delta, Lambda, B, C, S, D, h0) -> (y, h_T)`` replace the GPU
+    summary, carry and scan (defaults: ``ssm_scan_summary``,
+    ``ssm_scan_carry`` and ``ssm_scan_cayley`` with ``time_chunks``).
+    """
+    from .ssm_fused import ssm_scan_carry, ssm_scan_cayley, ssm_scan_summary
+
+    if summary_fn is None:
+        def summary_fn(d, L, Bm, Cm, s, Dk):
+            return ssm_scan_summary(d, L, Bm, Cm, s, Dk, time_chunks=time_chunks)
+    if carry_fn is None:
+        carry_fn = ssm_scan_carry
+    if scan_fn is None:
+        def scan_fn(d, L, Bm, Cm, s, Dk, hs=None):
+            return ssm_scan_cayley(d, L, Bm, Cm, s, Dk, h0=hs, return_final_state=True,
+                                   time_chunks=time_chunks)
+
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    if world == 1:
+        return scan_fn(delta, Lambda, B, C, S, D, h0)
+    rank = dist.get_rank(group)
+    P, E = summary_fn(delta, Lambda, B, C, S, D)
+    P_all = torch.empty((world,) + tuple(P.shape), dtype=P.dtype, device=P.device)
+    E_all = torch.empty_like(P_all)
+    dist.all_gather_into_tensor(P_all.view(world * P.shape[0], *P.shape[1:]), P.contiguous(),
+                                group=group)
+    dist.all_gather_into_tensor(E_all.view(world * E.shape[0], *E.shape[1:]), E.contiguous(),
+                                group=group)
+    hin, hT = carry_fn(P_all, E_all, h0)
+    y, _ = scan_fn(delta, Lambda, B, C, S, D, hin[rank])
+    return y, hT

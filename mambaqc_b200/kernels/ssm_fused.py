@@ -250,6 +250,79 @@ def _run_scan_chunked(delta, Lam, B, C, S, D, h0, eps, nchunks, return_final_sta
     return y, hT
 
 
+def ssm_scan_summary(delta: torch.Tensor, Lambda: torch.Tensor, B: torch.Tensor,
+                     C: torch.Tensor, S: torch.Tensor, D: torch.Tensor, eps: float = 1e-6,
+                     time_chunks: int | str = "auto"):
+    """The affine map of a time range of the scan (no autograd).
+
+    Over the steps of the inputs (shapes as in ``ssm_scan_cayley``) the state
+    evolves as h -> P (x) h + E. Returns (P, E), both fp32 [B, D, N, 4]:
+    - P = q_{T-1} (x) ... (x) q_0;
+    - E = the final state reached from h = 0.
+
+    A time-sharded scan exchanges these summaries between ranks
+    (``mqc_ssm_scan_fwd_summary``). ``time_chunks`` splits the range
+    time-parallel, as in ``ssm_scan_cayley``.
+    """
+    dt = delta.dtype
+    bsz, seqlen, dm = delta.shape
+    ds = Lambda.shape[1]
+    shared = B.dim() == 4
+    _lib.require_cuda(delta, Lambda, B, C, S, D, what="ssm_scan_summary")
+    nc = (auto_time_chunks(bsz, seqlen, dm, ds, delta.device) if time_chunks == "auto"
+          else int(time_chunks))
+    if seqlen == 0 or seqlen % nc:
+        nc = 1
+    va = _vec_align(dt)
+    dc = _prep(delta, 4)
+    Lc = _prep(Lambda.float(), 16)
+    Bc = _prep(B, 16 if shared else va)
+    Cc = _prep(C, 16 if shared else va)
+    Sc = _prep(S, va)
+    Df, dsb, dst, dsd = _skip_operand(D, bsz, seqlen, dm)
+    P = torch.empty(bsz, dm, ds, 4, dtype=torch.float32, device=delta.device)
+    E = torch.empty_like(P)
+    lib = _lib.load()
+    ws_bytes = lib.mqc_ssm_scan_fwd_summary_workspace_size(bsz, dm, ds, nc)
+    ws = torch.empty(max(4, ws_bytes // 4), dtype=torch.float32, device=delta.device)
+    flags = (_lib.MQC_SSM_BC_SHARED if shared else 0) | (_lib.MQC_SSM_S_REAL if S.dim() == 3 else 0)
+    status = _lib.status_word(delta.device)
+    a = _lib.SsmScanArgs(
+        batch=bsz, seq_len=seqlen, channels=dm, d_state=ds, dtype=_lib.dtype_code(dc),
+        flags=flags, eps=float(eps), reserved0=0, delta=dc.data_ptr(), lambda_=Lc.data_ptr(),
+        q=None, Bm=Bc.data_ptr(), Cm=Cc.data_ptr(), s=Sc.data_ptr(), dskip=Df.data_ptr(),
+        dskip_sb=dsb, dskip_st=dst, dskip_sd=dsd, h0=None, y=None, hT=None,
+        status=status.data_ptr(), wait_poll_limit=-1, ckpt=None, ckpt_every=0)
+    with torch.cuda.device(delta.device):
+        _lib.call("mqc_ssm_scan_fwd_summary", ctypes.byref(a), int(nc), P.data_ptr(),
+                  E.data_ptr(), ws.data_ptr(), ws_bytes, _lib.stream_ptr(delta.device))
+    if _lib.sync_checks_enabled():
+        _lib.check_device_status(delta.device)
+    return P, E
+
+
+def ssm_scan_carry(P: torch.Tensor, E: torch.Tensor, h0: torch.Tensor | None = None):
+    """Start states of consecutive time segments from their summaries.
+
+    P, E [S, B, D, N, 4] fp32 (segment s = time range s, in order); h0
+    [B, D, N, 4] or None (zero). Returns (hin [S, B, D, N, 4], h_T [B, D, N, 4]):
+    H_0 = h0, H_{s+1} = P_s (x) H_s + E_s, hin[s] = H_s, h_T = H_S
+    (``mqc_ssm_scan_carry``).
+    """
+    assert P.shape == E.shape and P.dim() == 5 and P.shape[-1] == 4
+    _lib.require_cuda(P, E, h0, what="ssm_scan_carry")
+    nseg, bsz, dm, ds, _ = P.shape
+    Pc = _prep(P.float(), 16)
+    Ec = _prep(E.float(), 16)
+    h0c = _prep(h0.float(), 16) if h0 is not None else None
+    hin = torch.empty_like(Pc)
+    hT = torch.empty(bsz, dm, ds, 4, dtype=torch.float32, device=P.device)
+    with torch.cuda.device(P.device):
+        _lib.call("mqc_ssm_scan_carry", Pc.data_ptr(), Ec.data_ptr(), _lib.ptr(h0c),
+                  hin.data_ptr(), hT.data_ptr(), nseg, bsz, dm * ds, _lib.stream_ptr(P.device))
+    return hin, hT
+
+
 def ssm_scan_cayley(delta: torch.Tensor, Lambda: torch.Tensor, B: torch.Tensor,
                     C: torch.Tensor, S: torch.Tensor, D: torch.Tensor,
                     h0: torch.Tensor | None = None, eps: float = 1e-6,

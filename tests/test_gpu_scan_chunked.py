@@ -99,3 +99,58 @@ def test_config5_full_size_chunked_vs_sequential():
         # accumulated over 65536 steps as well (about 1.2e-5 measured)
         assert rel_l2(h[:, ci], h_ref) < min(RTOL_BF16, 5e-5)
         assert rel_l2(y[:, :, ci], y_ref) < RTOL_BF16
+
+
+# ------------------------------------------------------------ time-sharded scan
+
+def test_scan_summary_matches_oracle():
+    """(P, E) of a range: P the left-ordered product of the Cayley steps, E the
+    final state from zero, with and without time chunks inside the range."""
+    from mambaqc_b200.kernels import ssm_scan_summary
+    inp = make_scan_inputs(2, 512, 5, 16, shared=True, s_real=True, seed=31)
+    q = ref.cayley(inp["delta"][..., None, None] * inp["Lambda"][None, None])
+    P_ref = torch.zeros(2, 5, 16, 4, dtype=torch.float64)
+    P_ref[..., 0] = 1
+    for t in range(512):
+        P_ref = ref.qmul(q[:, t], P_ref)
+    E_ref = ref.ssm_scan_cayley(*(inp[k] for k in ("delta", "Lambda", "B", "C", "S", "D")))[1]
+    d = to_dev(inp, torch.float32)
+    for nc in (1, 4, "auto"):
+        P, E = ssm_scan_summary(d["delta"], d["Lambda"], d["B"], d["C"], d["S"], d["D"],
+                                time_chunks=nc)
+        assert rel_l2(P, P_ref) < RTOL_F32, nc
+        assert rel_l2(E, E_ref) < RTOL_F32, nc
+
+
+@pytest.mark.parametrize("shared,s_real,dtype", [(True, True, torch.float32),
+                                                 (True, True, torch.bfloat16),
+                                                 (False, True, torch.float32),
+                                                 (True, False, torch.float32)])
+def test_time_sharded_scan_emulated_on_one_gpu(shared, s_real, dtype):
+    """The time-sharded decomposition with 4 ranks emulated in turn on one GPU:
+    per-range summaries, the carry over ranks, and each range scanned from its
+    start state reproduce the unsharded scan (y and the final state)."""
+    from mambaqc_b200.kernels import ssm_scan_carry, ssm_scan_summary
+    from mambaqc_b200.kernels.sharded import time_shard
+    world = 4
+    inp = make_scan_inputs(2, 2048, 24, 16, shared=shared, s_real=s_real, seed=41)
+    d = to_dev(inp, dtype)
+    h0 = torch.randn(2, 24, 16, 4, generator=gen(42)).to(DEV)
+    keys = ("delta", "Lambda", "B", "C", "S", "D")
+    with torch.no_grad():
+        y_full, h_full = ssm_scan_cayley(*(d[k] for k in keys), h0=h0, return_final_state=True,
+                                         time_chunks=1)
+        parts = []
+        for r in range(world):
+            parts.append({k: (d[k] if k in ("Lambda", "D") else time_shard(d[k], r, world))
+                          for k in keys})
+        sums = [ssm_scan_summary(*(p[k] for k in keys)) for p in parts]
+        hin, hT = ssm_scan_carry(torch.stack([s[0] for s in sums]),
+                                 torch.stack([s[1] for s in sums]), h0)
+        ys = [ssm_scan_cayley(*(p[k] for k in keys), h0=hin[r], time_chunks=1)
+              for r, p in enumerate(parts)]
+    torch.cuda.synchronize()
+    y = torch.cat(ys, dim=1)
+    assert rel_l2(hT, h_full) < RTOL_F32
+    tol = RTOL_F32 if dtype == torch.float32 else RTOL_BF16
+    assert rel_l2(y.float(), y_full.float()) < tol

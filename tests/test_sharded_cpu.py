@@ -74,3 +74,68 @@ def test_channel_sharded_scan_matches_unsharded(world):
 def test_channel_shard_rejects_uneven_split():
     with pytest.raises(ValueError):
         channel_shard(torch.zeros(1, 2, 5), 0, 2, 2)
+
+
+# ------------------------------------------------------------ time-sharded scan
+
+def _oracle_summary(d, L, Bm, Cm, s, Dk):
+    """(P, E) of a time range from the oracle: P the left-ordered product of the
+    Cayley steps, E the final state from zero."""
+    bsz, seqlen, dm = d.shape
+    q = ref.cayley(d[..., None, None] * L[None, None])          # [B,T,D,N,4]
+    P = torch.zeros(bsz, dm, L.shape[1], 4, dtype=d.dtype)
+    P[..., 0] = 1
+    for t in range(seqlen):
+        P = ref.qmul(q[:, t], P)
+    E = ref.ssm_scan_cayley(d, L, Bm, Cm, s, Dk)[1]
+    return P, E
+
+
+def _oracle_carry(P_all, E_all, h0):
+    H = torch.zeros_like(P_all[0]) if h0 is None else h0
+    hin = []
+    for s in range(P_all.shape[0]):
+        hin.append(H)
+        H = ref.qmul(P_all[s], H) + E_all[s]
+    return torch.stack(hin), H
+
+
+def _time_worker(rank, world, port, q):
+    from mambaqc_b200.kernels.sharded import ssm_scan_cayley_time_sharded, time_shard
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        delta, lam, Bm, Cm, x, Dk = _inputs()
+        h0 = torch.randn(1, 6, 4, 4, generator=torch.Generator().manual_seed(8)).double()
+        shard = (time_shard(delta, rank, world), lam, time_shard(Bm, rank, world),
+                 time_shard(Cm, rank, world), time_shard(x, rank, world), Dk)
+        y, hT = ssm_scan_cayley_time_sharded(*shard, h0=h0, summary_fn=_oracle_summary,
+                                             carry_fn=_oracle_carry, scan_fn=_oracle_scan)
+        q.put((rank, (y, hT)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_time_sharded_scan_matches_unsharded(world):
+    """Each rank summarises its time range, the summaries are all-gathered and
+    folded into each rank's start state; the ranks' outputs, concatenated in
+    time, and the final state equal the unsharded scan."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_time_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    inp = _inputs()
+    h0 = torch.randn(1, 6, 4, 4, generator=torch.Generator().manual_seed(8)).double()
+    y_full, h_full = ref.ssm_scan_cayley(*inp, h0=h0)
+    y = torch.cat([results[r][0] for r in range(world)], dim=1)
+    assert torch.allclose(y, y_full, rtol=1e-10, atol=1e-12)
+    for r in range(world):
+        assert torch.allclose(results[r][1], h_full, rtol=1e-10, atol=1e-12)
