@@ -223,6 +223,15 @@ MQC_API int mqc_ssm_scan_fwd_summary(const mqc_ssm_scan_args* args, int64_t nchu
                                      float* E, void* workspace, size_t workspace_bytes,
                                      void* stream);
 
+/* The scan of a range whose chunk summaries are already in `workspace`: a
+ * mqc_ssm_scan_fwd_summary call with the same inputs and nchunks filled it.
+ * Runs only the carry from args->h0 and the full pass, so a time-sharded rank
+ * scans its range with one state-only pass in total, not two. Same arguments
+ * and results as mqc_ssm_scan_fwd_chunked. No counterpart in the reference. */
+MQC_API int mqc_ssm_scan_fwd_chunked_resume(const mqc_ssm_scan_args* args, int64_t nchunks,
+                                            void* workspace, size_t workspace_bytes,
+                                            void* stream);
+
 /* Start states of consecutive time segments from their summaries
  * (mqc_ssm_scan_fwd_summary):
  *   H_0 = h0 (zero if NULL);  H_{s+1} = P_s (x) H_s + E_s;

@@ -113,6 +113,8 @@ _SIGNATURES.update({
                                  _c_void_p, ctypes.c_size_t, _c_void_p],
     "mqc_ssm_scan_carry": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64,
                            _i64, _c_void_p],
+    "mqc_ssm_scan_fwd_chunked_resume": [ctypes.POINTER(SsmScanArgs), _i64, _c_void_p,
+                                        ctypes.c_size_t, _c_void_p],
 })
 _SIZE_FUNCS = {"mqc_qln_bwd_workspace_size": [_i64, _i64],
                "mqc_ssm_scan_fwd_chunked_workspace_size": [_i64, _i64, _i64, _i64],

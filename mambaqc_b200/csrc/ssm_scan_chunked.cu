@@ -91,6 +91,30 @@ size_t chunked_workspace(int64_t batch, int64_t nchunks, int64_t lanes) {
 using namespace mqc;
 using namespace mqc::scan;
 
+namespace {
+
+// Carry (start state of every chunk from the chunk summaries P, hloc and h0, and
+// the final state) followed by pass 2: the regular scan of every chunk from its
+// start state, chunks folded into the batch.
+int carry_and_rescan(const mqc_ssm_scan_args* a, const FwdParams& p, int64_t nchunks,
+                     const float* Pbuf, const float* hloc, float* hin, void* stream) {
+  const int64_t lanes = int64_t(p.D) * p.N;
+  cudaStream_t st = as_stream(stream);
+  dim3 grid{unsigned((lanes + kCarryThreads - 1) / kCarryThreads), unsigned(p.B), 1u};
+  chunk_carry_kernel<<<grid, kCarryThreads, 0, st>>>(Pbuf, hloc, p.h0, hin, p.hT, int(nchunks),
+                                                     lanes);
+  int rc = check_launch("mqc_ssm_scan_fwd_chunked(carry)");
+  if (rc != MQC_OK) return rc;
+  mqc_ssm_scan_args a2 = *a;
+  a2.batch = int64_t(p.B) * nchunks;
+  a2.seq_len = p.T / nchunks;
+  a2.h0 = hin;
+  a2.hT = nullptr;
+  return mqc_ssm_scan_fwd(&a2, stream);
+}
+
+}  // namespace
+
 extern "C" size_t mqc_ssm_scan_fwd_chunked_workspace_size(int64_t batch, int64_t channels,
                                                           int64_t d_state, int64_t nchunks) {
   if (batch <= 0 || channels <= 0 || d_state <= 0 || nchunks <= 0) return 0;
@@ -146,26 +170,15 @@ extern "C" int mqc_ssm_scan_fwd_chunked(const mqc_ssm_scan_args* a, int64_t nchu
               : dispatch_state_only(p1, a->dtype, s_real, shared, st);
   if (rc != MQC_OK) return rc;
 
-  // carry: start state of every chunk, and the final state
-  dim3 grid{unsigned((lanes + kCarryThreads - 1) / kCarryThreads), unsigned(p.B), 1u};
-  chunk_carry_kernel<<<grid, kCarryThreads, 0, st>>>(Pbuf, hloc, p.h0, hin, p.hT, int(nchunks),
-                                                     lanes);
-  rc = check_launch("mqc_ssm_scan_fwd_chunked(carry)");
-  if (rc != MQC_OK) return rc;
-
-  // pass 2: the regular scan of every chunk from its start state
-  mqc_ssm_scan_args a2 = *a;
-  a2.batch = int64_t(p.B) * nchunks;
-  a2.seq_len = p.T / nchunks;
-  a2.h0 = hin;
-  a2.hT = nullptr;
-  return mqc_ssm_scan_fwd(&a2, stream);
+  return carry_and_rescan(a, p, nchunks, Pbuf, hloc, hin, stream);
 }
 
 extern "C" size_t mqc_ssm_scan_fwd_summary_workspace_size(int64_t batch, int64_t channels,
                                                           int64_t d_state, int64_t nchunks) {
+  // the chunk summaries plus room for the chunk start states, so that the same
+  // workspace can be handed to mqc_ssm_scan_fwd_chunked_resume
   if (batch <= 0 || channels <= 0 || d_state <= 0 || nchunks <= 1) return 0;
-  return size_t(2) * size_t(batch) * size_t(nchunks) * size_t(channels * d_state) * 16;
+  return chunked_workspace(batch, nchunks, channels * d_state);
 }
 
 extern "C" int mqc_ssm_scan_fwd_summary(const mqc_ssm_scan_args* a, int64_t nchunks, float* P,
@@ -251,4 +264,35 @@ extern "C" int mqc_ssm_scan_carry(const float* P, const float* E, const float* h
   segment_carry_kernel<<<grid, kCarryThreads, 0, as_stream(stream)>>>(
       P, E, h0, hin, hT, int(segments), int(batch), lanes);
   return check_launch(name);
+}
+
+extern "C" int mqc_ssm_scan_fwd_chunked_resume(const mqc_ssm_scan_args* a, int64_t nchunks,
+                                               void* workspace, size_t workspace_bytes,
+                                               void* stream) {
+  clear_error();
+  const char* name = "mqc_ssm_scan_fwd_chunked_resume";
+  MQC_REQUIRE(a != nullptr, MQC_ERR_INVALID_VALUE, "%s: null args", name);
+  MQC_REQUIRE(!(a->flags & MQC_SSM_Q_GIVEN), MQC_ERR_UNSUPPORTED,
+              "%s: explicit q is not supported (use the fused form)", name);
+  MQC_REQUIRE(a->ckpt == nullptr, MQC_ERR_UNSUPPORTED, "%s: no checkpoints (forward only)", name);
+  MQC_REQUIRE(nchunks >= 1, MQC_ERR_INVALID_VALUE, "%s: nchunks must be >= 1", name);
+  FwdParams p{};
+  int rc = validate_and_fill(a, &p, name);
+  if (rc != MQC_OK || p.T == 0 || p.B == 0 || p.D == 0) return rc;
+  if (nchunks == 1) return mqc_ssm_scan_fwd(a, stream);
+  MQC_REQUIRE(p.T % nchunks == 0, MQC_ERR_INVALID_VALUE, "%s: seq_len %d not divisible by %lld",
+              name, p.T, (long long)nchunks);
+  MQC_REQUIRE(a->dskip_sb == 0 && a->dskip_st == 0, MQC_ERR_UNSUPPORTED,
+              "%s: the skip weight must be per channel ([D], strides 0 over batch and time)", name);
+  MQC_REQUIRE(int64_t(p.B) * nchunks <= 65535, MQC_ERR_UNSUPPORTED,
+              "%s: batch * nchunks must be <= 65535", name);
+  const int64_t lanes = int64_t(p.D) * p.N;
+  const size_t need = chunked_workspace(p.B, nchunks, lanes);
+  MQC_REQUIRE(workspace != nullptr && workspace_bytes >= need && aligned(workspace, 16),
+              MQC_ERR_INVALID_VALUE, "%s: 16-byte aligned workspace of %zu bytes required", name,
+              need);
+  const float* Pbuf = static_cast<const float*>(workspace);
+  const float* hloc = Pbuf + size_t(p.B) * nchunks * lanes * 4;
+  float* hin = static_cast<float*>(workspace) + size_t(2) * p.B * nchunks * lanes * 4;
+  return carry_and_rescan(a, p, nchunks, Pbuf, hloc, hin, stream);
 }

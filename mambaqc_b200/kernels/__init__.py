@@ -17,7 +17,7 @@ from .parallel_scan import parallel_scan_quaternion
 from .quaternion_norm import quaternion_layer_norm_fused
 from .ssm_fused import (ssm_step_fused, ssm_forward_fused, ssm_scan_cayley,
                         ssm_scan_cayley_from_host, ssm_step_cayley, ssm_scan_summary,
-                        ssm_scan_carry)
+                        ssm_scan_carry, ssm_scan_cayley_resume)
 from .block_fused import causal_conv1d_silu, gate_residual, ssm_scan_inputs
 
 # Importing the submodule ``quaternion_norm`` (the LayerNorm file) rebinds the
@@ -41,6 +41,7 @@ __all__ = [
     "ssm_step_cayley",
     "ssm_scan_summary",
     "ssm_scan_carry",
+    "ssm_scan_cayley_resume",
     "causal_conv1d_silu",
     "ssm_scan_inputs",
     "gate_residual",

@@ -151,7 +151,19 @@ def ssm_scan_cayley_time_sharded(delta: torch.Tensor, Lambda: torch.Tensor, B: t
     summary, carry and scan (defaults: ``ssm_scan_summary``,
     ``ssm_scan_carry`` and ``ssm_scan_cayley`` with ``time_chunks``).
     """
-    from .ssm_fused import ssm_scan_carry, ssm_scan_cayley, ssm_scan_summary
+    from .ssm_fused import ssm_scan_carry, ssm_scan_cayley, ssm_scan_cayley_resume, ssm_scan_summary
+
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    if summary_fn is None and scan_fn is None and world > 1:
+        # GPU default: the range is summarised once, in time chunks, and its scan
+        # resumes from those chunk summaries (one state-only pass in total)
+        rank = dist.get_rank(group)
+        summ = ssm_scan_summary(delta, Lambda, B, C, S, D, time_chunks=time_chunks,
+                                keep_chunks=True)
+        P_all, E_all = _gather_summaries(summ.P, summ.E, world, group)
+        hin, hT = (carry_fn or ssm_scan_carry)(P_all, E_all, h0)
+        y = ssm_scan_cayley_resume(delta, Lambda, B, C, S, D, summ, h0=hin[rank])
+        return y, hT
 
     if summary_fn is None:
         def summary_fn(d, L, Bm, Cm, s, Dk):
@@ -163,17 +175,22 @@ def ssm_scan_cayley_time_sharded(delta: torch.Tensor, Lambda: torch.Tensor, B: t
             return ssm_scan_cayley(d, L, Bm, Cm, s, Dk, h0=hs, return_final_state=True,
                                    time_chunks=time_chunks)
 
-    world = dist.get_world_size(group) if dist.is_initialized() else 1
     if world == 1:
         return scan_fn(delta, Lambda, B, C, S, D, h0)
     rank = dist.get_rank(group)
     P, E = summary_fn(delta, Lambda, B, C, S, D)
+    P_all, E_all = _gather_summaries(P, E, world, group)
+    hin, hT = carry_fn(P_all, E_all, h0)
+    y, _ = scan_fn(delta, Lambda, B, C, S, D, hin[rank])
+    return y, hT
+
+
+def _gather_summaries(P: torch.Tensor, E: torch.Tensor, world: int, group):
+    """All-gather of every rank's range summary: ([world, ...], [world, ...])."""
     P_all = torch.empty((world,) + tuple(P.shape), dtype=P.dtype, device=P.device)
     E_all = torch.empty_like(P_all)
     dist.all_gather_into_tensor(P_all.view(world * P.shape[0], *P.shape[1:]), P.contiguous(),
                                 group=group)
     dist.all_gather_into_tensor(E_all.view(world * E.shape[0], *E.shape[1:]), E.contiguous(),
                                 group=group)
-    hin, hT = carry_fn(P_all, E_all, h0)
-    y, _ = scan_fn(delta, Lambda, B, C, S, D, hin[rank])
-    return y, hT
+    return P_all, E_all

@@ -250,9 +250,19 @@ def _run_scan_chunked(delta, Lam, B, C, S, D, h0, eps, nchunks, return_final_sta
     return y, hT
 
 
+class RangeSummary:
+    """Result of ``ssm_scan_summary(..., keep_chunks=True)``: the range's P and E
+    plus the per-chunk summaries (kept in ``workspace``) that
+    ``ssm_scan_cayley_resume`` reuses instead of repeating the state-only pass."""
+
+    def __init__(self, P, E, workspace, ws_bytes, nchunks):
+        self.P, self.E = P, E
+        self.workspace, self.ws_bytes, self.nchunks = workspace, ws_bytes, nchunks
+
+
 def ssm_scan_summary(delta: torch.Tensor, Lambda: torch.Tensor, B: torch.Tensor,
                      C: torch.Tensor, S: torch.Tensor, D: torch.Tensor, eps: float = 1e-6,
-                     time_chunks: int | str = "auto"):
+                     time_chunks: int | str = "auto", keep_chunks: bool = False):
     """The affine map of a time range of the scan (no autograd).
 
     Over the steps of the inputs (shapes as in ``ssm_scan_cayley``) the state
@@ -262,7 +272,8 @@ def ssm_scan_summary(delta: torch.Tensor, Lambda: torch.Tensor, B: torch.Tensor,
 
     A time-sharded scan exchanges these summaries between ranks
     (``mqc_ssm_scan_fwd_summary``). ``time_chunks`` splits the range
-    time-parallel, as in ``ssm_scan_cayley``.
+    time-parallel, as in ``ssm_scan_cayley``. With ``keep_chunks`` a
+    ``RangeSummary`` is returned instead, for ``ssm_scan_cayley_resume``.
     """
     dt = delta.dtype
     bsz, seqlen, dm = delta.shape
@@ -298,7 +309,47 @@ def ssm_scan_summary(delta: torch.Tensor, Lambda: torch.Tensor, B: torch.Tensor,
                   E.data_ptr(), ws.data_ptr(), ws_bytes, _lib.stream_ptr(delta.device))
     if _lib.sync_checks_enabled():
         _lib.check_device_status(delta.device)
+    if keep_chunks:
+        return RangeSummary(P, E, ws, ws_bytes, nc)
     return P, E
+
+
+def ssm_scan_cayley_resume(delta: torch.Tensor, Lambda: torch.Tensor, B: torch.Tensor,
+                           C: torch.Tensor, S: torch.Tensor, D: torch.Tensor,
+                           summary: RangeSummary, h0: torch.Tensor | None = None,
+                           eps: float = 1e-6, return_final_state: bool = False):
+    """``ssm_scan_cayley`` (no autograd) of the same inputs that ``summary`` was
+    made from, starting from h0: only the carry and the full pass run
+    (``mqc_ssm_scan_fwd_chunked_resume``), reusing the summary's chunks."""
+    dt = delta.dtype
+    bsz, seqlen, dm = delta.shape
+    ds = Lambda.shape[1]
+    shared = B.dim() == 4
+    va = _vec_align(dt)
+    dc = _prep(delta, 4)
+    Lc = _prep(Lambda.float(), 16)
+    Bc = _prep(B, 16 if shared else va)
+    Cc = _prep(C, 16 if shared else va)
+    Sc = _prep(S, va)
+    Df, dsb, dst, dsd = _skip_operand(D, bsz, seqlen, dm)
+    h0c = _prep(h0.float(), 16) if h0 is not None else None
+    y = torch.empty(bsz, seqlen, dm, 4, dtype=dt, device=delta.device)
+    hT = (torch.empty(bsz, dm, ds, 4, dtype=torch.float32, device=delta.device)
+          if return_final_state else None)
+    flags = (_lib.MQC_SSM_BC_SHARED if shared else 0) | (_lib.MQC_SSM_S_REAL if S.dim() == 3 else 0)
+    status = _lib.status_word(delta.device)
+    a = _lib.SsmScanArgs(
+        batch=bsz, seq_len=seqlen, channels=dm, d_state=ds, dtype=_lib.dtype_code(dc),
+        flags=flags, eps=float(eps), reserved0=0, delta=dc.data_ptr(), lambda_=Lc.data_ptr(),
+        q=None, Bm=Bc.data_ptr(), Cm=Cc.data_ptr(), s=Sc.data_ptr(), dskip=Df.data_ptr(),
+        dskip_sb=dsb, dskip_st=dst, dskip_sd=dsd, h0=_lib.ptr(h0c), y=y.data_ptr(),
+        hT=_lib.ptr(hT), status=status.data_ptr(), wait_poll_limit=-1, ckpt=None, ckpt_every=0)
+    with torch.cuda.device(delta.device):
+        _lib.call("mqc_ssm_scan_fwd_chunked_resume", ctypes.byref(a), int(summary.nchunks),
+                  summary.workspace.data_ptr(), summary.ws_bytes, _lib.stream_ptr(delta.device))
+    if _lib.sync_checks_enabled():
+        _lib.check_device_status(delta.device)
+    return (y, hT) if return_final_state else y
 
 
 def ssm_scan_carry(P: torch.Tensor, E: torch.Tensor, h0: torch.Tensor | None = None):

@@ -154,3 +154,37 @@ def test_time_sharded_scan_emulated_on_one_gpu(shared, s_real, dtype):
     assert rel_l2(hT, h_full) < RTOL_F32
     tol = RTOL_F32 if dtype == torch.float32 else RTOL_BF16
     assert rel_l2(y.float(), y_full.float()) < tol
+
+
+@pytest.mark.parametrize("nc", [1, 4, 8])
+def test_resume_from_summary_equals_chunked_scan(nc):
+    """A range scanned by resuming from its summary's chunks (carry + full pass)
+    is bit-identical to the time-chunked scan with the same chunks, and the
+    emulated 4-rank time-sharded scan built on it matches the unsharded scan."""
+    from mambaqc_b200.kernels import ssm_scan_carry, ssm_scan_cayley_resume, ssm_scan_summary
+    from mambaqc_b200.kernels.sharded import time_shard
+    keys = ("delta", "Lambda", "B", "C", "S", "D")
+    inp = make_scan_inputs(1, 4096, 12, 64, shared=True, s_real=True, seed=51)
+    d = to_dev(inp, torch.bfloat16)
+    h0 = torch.randn(1, 12, 64, 4, generator=gen(52)).to(DEV)
+    with torch.no_grad():
+        y_c, h_c = ssm_scan_cayley(*(d[k] for k in keys), h0=h0, return_final_state=True,
+                                   time_chunks=nc)
+        summ = ssm_scan_summary(*(d[k] for k in keys), time_chunks=nc, keep_chunks=True)
+        y_r, h_r = ssm_scan_cayley_resume(*(d[k] for k in keys), summary=summ, h0=h0,
+                                          return_final_state=True)
+        world = 4
+        parts = [{k: (d[k] if k in ("Lambda", "D") else time_shard(d[k], r, world)) for k in keys}
+                 for r in range(world)]
+        summs = [ssm_scan_summary(*(p[k] for k in keys), time_chunks=nc, keep_chunks=True)
+                 for p in parts]
+        hin, hT = ssm_scan_carry(torch.stack([s.P for s in summs]),
+                                 torch.stack([s.E for s in summs]), h0)
+        ys = [ssm_scan_cayley_resume(*(p[k] for k in keys), summary=s, h0=hin[r])
+              for r, (p, s) in enumerate(zip(parts, summs))]
+    torch.cuda.synchronize()
+    assert torch.equal(y_r, y_c) and torch.equal(h_r, h_c)
+    y_full, h_full = ssm_scan_cayley(*(d[k] for k in keys), h0=h0, return_final_state=True,
+                                     time_chunks=1)
+    assert rel_l2(hT, h_full) < RTOL_F32
+    assert rel_l2(torch.cat(ys, dim=1).float(), y_full.float()) < RTOL_BF16
