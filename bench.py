@@ -21,6 +21,7 @@ workload per step.
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import math
 import os
@@ -88,7 +89,6 @@ def dist_setup(args):
         backend = "nccl" if (args.impl == "b200" and torch.cuda.is_available()) else "gloo"
         if backend == "nccl":
             torch.cuda.set_device(local)
-        import datetime
         kw = {"device_id": torch.device(f"cuda:{local}")} if backend == "nccl" else {}
         dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300), **kw)
     return world, rank, local
@@ -126,7 +126,8 @@ class ClockSampler:
 
     FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap,"
+              "timestamp")
 
     def __init__(self, dev):
         self.proc = None
@@ -142,13 +143,24 @@ class ClockSampler:
             os.close(fd)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", "20"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            # let the sampler start up before the timed region begins
+            t_end = time.time() + 3.0
+            while time.time() < t_end and Path(self.path).stat().st_size == 0:
+                time.sleep(0.02)
         except Exception:
             self.proc = None
+        self.window = [time.time(), None]
+
+    def mark_end(self):
+        """End of the timed region (samples after it are not counted)."""
+        self.window[1] = time.time()
 
     def stop(self):
         if self.proc is None:
             return None
+        if self.window[1] is None:
+            self.mark_end()
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -165,6 +177,18 @@ class ClockSampler:
         os.unlink(self.path)
         if not rows:
             return None
+        # keep the samples taken between the start of the warm-up and the end of
+        # the timed region (all of them if the timestamps cannot be read)
+        inside = []
+        for r in rows:
+            try:
+                ts = datetime.datetime.strptime(r[10], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+            except (IndexError, ValueError):
+                inside = rows
+                break
+            if self.window[0] - 0.05 <= ts <= self.window[1] + 0.05:
+                inside.append(r)
+        rows = inside or rows
 
         def num(s):
             try:
@@ -351,6 +375,7 @@ def run_b200(args, world, rank, local):
     clocks = ClockSampler(dev)
     clocks.start()
     ms_total = timed(step, args.steps, args.warmup, world, stream)
+    clocks.mark_end()
     clk = clocks.stop()
     _lib.check_device_status(dev)
     ms_step_local = ms_total / args.steps
