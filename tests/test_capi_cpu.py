@@ -190,3 +190,67 @@ def test_reference_preconditions_raise_assertion():
     with pytest.raises(AssertionError):
         ssm_step_fused(torch.zeros(1, 2, 3, 4), torch.zeros(1, 2, 3, 4), torch.zeros(1, 2, 3),
                        torch.zeros(1, 2, 3, 4), torch.zeros(1, 2), torch.zeros(1, 2, 3, 4))
+
+
+@no_gpu
+def test_block_glue_argument_validation_without_gpu():
+    """The block glue entry points reject bad arguments before any CUDA call."""
+    lib = _lib.load()
+    fake = 0x10000
+    # conv: kernel size outside 1..8, row stride below the channel count, bad dtype
+    assert lib.mqc_conv_silu_fwd(fake, 16, fake, None, fake, 2, 8, 16, 9, 0, None) == UNSUPPORTED
+    assert lib.mqc_conv_silu_fwd(fake, 8, fake, None, fake, 2, 8, 16, 4, 0, None) == INVALID
+    assert b"row stride" in lib.mqc_last_error()
+    assert lib.mqc_conv_silu_fwd(fake, 16, fake, None, fake, 2, 8, 16, 4, 5, None) == INVALID
+    assert lib.mqc_conv_silu_fwd(fake, 16, fake, None, fake, 0, 8, 16, 4, 0, None) == 0
+    need = lib.mqc_conv_silu_bwd_workspace_size(2, 64, 16, 4)
+    assert need > 0 and lib.mqc_conv_silu_bwd_workspace_size(2, 64, 16, 9) == 0
+    assert lib.mqc_conv_silu_bwd(fake, 16, fake, None, fake, fake, fake, None, 2, 64, 16, 4, 0,
+                                 fake, need - 1, None) == INVALID
+    assert b"workspace" in lib.mqc_last_error()
+    # elementwise glue: null pointers, strides below the width
+    assert lib.mqc_scan_inputs_fwd(fake, 16, None, 16, fake, fake, fake, 4, 16, 0, None) == INVALID
+    assert lib.mqc_scan_inputs_fwd(fake, 8, fake, 16, fake, fake, fake, 4, 16, 0, None) == INVALID
+    assert lib.mqc_gate_residual_fwd(fake, fake, 8, fake, fake, 4, 16, 0, None) == INVALID
+    assert lib.mqc_gate_residual_bwd(fake, 16, fake, fake, fake, fake, 4, 16, 3, None) == INVALID
+    assert lib.mqc_scan_inputs_bwd(fake, 16, fake, 16, fake, None, None, fake, fake, fake, 0, 16,
+                                   0, None) == 0
+
+
+@no_gpu
+def test_time_shard_entry_points_validation_without_gpu():
+    """Range summary, carry and resume reject bad arguments before any CUDA call."""
+    lib = _lib.load()
+    fake = 0x10000
+    base = dict(batch=1, seq_len=64, channels=4, d_state=16, dtype=0,
+                flags=_lib.MQC_SSM_BC_SHARED | _lib.MQC_SSM_S_REAL, eps=1e-6, reserved0=0,
+                delta=fake, lambda_=fake, q=None, Bm=fake, Cm=fake, s=fake, dskip=fake,
+                dskip_sb=0, dskip_st=0, dskip_sd=1, h0=None, y=None, hT=None, status=None,
+                wait_poll_limit=-1)
+
+    def summary(nchunks=1, P=fake, E=fake, **kw):
+        a = _lib.SsmScanArgs(**{**base, **kw})
+        return lib.mqc_ssm_scan_fwd_summary(ctypes.byref(a), nchunks, P, E, None, 0, None)
+
+    assert summary(h0=fake) == INVALID  # the summary is the map from the zero state
+    assert b"zero state" in lib.mqc_last_error()
+    assert summary(hT=fake) == INVALID
+    assert summary(flags=_lib.MQC_SSM_Q_GIVEN) == UNSUPPORTED
+    assert summary(nchunks=0) == INVALID
+    assert summary(P=fake + 4) == INVALID
+    assert summary(nchunks=3) == INVALID  # 64 steps do not split into 3 chunks
+    assert summary(nchunks=4) == INVALID  # chunks need a workspace
+    assert b"workspace" in lib.mqc_last_error()
+    assert lib.mqc_ssm_scan_fwd_summary_workspace_size(1, 4, 16, 4) == \
+        lib.mqc_ssm_scan_fwd_chunked_workspace_size(1, 4, 16, 4)
+    assert lib.mqc_ssm_scan_fwd_summary_workspace_size(1, 4, 16, 1) == 0
+    # carry
+    assert lib.mqc_ssm_scan_carry(fake, fake, None, fake, fake, -1, 1, 64, None) == INVALID
+    assert lib.mqc_ssm_scan_carry(None, fake, None, fake, fake, 2, 1, 64, None) == INVALID
+    assert lib.mqc_ssm_scan_carry(fake + 8, fake, None, fake, fake, 2, 1, 64, None) == MISALIGNED
+    assert lib.mqc_ssm_scan_carry(fake, fake, None, fake, fake, 2, 0, 64, None) == 0
+    # resume needs the summary's workspace
+    a = _lib.SsmScanArgs(**{**base, "y": fake})
+    assert lib.mqc_ssm_scan_fwd_chunked_resume(ctypes.byref(a), 4, None, 0, None) == INVALID
+    assert b"workspace" in lib.mqc_last_error()
+    assert lib.mqc_ssm_scan_fwd_chunked_resume(ctypes.byref(a), 3, None, 0, None) == INVALID
