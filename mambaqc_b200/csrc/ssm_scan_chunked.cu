@@ -154,9 +154,12 @@ extern "C" int mqc_ssm_scan_fwd_chunked(const mqc_ssm_scan_args* a, int64_t nchu
   const bool s_real = a->flags & MQC_SSM_S_REAL;
   const bool shared = a->flags & MQC_SSM_BC_SHARED;
 
-  // pass 1: state-only scan of each chunk from zero, chunks folded into the batch
+  // pass 1: state-only scan of each chunk from zero, chunks folded into the batch.
+  // With one batch row the last chunk's summary is never read (the final state
+  // comes out of pass 2), so pass 1 stops one chunk short.
+  const bool skip_last = p.B == 1;
   FwdParams p1 = p;
-  p1.B = int(int64_t(p.B) * nchunks);
+  p1.B = skip_last ? int(nchunks - 1) : int(int64_t(p.B) * nchunks);
   p1.T = int(p.T / nchunks);
   p1.h0 = nullptr;
   p1.hT = hloc;
@@ -169,8 +172,29 @@ extern "C" int mqc_ssm_scan_fwd_chunked(const mqc_ssm_scan_args* a, int64_t nchu
   rc = packed ? dispatch_state_only_packed(p1, a->dtype, s_real, st)
               : dispatch_state_only(p1, a->dtype, s_real, shared, st);
   if (rc != MQC_OK) return rc;
+  if (!skip_last) return carry_and_rescan(a, p, nchunks, Pbuf, hloc, hin, stream);
 
-  return carry_and_rescan(a, p, nchunks, Pbuf, hloc, hin, stream);
+  // one batch row: carry over the first nc-1 summaries gives every chunk's start
+  // state (the last one written as the carry's final state); pass 2 then writes
+  // each chunk's final state into hloc (free by then) and the last one is hT
+  dim3 grid{unsigned((lanes + kCarryThreads - 1) / kCarryThreads), 1u, 1u};
+  chunk_carry_kernel<<<grid, kCarryThreads, 0, st>>>(Pbuf, hloc, p.h0, hin,
+                                                     hin + size_t(nchunks - 1) * lanes * 4,
+                                                     int(nchunks - 1), lanes);
+  rc = check_launch("mqc_ssm_scan_fwd_chunked(carry)");
+  if (rc != MQC_OK) return rc;
+  mqc_ssm_scan_args a2 = *a;
+  a2.batch = nchunks;
+  a2.seq_len = p.T / nchunks;
+  a2.h0 = hin;
+  a2.hT = p.hT != nullptr ? hloc : nullptr;
+  rc = mqc_ssm_scan_fwd(&a2, stream);
+  if (rc != MQC_OK || p.hT == nullptr) return rc;
+  const cudaError_t e = cudaMemcpyAsync(p.hT, hloc + size_t(nchunks - 1) * lanes * 4,
+                                        size_t(lanes) * 16, cudaMemcpyDeviceToDevice, st);
+  return e == cudaSuccess ? MQC_OK
+                          : fail(MQC_ERR_CUDA, "%s: final state copy: %s", name,
+                                 cudaGetErrorString(e));
 }
 
 extern "C" size_t mqc_ssm_scan_fwd_summary_workspace_size(int64_t batch, int64_t channels,
