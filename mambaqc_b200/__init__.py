@@ -36,15 +36,16 @@ _ALIASES = {
     "mambaqc.layers.causal_conv1d": "mambaqc_b200.layers.causal_conv1d",
     "mambaqc.models": "mambaqc_b200.models",
     "mambaqc.models.quaternion_mamba2_block": "mambaqc_b200.models.quaternion_mamba2_block",
+    "mambaqc.models.quaternion_mamba2": "mambaqc_b200.models.quaternion_mamba2",
 }
 
 
 def install_as_mambaqc() -> None:
     """Make ``import mambaqc.<module>`` resolve to this package's GPU modules.
 
-    Only the hot-path modules listed above are aliased; the rest of the
-    reference package (LM wrapper, Lite variant, trainer, utils) is not part of
-    this library.
+    Only the modules listed above are aliased (the hot path, the block and the
+    LM wrapper that the training harness uses); the rest of the reference
+    package (Lite variant, trainer, utils) is not part of this library.
     """
     for alias, target in _ALIASES.items():
         sys.modules[alias] = importlib.import_module(target)

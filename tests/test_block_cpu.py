@@ -54,3 +54,23 @@ def test_install_as_mambaqc_aliases_modules():
         for k in [k for k in sys.modules if k == "mambaqc" or k.startswith("mambaqc.")]:
             del sys.modules[k]
         sys.modules.update(saved)
+
+
+def test_lm_structure_and_init_follow_the_reference_layout():
+    """Parameter names, vocabulary padding and init of the LM wrapper
+    (models/quaternion_mamba2.py:29-95), built on the CPU without running it."""
+    import torch
+    from mambaqc_b200.models import QuaternionMamba2, QuaternionMamba2Block
+
+    torch.manual_seed(0)
+    lm = QuaternionMamba2(100, d_model=16, n_layers=2, d_state=4)
+    assert lm.vocab_size_padded == 104
+    keys = list(lm.state_dict())
+    assert keys[0] == "embedding.weight" and keys[-3:] == ["norm_f.weight", "norm_f.bias",
+                                                           "lm_head.weight"]
+    blk = set(QuaternionMamba2Block(16, d_state=4).state_dict())
+    for i in range(2):
+        assert {k[len(f"layers.{i}."):] for k in keys if k.startswith(f"layers.{i}.")} == blk
+    assert abs(lm.embedding.weight.std().item() - 0.02) < 0.005
+    assert abs(lm.layers[0].in_proj.weight.std().item() - 0.02) < 0.005
+    assert lm.get_num_params() == sum(p.numel() for p in lm.parameters()) - 2 * 104 * 16
