@@ -89,13 +89,41 @@ class QuaternionMamba2(nn.Module):
         return {"logits": logits, "loss": loss}
 
     @torch.no_grad()
+    def _next_logits_cached(self, input_ids: torch.Tensor, caches: list | None):
+        """Logits of the next token. With ``caches`` None the prompt is run
+        through every block's ``prefill`` and the caches are made; otherwise the
+        last token alone is stepped through the blocks (recurrent decoding)."""
+        if caches is None:
+            x = self.embedding(input_ids)
+            caches = []
+            for layer in self.layers:
+                x, c = layer.prefill(x)
+                caches.append(c)
+            x = x[:, -1]
+        else:
+            x = self.embedding(input_ids[:, -1])
+            for layer, c in zip(self.layers, caches):
+                x = layer.step(x, c)
+        return self.lm_head(self.norm_f(x))[..., : self.vocab_size], caches
+
+    @torch.no_grad()
     def generate(self, input_ids: torch.Tensor, max_new_tokens: int = 100,
                  temperature: float = 1.0, top_k: int | None = None,
-                 top_p: float | None = None) -> torch.Tensor:
-        """Sample max_new_tokens tokens after the prompt; returns [B, T + new]."""
+                 top_p: float | None = None, use_cache: bool = False) -> torch.Tensor:
+        """Sample max_new_tokens tokens after the prompt; returns [B, T + new].
+
+        ``use_cache`` (an addition; off by default, as the reference always
+        recomputes) keeps each block's conv inputs and SSM state and advances
+        them one token at a time, so each new token costs one step instead of a
+        pass over the whole sequence."""
         self.eval()
+        caches = None
         for _ in range(max_new_tokens):
-            nxt = self.forward(input_ids)["logits"][:, -1, :] / temperature
+            if use_cache:
+                logits, caches = self._next_logits_cached(input_ids, caches)
+                nxt = logits / temperature
+            else:
+                nxt = self.forward(input_ids)["logits"][:, -1, :] / temperature
             if top_k is not None:
                 kth = torch.topk(nxt, top_k, dim=-1).values[..., -1:]
                 nxt = nxt.masked_fill(nxt < kth, float("-inf"))

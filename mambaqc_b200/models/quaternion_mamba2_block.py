@@ -29,7 +29,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from mambaqc_b200.kernels.block_fused import causal_conv1d_silu, gate_residual, ssm_scan_inputs
-from mambaqc_b200.kernels.ssm_fused import ssm_scan_cayley
+from mambaqc_b200.kernels.ssm_fused import ssm_scan_cayley, ssm_step_cayley
 from mambaqc_b200.layers.causal_conv1d import CausalConv1d
 from mambaqc_b200.layers.quaternion_linear import (
     quaternion_to_real_projection,
@@ -93,6 +93,45 @@ class QuaternionMamba2Block(nn.Module):
         y, h_T = ssm_scan_cayley(delta.to(dt), self.ssm_lambda(), Bq, Cq.to(dt), s_real.to(dt),
                                  self.D, return_final_state=True)
         return (y, h_T) if return_state else y
+
+    @torch.no_grad()
+    def prefill(self, x: torch.Tensor):
+        """Forward over a prompt x [B, T, d_model] that also returns the cache a
+        recurrent continuation needs: {"conv": the last d_conv-1 conv inputs
+        [B, d_conv-1, d_inner] (zeros before the start), "h": the SSM state
+        [B, d_inner, d_state, 4] fp32}."""
+        out, h_T = self.forward(x, return_ssm_state=True)
+        k1 = self.d_conv - 1
+        x_inner = self.in_proj(x)[..., : self.d_inner]
+        hist = x_inner.new_zeros(x.shape[0], k1, self.d_inner)
+        take = min(k1, x.shape[1])
+        if take > 0:
+            hist[:, k1 - take:] = x_inner[:, -take:]
+        return out, {"conv": hist, "h": h_T.contiguous()}
+
+    @torch.no_grad()
+    def step(self, x_t: torch.Tensor, cache: dict) -> torch.Tensor:
+        """One token through the block, x_t [B, d_model] -> [B, d_model], from
+        and into ``cache`` (see ``prefill``): the conv runs over the cached
+        inputs plus this one, and the SSM advances its state in place
+        (``ssm_step_cayley``). Same result as running the whole sequence
+        through ``forward`` and taking the last position."""
+        bsz = x_t.shape[0]
+        xz = self.in_proj(x_t)
+        x_in, z = xz.chunk(2, dim=-1)
+        window = torch.cat([cache["conv"].to(x_in.dtype), x_in[:, None]], dim=1)
+        conv = self.conv1d.conv
+        x_act = causal_conv1d_silu(window, conv.weight, conv.bias)[:, -1].contiguous()
+        cache["conv"] = window[:, 1:].contiguous()
+        delta, s_real = ssm_scan_inputs(self.dt_proj(x_act), self.gate_proj(x_act), x_act)
+        Bq = self.B_proj(x_act).view(bsz, self.d_inner, self.d_state, 4)
+        Cq = self.C_proj(x_act).view(bsz, self.d_inner, self.d_state, 4)
+        dt = Bq.dtype
+        y = ssm_step_cayley(delta.to(dt).contiguous(), self.ssm_lambda(), Bq.contiguous(),
+                            Cq.to(dt).contiguous(), s_real.to(dt).contiguous(), self.D,
+                            cache["h"])
+        y_real = self.out_proj(self.norm(y[:, None]))[:, 0]
+        return gate_residual(x_t, z[..., : self.d_model], y_real)
 
     def extra_repr(self) -> str:
         return (f"d_model={self.d_model}, d_state={self.d_state}, d_inner={self.d_inner}, "

@@ -89,3 +89,28 @@ def test_generate_shapes_and_sampling_controls():
     out = lm.generate(prompt, max_new_tokens=4, temperature=0.8, top_k=10, top_p=0.9)
     assert out.shape == (2, 9) and torch.equal(out[:, :5], prompt)
     assert int(out.max()) < V and int(out.min()) >= 0
+
+
+def test_block_step_matches_forward_last_position():
+    """prefill over a prompt, then single-token steps, give the same outputs as
+    running the whole sequence through the block."""
+    from mambaqc_b200.models import QuaternionMamba2Block
+    torch.manual_seed(0)
+    blk = QuaternionMamba2Block(32, d_state=8).to(DEV)
+    x = torch.randn(2, 20, 32, generator=gen(7)).to(DEV)
+    with torch.no_grad():
+        full = blk(x)
+        out, cache = blk.prefill(x[:, :2])
+        assert rel_l2(out, full[:, :2]) < RTOL_F32
+        for t in range(2, 20):
+            y_t = blk.step(x[:, t], cache)
+            assert rel_l2(y_t, full[:, t]) < RTOL_F32, t
+
+
+def test_cached_greedy_generation_matches_full_recompute():
+    torch.manual_seed(0)
+    lm = QuaternionMamba2(V, d_model=DM, n_layers=NL, d_state=NS).to(DEV)
+    prompt = torch.randint(0, V, (2, 6), generator=gen(8)).to(DEV)
+    a = lm.generate(prompt, max_new_tokens=12, top_k=1)
+    b = lm.generate(prompt, max_new_tokens=12, top_k=1, use_cache=True)
+    assert torch.equal(a, b)
