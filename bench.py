@@ -72,7 +72,8 @@ def parse_args():
     ap.add_argument("--shard", choices=["channel", "time"], default="channel",
                     help="config5 on >1 GPU: channel shards with y all-gathered, or time "
                          "shards exchanging range summaries (y then all-gathered too)")
-    ap.add_argument("--workload", choices=["config3", "config5", "config2", "decode", "block_glue"],
+    ap.add_argument("--workload", choices=["config3", "config5", "config2", "decode", "block_glue",
+                                           "config4_block"],
                     default="config3",
                     help="config5: B=1, T=65536, D=1536, N=64, bf16, channel-sharded over the "
                          "GPUs with an NCCL all-gather of y (strong scaling)")
@@ -962,6 +963,76 @@ def run_block_glue(args, world, rank, local):
     return 0
 
 
+def run_config4_block(args, world, rank, local):
+    """One block of the config-4 base preset (d_model 768, d_state 64, d_inner
+    1536) at B=4 per GPU, T=2048: forward + loss + backward under bf16 autocast,
+    the per-layer share of a config-4 training step (the full 14.66 B-parameter
+    model does not fit one replica per GPU with an fp32 optimizer). Reports the
+    time split into the per-channel B/C projections (cuBLAS) and the rest, and
+    the projection GEMMs' fraction of the measured bf16 tensor peak."""
+    from mambaqc_b200.models import QuaternionMamba2Block
+
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    bsz, seqlen, dmod, nst = 4, 2048, 768, 64
+    torch.manual_seed(0)
+    blk = QuaternionMamba2Block(dmod, d_state=nst).to(dev)
+    g = torch.Generator(device=dev).manual_seed(1 + rank)
+    x = torch.randn(bsz, seqlen, dmod, generator=g, device=dev).requires_grad_()
+    gout = torch.randn(bsz, seqlen, dmod, generator=g, device=dev)
+
+    def step():
+        blk.zero_grad(set_to_none=True)
+        x.grad = None
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            out = blk(x)
+        (out.float() * gout).sum().backward()
+
+    xa = torch.randn(bsz * seqlen, 2 * dmod, generator=g, device=dev).to(torch.bfloat16)
+    wb = blk.B_proj.weight.detach().to(torch.bfloat16) if hasattr(blk.B_proj, "weight") else None
+
+    def proj_only():
+        # the two per-channel projections' GEMMs of one step: forward and the two
+        # backward GEMMs (input and weight gradients), for B and C
+        for _ in range(2):
+            yb = xa @ wb.t()
+            _ = yb @ wb
+            _ = yb.t() @ xa
+
+    steps = max(3, min(args.steps, 10))
+    step()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(timed(step, steps, max(3, args.warmup), world, stream) / steps, world, dev)
+    ms_proj = None
+    if wb is not None:
+        ms_proj = max_over_ranks(timed(proj_only, steps, 3, world, stream) / steps, world, dev)
+    peaks, peak_kind = measured_peaks()
+    din = 2 * dmod
+    proj_flops = 2 * 3 * 2 * (bsz * seqlen) * din * (din * nst * 4)
+    if rank == 0:
+        line = {
+            "metric": "config-4 base block forward+backward tokens/s (one of 12 layers, bf16 "
+                      "autocast, fp32 scan state)",
+            "value": bsz * seqlen * world / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": steps, "warmup": max(3, args.warmup), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16 autocast", "data": "synthetic (seeded N(0,1) block input)",
+            "config": {"workload": "config4_base_block", "batch_per_gpu": bsz, "seq_len": seqlen,
+                       "d_model": dmod, "d_inner": din, "d_state": nst,
+                       "parallelism": f"dp{world} (independent replicas of one block)"},
+            "bc_projection_gemms_ms": ms_proj,
+            "bc_projection_tflops": (proj_flops / (ms_proj / 1e3) / 1e12) if ms_proj else None,
+            "bc_projection_frac_of_bf16_peak": ((proj_flops / (ms_proj / 1e3) / 1e12) /
+                                                peaks.get("bf16_tflops_sustained",
+                                                          peaks.get("bf16_tflops", 1590.0))
+                                                if ms_proj else None),
+            "bf16_peak_source": f"MEASURED_PEAKS.json ({peak_kind})",
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse_args()
     world, rank, local = dist_setup(args)
@@ -978,6 +1049,8 @@ def main():
             return run_decode(args, world, rank, local)
         if args.workload == "block_glue":
             return run_block_glue(args, world, rank, local)
+        if args.workload == "config4_block":
+            return run_config4_block(args, world, rank, local)
         return run_b200(args, world, rank, local)
     finally:
         if dist.is_initialized():
