@@ -31,7 +31,12 @@ namespace scan {
 constexpr int kSub = MQC_SSM_CKPT_EVERY;
 // Warps per CTA: the recomputed-state buffer is kSub * G * 32 lanes * 16 B per
 // warp, so the CTA shrinks as G grows (G=2: 8 warps, 64 KiB; G=8: 2 warps).
-__host__ __device__ constexpr int bwd_warps(int g) { return 16 / g; }
+// Per-channel B/C with G=2 keeps its states in registers and uses no shared
+// memory; there 4-warp CTAs let 3 CTAs (12 warps) share an SM at ~170
+// registers per thread, against one 8-warp CTA, and shorten the last wave.
+__host__ __device__ constexpr int bwd_warps(int g, bool bc_shared = true) {
+  return (g == 2 && !bc_shared) ? 4 : 16 / g;
+}
 constexpr int kMaxBwdSmem = 227 * 1024;
 
 struct BwdParams {
@@ -130,9 +135,9 @@ __host__ __device__ inline StageLayout stage_layout(int N, int cpb, int warps, i
 }
 
 template <typename T, int G, int NG, bool BC_SHARED, bool S_REAL, bool STAGE>
-__global__ void __launch_bounds__(32 * bwd_warps(G))
+__global__ void __launch_bounds__(32 * bwd_warps(G, BC_SHARED))
     ssm_scan_bwd_kernel(const BwdParams p) {
-  constexpr int kBwdWarps = bwd_warps(G);
+  constexpr int kBwdWarps = bwd_warps(G, BC_SHARED);
   constexpr int CPW = 32 / NG;
   constexpr int NP = NG * G;
   // fp32 with channel-shared B/C (when the stage fits): inputs staged in shared
@@ -854,7 +859,7 @@ int launch_bwd_packed(BwdParams p, cudaStream_t st) {
 
 template <typename T, int G, int NG, bool BC_SHARED, bool S_REAL>
 int launch_bwd(BwdParams p, cudaStream_t st) {
-  constexpr int kBwdWarps = bwd_warps(G);
+  constexpr int kBwdWarps = bwd_warps(G, BC_SHARED);
   constexpr int CPW = 32 / NG;
   p.cpb = kBwdWarps * CPW;
   const size_t base = (G == 2 ? 0 : size_t(kBwdWarps) * kSub * G * 32 * 16) +
