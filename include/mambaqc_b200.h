@@ -96,21 +96,24 @@ MQC_API int mqc_cayley_bwd(const void* z, const void* dq, void* dz, int64_t n, f
 MQC_API int mqc_prefix_prod(const void* q, void* out, int64_t batch, int64_t seq_len, int64_t lanes,
                     int dtype, void* stream);
 
-/* Same result as mqc_prefix_prod (up to rounding: it splits time into chunks
- * whenever the lanes give fewer than 1024 threads per SM, a more eager split
- * than mqc_prefix_prod's), allocating nothing. No counterpart in the
+/* Same result as mqc_prefix_prod, allocating nothing. No counterpart in the
  * reference. For callers that cannot allocate device memory while they run --
  * e.g. a server that gives all device memory to its own allocator at start-up,
  * or a process on a fixed device-memory budget where an allocation failing
  * mid-run is not acceptable. When time is split into chunks, the chunk products
  * live in a fixed 4 MiB static device array that every GPU loading this library
- * holds until exit; sizes needing more (batch * chunks * lanes * 16 bytes) are
- * rejected with MQC_ERR_UNSUPPORTED and a message giving the bytes needed. The
- * first call on a device looks up the array's device address (set-up, once per
- * device, with that device current); make that first call before any stream
- * capture. All calls share the one array: calls that overlap on the GPU (e.g.
- * on two streams of one device) race. Nothing in the array needs clearing
- * between calls: each call writes every entry it reads. */
+ * holds until exit. The chunk count follows mqc_prefix_prod's rule, capped so
+ * that the products (batch * chunks * lanes * 16 bytes) fit in the array; a size
+ * where not even two chunks fit runs as one pass over time, which needs no
+ * scratch. So every size mqc_prefix_prod accepts is served (bit for bit equal
+ * where the cap does not bind, equal up to rounding where it does), and the only
+ * rejections are mqc_prefix_prod's own (MQC_ERR_UNSUPPORTED for a grid beyond
+ * batch 65535). The first call in each device context looks up the array's
+ * device address (set-up, once per context, with that device current); make
+ * that first call before any stream capture. All calls share the one array:
+ * calls that overlap on the GPU (e.g. on two streams of one device) race.
+ * Nothing in the array needs clearing between calls: each call writes every
+ * entry it reads. */
 MQC_API int mqc_prefix_prod_noalloc(const void* q, void* out, int64_t batch, int64_t seq_len,
                                     int64_t lanes, int dtype, void* stream);
 

@@ -182,30 +182,71 @@ namespace {
 constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // 4 MiB = 262144 chunk products
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
 
-constexpr int kMaxDevicesNoAlloc = 64;
-std::mutex g_noalloc_mutex;
-float* g_noalloc_ptr[kMaxDevicesNoAlloc] = {};
+// Device address of g_noalloc_scratch in the current context. In host code the
+// array's name is only a host-side stand-in, so the address is looked up with
+// cudaGetSymbolAddress, with the device current, the first time a context calls
+// this entry point, and cached under that context's process-unique id
+// (cuCtxGetId). A context created later on the same device -- after
+// cudaDeviceReset, or a driver-API context -- has a new id and gets its own
+// lookup, so a cached address never outlives the context it belongs to.
+using CtxGetCurrentFn = int (*)(void**);
+using CtxGetIdFn = int (*)(void*, unsigned long long*);
 
-// Device address of g_noalloc_scratch on the current device. In host code the
-// array's name is only a host-side stand-in, so the address is looked up once per
-// device (with that device current) and cached.
+constexpr int kNoAllocCacheSlots = 64;
+struct NoAllocSlot {
+  unsigned long long ctx_id;
+  float* ptr;
+};
+std::mutex g_noalloc_mutex;
+NoAllocSlot g_noalloc_cache[kNoAllocCacheSlots] = {};
+int g_noalloc_next = 0;
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+CtxGetIdFn g_ctx_get_id = nullptr;
+
 int noalloc_scratch(float** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess)
     return fail(MQC_ERR_CUDA, "mqc_prefix_prod_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
-  if (dev < 0 || dev >= kMaxDevicesNoAlloc)
-    return fail(MQC_ERR_UNSUPPORTED, "mqc_prefix_prod_noalloc: device %d out of range", dev);
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (g_noalloc_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr)
-      return fail(MQC_ERR_CUDA, "mqc_prefix_prod_noalloc: cudaGetSymbolAddress: %s",
-                  cudaGetErrorString(e));
-    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  if (g_ctx_get_current == nullptr || g_ctx_get_id == nullptr) {
+    void* f1 = nullptr;
+    void* f2 = nullptr;
+    cudaDriverEntryPointQueryResult q1{}, q2{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f1, cudaEnableDefault, &q1) != cudaSuccess ||
+        cudaGetDriverEntryPoint("cuCtxGetId", &f2, cudaEnableDefault, &q2) != cudaSuccess ||
+        f1 == nullptr || f2 == nullptr)
+      return fail(MQC_ERR_CUDA, "mqc_prefix_prod_noalloc: driver entry points "
+                                "cuCtxGetCurrent/cuCtxGetId unavailable");
+    g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(f1);
+    g_ctx_get_id = reinterpret_cast<CtxGetIdFn>(f2);
   }
-  *out = g_noalloc_ptr[dev];
+  void* ctx = nullptr;
+  unsigned long long id = 0;
+  if (g_ctx_get_current(&ctx) == 0 && ctx == nullptr) {
+    // the runtime has not bound a context to this thread yet: cudaSetDevice
+    // initialises the device's primary context and makes it current
+    e = cudaSetDevice(dev);
+    if (e != cudaSuccess)
+      return fail(MQC_ERR_CUDA, "mqc_prefix_prod_noalloc: cudaSetDevice: %s",
+                  cudaGetErrorString(e));
+  }
+  if (g_ctx_get_current(&ctx) != 0 || ctx == nullptr || g_ctx_get_id(ctx, &id) != 0)
+    return fail(MQC_ERR_CUDA, "mqc_prefix_prod_noalloc: cannot identify the current context");
+  for (const NoAllocSlot& s : g_noalloc_cache) {
+    if (s.ptr != nullptr && s.ctx_id == id) {
+      *out = s.ptr;
+      return MQC_OK;
+    }
+  }
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || p == nullptr)
+    return fail(MQC_ERR_CUDA, "mqc_prefix_prod_noalloc: cudaGetSymbolAddress: %s",
+                cudaGetErrorString(e));
+  g_noalloc_cache[g_noalloc_next] = NoAllocSlot{id, static_cast<float*>(p)};
+  g_noalloc_next = (g_noalloc_next + 1) % kNoAllocCacheSlots;
+  *out = static_cast<float*>(p);
   return MQC_OK;
 }
 
@@ -218,10 +259,11 @@ int launch_noalloc(const void* qv, void* outv, int64_t batch, int64_t seq_len, i
   MQC_REQUIRE(lane_blocks <= 0x7fffffff && batch <= 65535, MQC_ERR_UNSUPPORTED,
               "mqc_prefix_prod_noalloc: grid too large (batch=%lld lanes=%lld)", (long long)batch,
               (long long)lanes);
-  // time chunks whenever the lanes give fewer than 1024 threads per SM (a more
-  // eager split than mqc_prefix_prod's, kept so that the chunk scratch, and with
-  // it the sizes this entry point rejects, stay as documented)
-  const int64_t want_threads = int64_t(num_sms()) * 1024;
+  // Same chunking rule as mqc_prefix_prod, with the chunk count further capped
+  // so that the chunk products (batch * chunks * lanes * 16 bytes) fit in the
+  // static array; when not even two chunks fit, the single pass runs, which
+  // needs no scratch. Every size mqc_prefix_prod accepts is therefore served.
+  const int64_t want_threads = int64_t(num_sms()) * 256;
   const int64_t have = batch * lanes;
   int64_t nchunks = 1;
   if (have < want_threads && seq_len >= 64) {
@@ -229,6 +271,12 @@ int launch_noalloc(const void* qv, void* outv, int64_t batch, int64_t seq_len, i
     const int64_t max_chunks = seq_len / 32;
     if (nchunks > max_chunks) nchunks = max_chunks;
     if (nchunks > 1024) nchunks = 1024;
+    const int64_t fit = int64_t(kNoAllocScratchBytes / (size_t(have) * 16));
+    if (nchunks > fit) nchunks = fit;
+  }
+  if (nchunks > 1) {
+    const int64_t chunk = (seq_len + nchunks - 1) / nchunks;
+    nchunks = (seq_len + chunk - 1) / chunk;
   }
   if (nchunks <= 1) {
     dim3 grid{unsigned(lane_blocks), unsigned(batch), 1u};
@@ -236,12 +284,11 @@ int launch_noalloc(const void* qv, void* outv, int64_t batch, int64_t seq_len, i
     return check_launch("mqc_prefix_prod_noalloc");
   }
   const int64_t chunk = (seq_len + nchunks - 1) / nchunks;
-  nchunks = (seq_len + chunk - 1) / chunk;
   const size_t need = size_t(batch) * size_t(nchunks) * size_t(lanes) * 16;
+  // unreachable by construction of nchunks; kept as the array's hard guard
   MQC_REQUIRE(need <= kNoAllocScratchBytes, MQC_ERR_UNSUPPORTED,
-              "mqc_prefix_prod_noalloc: this size needs %zu bytes of chunk scratch "
-              "(batch*chunks*lanes*16 with %lld chunks); the static maximum is %zu bytes",
-              need, (long long)nchunks, kNoAllocScratchBytes);
+              "mqc_prefix_prod_noalloc: %zu bytes of chunk scratch exceed the static maximum "
+              "of %zu bytes", need, kNoAllocScratchBytes);
   float* P = nullptr;
   int rc = noalloc_scratch(&P);
   if (rc != MQC_OK) return rc;

@@ -35,6 +35,7 @@ __all__ = [
     "qmul", "qconj", "qinv", "qnorm", "cayley", "prefix_product",
     "ssm_step", "ssm_forward", "ssm_scan_cayley", "layer_norm",
     "layer_norm_padded_compat", "block_forward", "lambda_from_params",
+    "block_ssm_channels",
 ]
 
 
@@ -284,3 +285,32 @@ def block_forward(params: dict, x: torch.Tensor, d_state: int, d_conv: int = 4,
     if return_state:
         return out, h_T
     return out
+
+
+def block_ssm_channels(params: dict, x: torch.Tensor, d_state: int, chans: torch.Tensor,
+                       d_conv: int = 4):
+    """The block's SSM (block.py:130-144 then :168-230) on a subset of channels.
+
+    Runs in_proj, the causal conv + SiLU and dt_proj / gate_proj over all
+    channels (they are cheap and the SSM inputs of a channel need the whole conv
+    output row), but projects B and C only for the channels in ``chans``
+    (rows ``c*d_state*4 .. (c+1)*d_state*4`` of B_proj / C_proj), and scans those.
+    Channels are independent recurrences, so the result equals the same channels
+    of the full block's SSM. Returns (y_q [B,T,k,4], h_T [B,k,N,4]).
+    """
+    bsz, seqlen, _ = x.shape
+    p = params
+    xz = F.linear(x, p["in_proj.weight"], p.get("in_proj.bias"))
+    x_in, _ = xz.chunk(2, dim=-1)
+    d_inner = x_in.shape[-1]
+    xc = F.pad(x_in.transpose(1, 2), (d_conv - 1, 0))
+    xc = F.conv1d(xc, p["conv1d.conv.weight"], p.get("conv1d.conv.bias"), groups=d_inner)
+    xa = F.silu(xc.transpose(1, 2))
+    delta = F.softplus(F.linear(xa, p["dt_proj.weight"], p["dt_proj.bias"]))
+    s_real = torch.sigmoid(F.linear(xa, p["gate_proj.weight"])) * xa
+    rows = (chans[:, None] * (d_state * 4) + torch.arange(d_state * 4)).reshape(-1)
+    k = chans.numel()
+    Bq = F.linear(xa, p["B_proj.weight"][rows]).view(bsz, seqlen, k, d_state, 4)
+    Cq = F.linear(xa, p["C_proj.weight"][rows]).view(bsz, seqlen, k, d_state, 4)
+    Lam = lambda_from_params(p["Lambda_alpha"][chans], p["Lambda_imag"][chans])
+    return ssm_scan_cayley(delta[..., chans], Lam, Bq, Cq, s_real[..., chans], p["D"][chans])

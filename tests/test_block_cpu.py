@@ -74,3 +74,18 @@ def test_lm_structure_and_init_follow_the_reference_layout():
     assert abs(lm.embedding.weight.std().item() - 0.02) < 0.005
     assert abs(lm.layers[0].in_proj.weight.std().item() - 0.02) < 0.005
     assert lm.get_num_params() == sum(p.numel() for p in lm.parameters()) - 2 * 104 * 16
+
+
+def test_oracle_block_ssm_channel_subset_matches_full_block():
+    """The oracle's channel-subset SSM (used by the config-4 GPU test to check
+    sampled channels) equals the same channels of the full oracle block SSM."""
+    from oracle import ref
+
+    torch.manual_seed(0)
+    blk = QuaternionMamba2Block(16, d_state=4)
+    params = {k: v.double() for k, v in blk.state_dict().items()}
+    x = torch.randn(2, 12, 16, generator=torch.Generator().manual_seed(1), dtype=torch.float64)
+    _, h_full = ref.block_forward(params, x, d_state=4, return_state=True)
+    chans = torch.tensor([0, 5, 31])
+    _, h_sub = ref.block_ssm_channels(params, x, 4, chans)
+    assert torch.allclose(h_sub, h_full[:, chans], rtol=1e-12, atol=1e-14)

@@ -67,3 +67,54 @@ def test_block_backward_matches_oracle_autograd():
             assert err < 1e-4, (name, err)
     finally:
         torch.backends.cudnn.allow_tf32 = prev
+
+
+def test_config4_block_shape_bf16_autocast():
+    """The config-4 base block (d_model 768, d_state 64, d_inner 1536) at B=4,
+    T=2048 under bf16 autocast, forward and backward, against the fp64 oracle
+    block. The GPU runs the whole shape; the checks use what a sample can pin:
+    * the block is causal, so with an upstream gradient that is zero outside
+      batch row 0 and steps [0, T0), the output there and every parameter
+      gradient depend only on x[0, :T0]; the oracle block runs that prefix;
+    * channels are independent recurrences, so the final SSM state of sampled
+      channels (all 2048 steps, every batch row) is checked against the oracle
+      SSM on those channels alone.
+    The projection weights are 604 M parameters each; their gradients are
+    compared on the rows of the sampled channels. Tolerance: bf16 (2e-2)."""
+    bsz, seqlen, dmod, nst, t0 = 4, 2048, 768, 64, 45
+    torch.manual_seed(0)
+    blk = QuaternionMamba2Block(dmod, d_state=nst)
+    g = gen(4)
+    x = torch.randn(bsz, seqlen, dmod, generator=g)
+    gout = torch.zeros(bsz, seqlen, dmod)
+    gout[0, :t0] = torch.randn(t0, dmod, generator=g)
+    params = {k: v.detach().double() for k, v in blk.state_dict().items()}
+    blk = blk.to(DEV)
+    xg = x.to(DEV).requires_grad_()
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        out, h_T = blk(xg, return_ssm_state=True)
+    (out.float() * gout.to(DEV)).sum().backward()
+    torch.cuda.synchronize()
+    from mambaqc_b200 import _lib
+    _lib.check_device_status(torch.device(DEV))
+    assert torch.isfinite(out.float()).all() and torch.isfinite(h_T).all()
+
+    chans = torch.tensor([0, 700, 1535])
+    for b in (0, 3):
+        _, h_ref = ref.block_ssm_channels(params, x[b:b + 1].double(), nst, chans)
+        assert rel_l2(h_T[b:b + 1, chans.to(DEV)], h_ref) < RTOL_BF16
+
+    leaves = {k: v.clone().requires_grad_() for k, v in params.items()}
+    xr = x[:1, :t0].double().requires_grad_()
+    out_ref = ref.block_forward(leaves, xr, d_state=nst)
+    (out_ref * gout[:1, :t0].double()).sum().backward()
+    assert rel_l2(out[:1, :t0], out_ref.detach()) < RTOL_BF16
+    assert rel_l2(xg.grad[:1, :t0], xr.grad) < RTOL_BF16
+    rows = (chans[:, None] * (nst * 4) + torch.arange(nst * 4)).reshape(-1)
+    for name, p in blk.named_parameters():
+        want = leaves[name].grad
+        got = p.grad
+        if name in ("B_proj.weight", "C_proj.weight"):
+            got, want = got[rows.to(DEV)], want[rows]
+        err = rel_l2(got, want)
+        assert err < RTOL_BF16, (name, err)

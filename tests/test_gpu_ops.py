@@ -276,3 +276,71 @@ def test_layernorm_backward_matches_oracle(dm):
     assert rel_l2(qg.grad, qr.grad) < 1e-4
     assert rel_l2(ln.gamma.grad, gr.grad) < 1e-5
     assert rel_l2(ln.beta.grad, br.grad) < 1e-6
+
+
+# ------------------------------------------- config 2 at the shapes the bench times
+
+def _cpu64(t):
+    return t.detach().double().cpu()
+
+
+def test_config2_qmul_full_shape():
+    """quaternion_multiply on p, q [2^26, 4] fp32 ~ N(0,1) (bench config 2a)."""
+    g = torch.Generator(device=DEV).manual_seed(0)
+    p = torch.randn(1 << 26, 4, generator=g, device=DEV)
+    q = torch.randn(1 << 26, 4, generator=g, device=DEV)
+    out = quaternion_multiply(p, q)
+    torch.cuda.synchronize()
+    assert rel_l2(out, ref.qmul(_cpu64(p), _cpu64(q))) < RTOL_F32
+
+
+def test_config2_cayley_full_shape():
+    """cayley_discretization_fused on z [2,16,768,64,4] with Re z <= 0 (config 2b)."""
+    g = torch.Generator(device=DEV).manual_seed(1)
+    z = torch.randn(2, 16, 768, 64, 4, generator=g, device=DEV)
+    z[..., 0] = -z[..., 0].abs()
+    q = cayley_discretization_fused(z)
+    torch.cuda.synchronize()
+    want = ref.cayley(_cpu64(z))
+    assert rel_l2(q, want) < RTOL_F32
+    assert bool((quaternion_norm(q) <= 1.0 + 1e-6).all())
+
+
+def test_config2_prefix_product_full_shape_single_pass():
+    """parallel_scan_quaternion on [2,256,768,64,4] with |q| in U(0.9, 0.999)
+    (config 2c): 98304 lanes per batch row fill the GPU, so this runs the
+    single-pass kernel the bench times. Whole-tensor rel-L2 and a per-step check
+    on a few lanes, whose products decay over T."""
+    g = torch.Generator(device=DEV).manual_seed(2)
+    u = torch.randn(2, 256, 768, 64, 4, generator=g, device=DEV)
+    r = torch.rand(2, 256, 768, 64, 1, generator=g, device=DEV) * 0.099 + 0.9
+    qs = u / torch.linalg.vector_norm(u, dim=-1, keepdim=True) * r
+    del u, r
+    out = parallel_scan_quaternion(qs)
+    torch.cuda.synchronize()
+    want = ref.prefix_product(_cpu64(qs))
+    assert rel_l2(out, want) < RTOL_F32
+    lanes = [(0, 0), (767, 63), (300, 17)]
+    for b in (0, 1):
+        for d, n in lanes:
+            got = _cpu64(out[b, :, d, n])
+            exp = want[b, :, d, n]
+            err = (got - exp).norm(dim=-1) / exp.norm(dim=-1)
+            assert float(err.max()) < 1e-5
+
+
+def test_config2_layernorm_full_shape():
+    """QuaternionLayerNorm on [4,2048,768,4] fp32 (config 2d), gamma = 1, beta = 0
+    as in the bench, and with random gamma/beta."""
+    g = torch.Generator(device=DEV).manual_seed(3)
+    x = torch.randn(4, 2048, 768, 4, generator=g, device=DEV)
+    gamma = torch.ones(768, device=DEV)
+    beta = torch.zeros(768, 4, device=DEV)
+    out = quaternion_layer_norm_fused(x, gamma, beta)
+    torch.cuda.synchronize()
+    assert rel_l2(out, ref.layer_norm(_cpu64(x), _cpu64(gamma), _cpu64(beta))) < RTOL_F32
+    gamma = 1.0 + 0.1 * torch.randn(768, generator=g, device=DEV)
+    beta = 0.1 * torch.randn(768, 4, generator=g, device=DEV)
+    out = quaternion_layer_norm_fused(x, gamma, beta)
+    torch.cuda.synchronize()
+    assert rel_l2(out, ref.layer_norm(_cpu64(x), _cpu64(gamma), _cpu64(beta))) < RTOL_F32

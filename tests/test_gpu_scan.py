@@ -76,6 +76,8 @@ CASES = [
     (1, 16, 300, 8, True, False),     # many channels, small N
     (1, 1, 4, 16, True, True),        # T = 1
     (4, 64, 1, 64, True, True),       # one channel
+    (2, 70, 10, 64, False, True),     # per-channel B/C at d_state 64 (the block's layout)
+    (2, 70, 10, 64, False, False),
 ]
 
 

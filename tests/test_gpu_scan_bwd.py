@@ -58,6 +58,9 @@ CASES = [
     (1, 19, 3, 100, True, False),   # G = 4
     (1, 8, 4, 16, True, True),      # one sub-block, no checkpoints
     (2, 1, 4, 16, False, True),     # T = 1
+    (2, 40, 6, 64, False, True),    # per-channel B/C at d_state 64 (the block's layout)
+    (2, 40, 6, 64, False, False),
+    (1, 77, 9, 64, False, True),    # ragged sub-blocks, odd channel count
 ]
 
 
@@ -78,13 +81,22 @@ def test_scan_backward_fp32(case):
         assert err < RTOL_F32, (k, err)
 
 
-def test_scan_backward_bf16():
-    inp = make_scan_inputs(2, 40, 16, 64, shared=True, s_real=True, seed=5)
+@pytest.mark.parametrize("shared,s_real", [(True, True), (False, True), (False, False)])
+def test_scan_backward_bf16(shared, s_real):
+    inp = make_scan_inputs(2, 40, 16, 64, shared=shared, s_real=s_real, seed=5)
     gy = torch.randn(2, 40, 16, 4, generator=gen(6), dtype=torch.float64)
-    _, g_ref = oracle_grads(inp, gy)
-    _, g_gpu = gpu_grads(inp, gy, torch.bfloat16)
-    for k in NAMES:
+    h0 = torch.randn(2, 16, 64, 4, generator=gen(7), dtype=torch.float64)
+    _, g_ref = oracle_grads(inp, gy, h0=h0)
+    _, g_gpu = gpu_grads(inp, gy, torch.bfloat16, h0=h0)
+    for k in (*NAMES, "h0"):
         assert rel_l2(g_gpu[k], g_ref[k]) < RTOL_BF16, k
+    # against the oracle on the bf16-rounded inputs the error is the rounding of
+    # the gradients themselves
+    rounded = {k: (v if k in ("Lambda", "D") else v.to(torch.bfloat16).double())
+               for k, v in inp.items()}
+    _, g_rr = oracle_grads(rounded, gy.float().double(), h0=h0)
+    for k in ("delta", "B", "C", "S"):
+        assert rel_l2(g_gpu[k], g_rr[k]) < 1e-2, k
 
 
 def test_scan_backward_without_final_state_gradient_and_no_h0():
@@ -148,3 +160,76 @@ def test_config3_full_size_backward_channel_sample():
                          x[b:b + 1].to(DEV), Dk.to(DEV))
     (y2 * gy[b:b + 1].to(DEV)).sum().backward()
     assert rel_l2(lv2.grad[cd], g_ref["Lambda"]) < RTOL_F32
+
+
+def _config3_perchannel_inputs(dtype, seed):
+    """Config-3 inputs with the reference block's per-channel B/C
+    [4, 2048, 1536, 64, 4], generated on the GPU (25.8 GB in fp32); the sampled
+    channels are copied to the CPU for the oracle, so both see the same bits."""
+    bsz, seqlen, dm, ds = 4, 2048, 1536, 64
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    x = torch.randn(bsz, seqlen, dm, generator=g, device=DEV)
+    delta = torch.nn.functional.softplus(torch.randn(bsz, seqlen, dm, generator=g, device=DEV) - 3)
+    lam = torch.empty(dm, ds, 4, device=DEV)
+    lam[..., 0] = -torch.exp(torch.empty(dm, ds, device=DEV).uniform_(
+        math.log(1e-3), math.log(1e-1), generator=g))
+    lam[..., 1:] = 0.5 * torch.randn(dm, ds, 3, generator=g, device=DEV)
+    Bm = (torch.randn(bsz, seqlen, dm, ds, 4, generator=g, device=DEV) / 8).to(dtype)
+    Cm = (torch.randn(bsz, seqlen, dm, ds, 4, generator=g, device=DEV) / 8).to(dtype)
+    Dk = 1.0 + 0.1 * torch.randn(dm, generator=g, device=DEV)
+    gy = torch.randn(bsz, seqlen, dm, 4, generator=g, device=DEV)
+    return dict(delta=delta.to(dtype), Lambda=lam, B=Bm, C=Cm, S=x.to(dtype), D=Dk), gy
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_config3_perchannel_full_size_forward_backward_channel_sample(dtype):
+    """Forward + backward at config 3 with per-channel B/C (B=4, T=2048, D=1536,
+    N=64), the layout the reference block feeds the scan: y, h_T and every
+    gradient of sampled channels against the fp64 oracle run on those channels
+    alone (channels are independent recurrences). bf16 inputs are checked
+    against the oracle on the same bf16-rounded values (and the bf16-rounded
+    upstream gradient the backward receives), so the tolerance covers the
+    kernel's fp32 arithmetic and its bf16 output rounding."""
+    from mambaqc_b200 import _lib
+    inp, gy = _config3_perchannel_inputs(dtype, seed=11 if dtype == torch.float32 else 12)
+    leaves = {k: v.requires_grad_() for k, v in inp.items()}
+    y, hT = ssm_scan_cayley(*(leaves[k] for k in NAMES), return_final_state=True)
+    (y.float() * gy).sum().backward()
+    torch.cuda.synchronize()
+    _lib.check_device_status(torch.device(DEV))
+    f32 = dtype == torch.float32
+    tol_y = RTOL_F32 if f32 else RTOL_BF16
+    tol_g = RTOL_F32 if f32 else 1e-2
+    gy_ref = gy.to(dtype).double().cpu()
+    cd = torch.tensor([0, 41, 777, 1535], device=DEV)
+
+    def sample_of(src, b):
+        s = dict(delta=src["delta"][b:b + 1, :, cd], Lambda=inp["Lambda"][cd],
+                 B=src["B"][b:b + 1, :, cd], C=src["C"][b:b + 1, :, cd],
+                 S=src["S"][b:b + 1, :, cd], D=inp["D"][cd])
+        return {k: v.detach().double().cpu() for k, v in s.items()}
+
+    for b in (0, 3):
+        smp = sample_of(inp, b)
+        leaves_ref = {k: v.clone().requires_grad_() for k, v in smp.items()}
+        y_ref, h_ref = ref.ssm_scan_cayley(*(leaves_ref[k] for k in NAMES))
+        (y_ref * gy_ref[b:b + 1, :, cd.cpu()]).sum().backward()
+        assert rel_l2(y[b:b + 1, :, cd], y_ref) < tol_y
+        assert rel_l2(hT[b:b + 1, cd], h_ref) < RTOL_F32
+        for k in ("delta", "S", "B", "C"):
+            err = rel_l2(leaves[k].grad[b:b + 1, :, cd], leaves_ref[k].grad)
+            assert err < tol_g, (k, err)
+    # dLambda and dD sum over the batch: the contribution of row b alone is
+    # checked by rerunning the GPU backward on that row
+    b = 1
+    one = {k: (v.detach()[b:b + 1] if k not in ("Lambda", "D") else v.detach().clone())
+           for k, v in inp.items()}
+    lam1 = one["Lambda"].requires_grad_()
+    d1 = one["D"].requires_grad_()
+    y1 = ssm_scan_cayley(one["delta"], lam1, one["B"], one["C"], one["S"], d1)
+    (y1.float() * gy[b:b + 1]).sum().backward()
+    smp = sample_of(one, 0)
+    _, g_ref = oracle_grads(smp, gy_ref[b:b + 1, :, cd.cpu()])
+    assert rel_l2(lam1.grad[cd], g_ref["Lambda"]) < tol_g
+    assert rel_l2(d1.grad[cd], g_ref["D"]) < tol_g
+    assert torch.isfinite(y.float()).all()
