@@ -62,7 +62,8 @@ def parse_args():
                     help="seconds of CPU work for the cpu_baseline sample")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the forward+backward and per-channel-layout sub-measurements")
-    ap.add_argument("--only", choices=["fwd_bwd", "perchannel"], default=None,
+    ap.add_argument("--only", choices=["fwd_bwd", "perchannel", "perchannel_fwd_bwd"],
+                    default=None,
                     help="run only this sub-measurement and print it (profiling aid)")
     ap.add_argument("--segments", type=int, default=4,
                     help="config5 on >1 GPU: time segments whose all-gather overlaps the "
@@ -303,28 +304,48 @@ def cpu_reference_sample(budget_s, dtype_name, layout, seed=0):
 
 # ----------------------------------------------------------------- main legs
 
+def config3_dict(world, layout):
+    """The `config` object of the config-3 line; both arms print this same dict."""
+    return {"workload": "config3_fused_scan_forward", "batch_per_gpu": BATCH,
+            "global_batch": BATCH * world, "seq_len": SEQ, "d_inner": CHANNELS,
+            "d_state": STATE, "layout": layout, "signal": "real x",
+            "parallelism": f"dp{world} (batch shards, no data-path collective)",
+            "l2": "inputs larger than L2 (310+ MB per step)"}
+
+
 def run_reference(args, world, rank):
+    """The reference arm: the reference's sequential fp32 PyTorch CPU path (the
+    oracle restatement) on the host cores. Each step is a bounded time-prefix of
+    the config-3 workload; `ms_per_step` is the wall time actually spent per
+    timed step and `value` the tokens of the timed steps over that time."""
     if rank != 0:
         return 0
     per_step_budget = min(args.cpu_budget_s, max(0.5, 150.0 / max(1, args.steps + args.warmup)))
-    vals = []
+    tokens = 0
+    seconds = 0.0
     info = None
     for i in range(args.warmup + args.steps):
         v, sample, threads, steps, elapsed = cpu_reference_sample(per_step_budget, args.dtype,
                                                                  args.layout, seed=i)
         if i >= args.warmup:
-            vals.append(v)
-            info = (sample, threads)
-    value = statistics.mean(vals)
+            tokens += BATCH * steps
+            seconds += elapsed
+            info = (sample, threads, steps)
+    value = tokens / seconds
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1e3 * BATCH * SEQ / value, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": "config3_fused_scan_forward", "batch_per_gpu": BATCH,
-                   "seq_len": SEQ, "d_inner": CHANNELS, "d_state": STATE, "layout": args.layout},
+        "ms_per_step": 1e3 * seconds / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32" if args.dtype == "fp32" else "bf16 inputs, f32 state",
+        "data": "synthetic (seeded, config-3 distributions)",
+        "config": config3_dict(world, args.layout),
+        "timed": {"seconds": seconds, "tokens": tokens,
+                  "tokens_per_step": tokens / args.steps,
+                  "note": "each step scans a time-prefix of the config-3 batch for a bounded "
+                          "wall time; ms_per_step is that measured time"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": info[1], "kind": "port",
-                         "sample": info[0] + " per step; tokens/s extrapolated over the prefix"},
+                         "sample": f"{info[0]}; last timed step: {info[2]} timesteps"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -332,10 +353,14 @@ def run_reference(args, world, rank):
     return 0
 
 
-# DRAM bytes (read + write) of one launch of the dominant kernel, from one ncu
-# capture (dram__bytes_read.sum + dram__bytes_write.sum; the capture is
-# summarised under profiles/), keyed by (dtype, layout); None where not captured.
+# DRAM bytes (read + write) of one launch of the dominant kernel, taken from the
+# ncu capture summarised in profiles/scan_fwd_packed_config3.md
+# (dram__bytes_read.sum + dram__bytes_write.sum), keyed by (dtype, layout). This
+# run does not measure it (no profiler runs inside the bench); None where no
+# capture exists.
 NCU_TRAFFIC_BYTES = {("fp32", "shared"): 119.68e6 + 152.29e6}
+NCU_TRAFFIC_SOURCE = ("ncu capture of the same kernel and workload, summarised in "
+                      "profiles/scan_fwd_packed_config3.md; not measured by this run")
 
 
 def launches_per_scan(dtype: str) -> int:
@@ -355,6 +380,9 @@ def run_b200(args, world, rank, local):
         if args.only == "fwd_bwd":
             inp = make_inputs(dev, args.dtype, args.layout, seed=1234 + rank)
             res = run_fwd_bwd(args, inp, dev, world, stream, ssm_scan_cayley)
+        elif args.only == "perchannel_fwd_bwd":
+            res = run_perchannel_fwd_bwd(args, dev, world, stream, ssm_scan_cayley,
+                                         measured_peaks()[0], args.dtype)
         else:
             res = run_perchannel(args, dev, world, stream, ssm_scan_cayley, measured_peaks()[0])
         if rank == 0:
@@ -397,12 +425,14 @@ def run_b200(args, world, rank, local):
                 "unit": "TFLOP/s", "frac": flops / sec / 1e12 / fp32_peak,
                 "peak_source": "FP32 FMA probe (mqc_probe_fp32_fma) run by bench.py, same clocks",
                 "algorithmic_flops_per_launch": flops,
-                "traffic": NCU_TRAFFIC_BYTES.get((args.dtype, args.layout))}
+                "traffic": NCU_TRAFFIC_BYTES.get((args.dtype, args.layout)),
+                "traffic_source": NCU_TRAFFIC_SOURCE}
     roofline_hbm = {"bound": "hbm", "achieved": abytes / sec / 1e9, "peak": peaks["hbm_gbs"],
                     "unit": "GB/s", "frac": abytes / sec / 1e9 / peaks["hbm_gbs"],
                     "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
                     "algorithmic_bytes_per_launch": abytes,
-                    "traffic": NCU_TRAFFIC_BYTES.get((args.dtype, args.layout))}
+                    "traffic": NCU_TRAFFIC_BYTES.get((args.dtype, args.layout)),
+                    "traffic_source": NCU_TRAFFIC_SOURCE}
 
     e2e = None
     if not args.no_e2e:
@@ -416,6 +446,8 @@ def run_b200(args, world, rank, local):
             torch.cuda.empty_cache()
             extras["perchannel_fwd"] = run_perchannel(args, dev, world, stream, ssm_scan_cayley,
                                                       peaks)
+            extras["perchannel_fwd_bwd"] = run_perchannel_fwd_bwd(
+                args, dev, world, stream, ssm_scan_cayley, peaks, "bf16")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -431,11 +463,7 @@ def run_b200(args, world, rank, local):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32" if args.dtype == "fp32" else "bf16 inputs, f32 state",
             "data": "synthetic (seeded, config-3 distributions)",
-            "config": {"workload": "config3_fused_scan_forward", "batch_per_gpu": BATCH,
-                       "global_batch": BATCH * world, "seq_len": SEQ, "d_inner": CHANNELS,
-                       "d_state": STATE, "layout": args.layout, "signal": "real x",
-                       "parallelism": f"dp{world} (batch shards, no data-path collective)",
-                       "l2": "inputs larger than L2 (310+ MB per step)"},
+            "config": config3_dict(world, args.layout),
             "roofline": roofline, "roofline_hbm": roofline_hbm,
             "gpu_launches": args.steps * launches_per_scan(args.dtype), "clocks": clk,
             "e2e": e2e, "cpu_baseline": cpu,
@@ -496,6 +524,76 @@ def run_fwd_bwd(args, inp, dev, world, stream, op):
     # shared dB/dC accumulators, the casts and the sums over batch
     return {"value": BATCH * SEQ * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
             "steps": steps, "what": "scan forward (with checkpoints) + backward, fp32"}
+
+
+def perchannel_bwd_bytes(inp):
+    """Algorithmic bytes of one per-channel scan backward: B, C, delta, x and dy
+    read once; dB, dC, ddelta, dx written once; Lambda read and its per-batch
+    partials written once. The forward's state checkpoints, which the backward
+    also reads, are an artefact of recomputation and are not counted."""
+    es = inp["B"].element_size()
+    bc = inp["B"].numel() * es
+    per_tc = inp["delta"].numel() * inp["delta"].element_size()
+    lam = inp["Lambda"].numel() * 4
+    return 4 * bc + 2 * per_tc + 2 * per_tc + per_tc * 4 + lam + BATCH * lam
+
+
+def run_perchannel_fwd_bwd(args, dev, world, stream, op, peaks, dtype_name):
+    """Forward (with the backward's state checkpoints) + backward of the scan in
+    the reference block's per-channel B/C layout [4,2048,1536,64,4], the config-4
+    training case. HBM-bound: B, C, dB and dC each cross HBM once in the
+    backward. Reports the step and the backward alone (CUDA events around the
+    autograd backward on the launching stream), each against the measured HBM
+    bandwidth."""
+    inp = make_inputs(dev, dtype_name, "perchannel", seed=2468)
+    leaves = {k: v.detach().requires_grad_() for k, v in inp.items()}
+    gy = torch.randn(BATCH, SEQ, CHANNELS, 4, device=dev).to(inp["delta"].dtype)
+    bwd_ms = []
+
+    def step(record=False):
+        for v in leaves.values():
+            v.grad = None
+        y = op(leaves["delta"], leaves["Lambda"], leaves["B"], leaves["C"], leaves["x"],
+               leaves["D"])
+        if record:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        y.backward(gy)
+        if record:
+            e1.record(stream)
+            bwd_ms.append((e0, e1))
+
+    steps = max(3, min(args.steps, 10))
+    ms = timed(lambda: step(True), steps, max(3, min(args.warmup, 3)), world, stream) / steps
+    torch.cuda.synchronize()
+    bwd = [a.elapsed_time(b) for a, b in bwd_ms[-steps:]]
+    ms_bwd = sum(bwd) / len(bwd)
+    es = inp["B"].element_size()
+    fwd_bytes = (2 * inp["B"].numel() * es + 2 * inp["delta"].numel() * inp["delta"].element_size()
+                 + inp["Lambda"].numel() * 4 + inp["delta"].numel() * 4 * es)
+    bwd_bytes = perchannel_bwd_bytes(inp)
+    hbm = peaks["hbm_gbs"]
+    ms_max = max_over_ranks(ms, world, dev)
+    ms_bwd_max = max_over_ranks(ms_bwd, world, dev)
+    res = {
+        "value": BATCH * SEQ * world / (ms_max / 1e3), "unit": "tokens/s", "ms_per_step": ms_max,
+        "backward_ms": ms_bwd_max, "steps": steps,
+        "dtype": "bf16 inputs, f32 state" if dtype_name == "bf16" else "f32",
+        "what": "per-channel B/C scan forward (with checkpoints) + backward",
+        "roofline": {"bound": "hbm", "kernel": "ssm_scan_bwd_pc_kernel (the backward)",
+                     "achieved": bwd_bytes / (ms_bwd / 1e3) / 1e9, "peak": hbm, "unit": "GB/s",
+                     "frac": bwd_bytes / (ms_bwd / 1e3) / 1e9 / hbm,
+                     "algorithmic_bytes_per_launch": bwd_bytes, "traffic": None,
+                     "peak_source": "MEASURED_PEAKS.json hbm_gbs"},
+        "roofline_step": {"bound": "hbm", "achieved": (fwd_bytes + bwd_bytes) / (ms / 1e3) / 1e9,
+                          "peak": hbm, "unit": "GB/s",
+                          "frac": (fwd_bytes + bwd_bytes) / (ms / 1e3) / 1e9 / hbm,
+                          "algorithmic_bytes_per_step": fwd_bytes + bwd_bytes},
+    }
+    del inp, leaves, gy
+    torch.cuda.empty_cache()
+    return res
 
 
 def run_perchannel(args, dev, world, stream, op, peaks):

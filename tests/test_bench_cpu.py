@@ -28,6 +28,14 @@ def test_reference_arm_single_process():
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
     assert line["e2e"]["h2d_bytes_per_step"] == 0
     assert line["higher_is_better"] is True
+    # ms_per_step is the time actually spent per timed step, so it accounts for
+    # the run's wall time; the config dict is the one the GPU arm prints
+    timed = line["timed"]
+    assert abs(line["ms_per_step"] * line["steps"] - 1e3 * timed["seconds"]) < 1e-6 * 1e3 * timed["seconds"] + 1e-6
+    assert abs(line["value"] - timed["tokens"] / timed["seconds"]) < 1e-6 * line["value"]
+    sys.path.insert(0, str(ROOT))
+    import bench
+    assert line["config"] == bench.config3_dict(1, "shared")
 
 
 @pytest.mark.timeout(600)

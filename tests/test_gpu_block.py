@@ -8,7 +8,7 @@ import pytest
 import torch
 
 from oracle import ref
-from tests.gpu_util import DEV, RTOL_F32, gen, make_lambda, rel_l2
+from tests.gpu_util import DEV, RTOL_BF16, RTOL_F32, gen, make_lambda, rel_l2
 
 pytestmark = pytest.mark.gpu
 

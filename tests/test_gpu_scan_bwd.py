@@ -81,11 +81,15 @@ def test_scan_backward_fp32(case):
         assert err < RTOL_F32, (k, err)
 
 
-@pytest.mark.parametrize("shared,s_real", [(True, True), (False, True), (False, False)])
-def test_scan_backward_bf16(shared, s_real):
-    inp = make_scan_inputs(2, 40, 16, 64, shared=shared, s_real=s_real, seed=5)
-    gy = torch.randn(2, 40, 16, 4, generator=gen(6), dtype=torch.float64)
-    h0 = torch.randn(2, 16, 64, 4, generator=gen(7), dtype=torch.float64)
+@pytest.mark.parametrize("shared,s_real,dm", [(True, True, 16), (False, True, 16),
+                                              (False, False, 16), (False, True, 9),
+                                              (False, False, 7)])
+def test_scan_backward_bf16(shared, s_real, dm):
+    # odd channel counts put consecutive steps of a bf16 delta / x in alternating
+    # halves of a 32-bit word
+    inp = make_scan_inputs(2, 40, dm, 64, shared=shared, s_real=s_real, seed=5)
+    gy = torch.randn(2, 40, dm, 4, generator=gen(6), dtype=torch.float64)
+    h0 = torch.randn(2, dm, 64, 4, generator=gen(7), dtype=torch.float64)
     _, g_ref = oracle_grads(inp, gy, h0=h0)
     _, g_gpu = gpu_grads(inp, gy, torch.bfloat16, h0=h0)
     for k in (*NAMES, "h0"):
