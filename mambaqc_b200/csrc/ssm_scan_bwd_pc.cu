@@ -73,31 +73,54 @@ __device__ __forceinline__ float word_value(uint32_t w, int half) {
     return __uint_as_float(half ? (w & 0xffff0000u) : (w << 16));
   }
 }
-// Shared-memory loads issued in program order (ld.volatile.shared): the
+// Shared-memory loads issued in program order (ld.volatile.shared) from a
+// 32-bit shared address plus a compile-time byte offset. In order, because the
 // straight-line sub-block code would otherwise let the compiler hoist the loads
-// of later steps, each holding registers until its step runs; in order, at most
-// about one step of loaded operands is live ahead of its use.
-__device__ __forceinline__ uint32_t lds_u32(const void* p) {
+// of later steps, each holding registers until its step runs; with an
+// immediate offset, because every step's operands sit at fixed offsets from a
+// per-lane base, so no address arithmetic is issued per load.
+template <int OFF>
+__device__ __forceinline__ uint32_t ldsi_u32(uint32_t a) {
   uint32_t v;
-  asm volatile("ld.volatile.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_addr(p)));
+  asm volatile("ld.volatile.shared.u32 %0, [%1+%2];" : "=r"(v) : "r"(a), "n"(OFF));
   return v;
 }
-__device__ __forceinline__ float4 lds_f4(const void* p) {
+template <int OFF>
+__device__ __forceinline__ float4 ldsi_f4(uint32_t a) {
   float4 v;
-  asm volatile("ld.volatile.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+  asm volatile("ld.volatile.shared.v4.f32 {%0, %1, %2, %3}, [%4+%5];"
                : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(smem_addr(p)));
+               : "r"(a), "n"(OFF));
   return v;
 }
-// One quaternion in the storage type from shared memory, in order.
-template <typename T>
-__device__ __forceinline__ float4 lds_q(const T* p) {
+// One quaternion in the storage type.
+template <typename T, int OFF>
+__device__ __forceinline__ float4 ldsi_q(uint32_t a) {
   if constexpr (std::is_same<T, float>::value) {
-    return lds_f4(p);
+    return ldsi_f4<OFF>(a);
   } else {
-    uint32_t a, b;
-    asm volatile("ld.volatile.shared.v2.u32 {%0, %1}, [%2];" : "=r"(a), "=r"(b) : "r"(smem_addr(p)));
-    return QIO<__nv_bfloat16>::unpack(make_uint2(a, b));
+    uint32_t x, y;
+    asm volatile("ld.volatile.shared.v2.u32 {%0, %1}, [%2+%3];"
+                 : "=r"(x), "=r"(y)
+                 : "r"(a), "n"(OFF));
+    return QIO<__nv_bfloat16>::unpack(make_uint2(x, y));
+  }
+}
+
+// f(std::integral_constant<int, I>) for I = B, B+1, ..., E-1 (unrolled at compile time)
+template <int B, int E, typename F>
+__device__ __forceinline__ void static_for(F&& f) {
+  if constexpr (B < E) {
+    f(std::integral_constant<int, B>{});
+    static_for<B + 1, E>(f);
+  }
+}
+// f(std::integral_constant<int, I>) for I = B, B-1, ..., E
+template <int B, int E, typename F>
+__device__ __forceinline__ void static_for_down(F&& f) {
+  if constexpr (B >= E) {
+    f(std::integral_constant<int, B>{});
+    static_for_down<B - 1, E>(f);
   }
 }
 
@@ -125,7 +148,9 @@ constexpr int pc_min_ctas() {
   return 3;
 }
 
-template <typename T, int NG, bool S_REAL>
+// EXACT: N == 2 * NG and every warp has CPW channels, so no lane is padding and
+// no state guard is compiled.
+template <typename T, int NG, bool S_REAL, bool EXACT>
 __global__ void __launch_bounds__(32 * pc_warps<T>(), pc_min_ctas<T>())
     ssm_scan_bwd_pc_kernel(const BwdParams p) {
   using namespace ::mqc::pk;
@@ -140,17 +165,17 @@ __global__ void __launch_bounds__(32 * pc_warps<T>(), pc_min_ctas<T>())
   const int c0 = (blockIdx.x * WARPS + warp) * CPW;  // first channel of this warp
   if (c0 >= p.D) return;                             // warp-uniform; no CTA barriers follow
   const int T_ = p.T, D = p.D, N = p.N;
-  const int nch = min(CPW, D - c0);
-  const bool active = chl < nch;
+  const int nch = EXACT ? CPW : min(CPW, D - c0);
+  const bool active = EXACT || chl < nch;
   const int c = active ? c0 + chl : c0;
   const int n0 = ng, n1 = ng + NG;
-  const bool ok0 = active && n0 < N, ok1 = active && n1 < N;
+  const bool ok0 = EXACT || (active && n0 < N), ok1 = EXACT || (active && n1 < N);
   unsigned char* wbase = smem_raw + size_t(warp) * 2 * G::STAGE_BYTES;
 
   // Zero the padding of both stages once (states N..NP of every channel slot and
   // the slots of absent channels); the copies never write there, so padded
   // lanes read zeros and contribute nothing to the per-channel sums.
-  if (N < NP || nch < CPW) {
+  if (!EXACT && (N < NP || nch < CPW)) {
     for (int st = 0; st < 2; ++st) {
       T* sbc = reinterpret_cast<T*>(wbase + size_t(st) * G::STAGE_BYTES);
       float* shs = reinterpret_cast<float*>(wbase + size_t(st) * G::STAGE_BYTES + G::BC_BYTES);
@@ -269,120 +294,134 @@ __global__ void __launch_bounds__(32 * pc_warps<T>(), pc_min_ctas<T>())
     }
     __syncwarp();
     const unsigned char* stg = wbase + size_t(buf) * G::STAGE_BYTES;
-    const T* sbc = reinterpret_cast<const T*>(stg) + chl * NP * 4;
-    const float* shs = reinterpret_cast<const float*>(stg + G::BC_BYTES) + chl * NP * 4;
+    // per-lane 32-bit shared addresses; every operand below is at a
+    // compile-time offset from one of them
+    constexpr int ES = int(sizeof(T));
+    const uint32_t sbase = smem_addr(stg);
+    const uint32_t bcl = sbase + uint32_t((chl * NP + n0) * 4 * ES);
+    const uint32_t hsl = sbase + uint32_t(G::BC_BYTES + (chl * NP + n0) * 16);
+    const uint32_t itl = sbase + uint32_t(G::BC_BYTES + G::HST_BYTES + chl * G::ITEM_BYTES);
     const bool zero_start = sb == 0 && p.h0 == nullptr;
-    const QPair hstart =
-        zero_start ? qp_zero()
-                   : qp_from(lds_f4(shs + n0 * 4), lds_f4(shs + n1 * 4));
-    auto ld_pair = [&](int tt, int which) -> QPair {
-      const T* r = sbc + (tt * 2 + which) * ROW;
-      return qp_from(lds_q<T>(r + n0 * 4), lds_q<T>(r + n1 * 4));
+    const QPair hstart = zero_start ? qp_zero()
+                                    : qp_from(ldsi_f4<0>(hsl), ldsi_f4<NG * 16>(hsl));
+    // B (which = 0) or C (1) of step TT: the lane's states n0 and n0 + NG
+    auto ld_pair = [&](auto tt_c, auto which_c) -> QPair {
+      constexpr int TT = decltype(tt_c)::value, WH = decltype(which_c)::value;
+      constexpr int OFF = (TT * 2 + WH) * ROW * ES;
+      return qp_from(ldsi_q<T, OFF>(bcl), ldsi_q<T, OFF + NG * 4 * ES>(bcl));
     };
-    // the items of this lane's channel: loads broadcast to its NG lanes
-    const unsigned char* sit = stg + G::BC_BYTES + G::HST_BYTES + chl * G::ITEM_BYTES;
-    // half of the fetched word that holds a bf16 delta / x: the element index
+    // per-(t, channel) items of step TT, broadcast to the channel's NG lanes;
+    // a bf16 delta / x sits in one half of its fetched word: the element index
     // advances by D per step, so with D odd the half alternates with the step
     const int dhalf = half_of(gdelta + ((int64_t(b) * T_ + t0) * D + c));
     const int shalf = half_of(gs + ((int64_t(b) * T_ + t0) * D + c));
     const int dodd = D & 1;
-    auto it_delta = [&](int tt) -> float {
-      return word_value<T>(lds_u32(sit + tt * CPW * G::ITEM_BYTES), dhalf ^ (tt & dodd));
+    auto it_delta = [&](auto tt_c) -> float {
+      constexpr int TT = decltype(tt_c)::value;
+      return word_value<T>(ldsi_u32<TT * CPW * G::ITEM_BYTES>(itl), dhalf ^ (TT & dodd));
     };
-    auto it_dsk = [&](int tt) -> float {
-      return __uint_as_float(lds_u32(sit + tt * CPW * G::ITEM_BYTES + 4));
+    auto it_dsk = [&](auto tt_c) -> float {
+      constexpr int TT = decltype(tt_c)::value;
+      return __uint_as_float(ldsi_u32<TT * CPW * G::ITEM_BYTES + 4>(itl));
     };
-    auto it_s = [&](int tt) -> float4 {
-      const unsigned char* q = sit + tt * CPW * G::ITEM_BYTES;
+    auto it_s = [&](auto tt_c) -> float4 {
+      constexpr int TT = decltype(tt_c)::value;
+      constexpr int OFF = TT * CPW * G::ITEM_BYTES;
       if constexpr (S_REAL)
-        return make_float4(word_value<T>(lds_u32(q + 8), shalf ^ (tt & dodd)), 0.f, 0.f, 0.f);
+        return make_float4(word_value<T>(ldsi_u32<OFF + 8>(itl), shalf ^ (TT & dodd)), 0.f, 0.f,
+                           0.f);
       else
-        return lds_q<T>(reinterpret_cast<const T*>(q + 16));
+        return ldsi_q<T, OFF + 16>(itl);
     };
-    auto it_dy = [&](int tt) -> float4 {
-      return lds_q<T>(reinterpret_cast<const T*>(sit + tt * CPW * G::ITEM_BYTES + 32));
+    auto it_dy = [&](auto tt_c) -> float4 {
+      constexpr int TT = decltype(tt_c)::value;
+      return ldsi_q<T, TT * CPW * G::ITEM_BYTES + 32>(itl);
     };
-    T* dBrow = gdB + int64_t(t0) * bc_step + chl * N * 4;
-    T* dCrow = gdC + int64_t(t0) * bc_step + chl * N * 4;
-    const int64_t row0 = (int64_t(b) * T_ + t0) * D + c;  // (b, t0, c) in [B,T,D]
+    // output pointers at the step the adjoint is on; it walks 7, 6, ..., 0, so
+    // they move back one step per adjoint step
+    T* dBp = gdB + int64_t(t0 + kSub - 1) * bc_step + (chl * N + n0) * 4;
+    T* dCp = gdC + int64_t(t0 + kSub - 1) * bc_step + (chl * N + n0) * 4;
+    T* ddp = static_cast<T*>(p.ddelta) + ((int64_t(b) * T_ + t0 + kSub - 1) * D + c);
+    T* dsp = static_cast<T*>(p.ds) + ((int64_t(b) * T_ + t0 + kSub - 1) * D + c) * (S_REAL ? 1 : 4);
 
     // one recompute step: h_t = q_t (x) h_{t-1} + B_t (x) S_t
-    auto fwd_step = [&](const QPair& h, int tt) -> QPair {
-      const float dl = it_delta(tt);
-      const QPair Bq = ld_pair(tt, 0);
+    auto fwd_step = [&](const QPair& h, auto tt_c) -> QPair {
+      const float dl = it_delta(tt_c);
+      const QPair Bq = ld_pair(tt_c, std::integral_constant<int, 0>{});
       const QPair qv = cayley_pair(dl, dl * dl, lc, eps);
       QPair inj;
       if constexpr (S_REAL) {
-        const float2 s2 = bc2(it_s(tt).x);
+        const float2 s2 = bc2(it_s(tt_c).x);
         inj = QPair{mul2(s2, Bq.x), mul2(s2, Bq.y), mul2(s2, Bq.z), mul2(s2, Bq.w)};
       } else {
-        inj = qp_mul_bcast(Bq, it_s(tt));
+        inj = qp_mul_bcast(Bq, it_s(tt_c));
       }
       return qp_mul_acc(qv, h, inj);
     };
-    // one adjoint step at tt, given the states after steps tt and tt - 1
-    auto adj_step = [&](int tt, const QPair& hcur, const QPair& hprev) {
-      const float dl = it_delta(tt);
-      const float4 sv = it_s(tt);
-      const float4 gy = it_dy(tt);
-      const float dsk = it_dsk(tt);
-      const QPair Bq = ld_pair(tt, 0), Cq = ld_pair(tt, 1);
-      // lambda_t = conj(C_t) (x) dy_t + conj(q_{t+1}) (x) lambda_{t+1}
-      const QPair cg = qp_mul_bcast(qp_conj(Cq), gy);
-      const QPair lam{add2(cg.x, carry.x), add2(cg.y, carry.y), add2(cg.z, carry.z),
-                      add2(cg.w, carry.w)};
-      const QPair qv = cayley_pair(dl, dl * dl, lc, eps);
-      const QPair dq = qp_mul_acc(lam, qp_conj(hprev), qp_zero());
-      const float2 d2 = bc2(dl);
-      const QPair z{mul2(d2, lq.x), mul2(d2, lq.y), mul2(d2, lq.z), mul2(d2, lq.w)};
-      const QPair dz = cayley_vjp_pair(z, dq, eps);
-      const float2 pdp = qp_dot(dz, lq);
-      dlam = QPair{fma2(d2, dz.x, dlam.x), fma2(d2, dz.y, dlam.y), fma2(d2, dz.z, dlam.z),
-                   fma2(d2, dz.w, dlam.w)};
-      QPair dB;
-      float4 psum = make_float4(ng == 0 ? dsk * gy.x : 0.f, ng == 0 ? dsk * gy.y : 0.f,
-                                ng == 0 ? dsk * gy.z : 0.f, ng == 0 ? dsk * gy.w : 0.f);
-      if constexpr (S_REAL) {
-        const float2 s2 = bc2(sv.x);
-        dB = QPair{mul2(s2, lam.x), mul2(s2, lam.y), mul2(s2, lam.z), mul2(s2, lam.w)};
-        const float2 bl = qp_dot(Bq, lam);
-        psum.x += bl.x + bl.y;
-      } else {
-        dB = qp_mul_bcast(lam, qconj(sv));
-        const QPair pl = qp_mul_acc(qp_conj(Bq), lam, qp_zero());
-        psum.x += pl.x.x + pl.x.y;
-        psum.y += pl.y.x + pl.y.y;
-        psum.z += pl.z.x + pl.z.y;
-        psum.w += pl.w.x + pl.w.y;
-      }
-      const QPair dC = qp_bmul(gy, qp_conj(hcur));
-      if (ok0) {
-        QIO<T>::st(dBrow + tt * bc_step + n0 * 4, qp_half(dB, 0));
-        QIO<T>::st(dCrow + tt * bc_step + n0 * 4, qp_half(dC, 0));
-      }
-      if (ok1) {
-        QIO<T>::st(dBrow + tt * bc_step + n1 * 4, qp_half(dB, 1));
-        QIO<T>::st(dCrow + tt * bc_step + n1 * 4, qp_half(dC, 1));
-      }
-      carry = qp_mul_acc(qp_conj(qv), lam, qp_zero());
-      // sum ddelta and dS over the channel's lanes at once (no partials are held
-      // across steps, which keeps the sub-block's register set small)
-      if constexpr (S_REAL) {
-        float v[2] = {pdp.x + pdp.y, psum.x};
-        const int k = reduce_scatter<2, NG>(v, ng);  // lanes with ng & 1 == k hold sum k
-        if (active && (ng >> 1) == 0) {
-          const int64_t row = row0 + int64_t(tt) * D;
-          QIO<T>::st1(static_cast<T*>(k == 0 ? p.ddelta : p.ds) + row, v[0]);
+    // one adjoint step at TT, given the states after steps TT and TT - 1; runs
+    // for TT < len only, but moves the output pointers back in every case
+    auto adj_step = [&](auto tt_c, bool run, const QPair& hcur, const QPair& hprev) {
+      if (run) {
+        const float dl = it_delta(tt_c);
+        const float4 sv = it_s(tt_c);
+        const float4 gy = it_dy(tt_c);
+        const float dsk = it_dsk(tt_c);
+        const QPair Bq = ld_pair(tt_c, std::integral_constant<int, 0>{});
+        const QPair Cq = ld_pair(tt_c, std::integral_constant<int, 1>{});
+        // lambda_t = conj(C_t) (x) dy_t + conj(q_{t+1}) (x) lambda_{t+1}
+        const QPair cg = qp_mul_bcast(qp_conj(Cq), gy);
+        const QPair lam{add2(cg.x, carry.x), add2(cg.y, carry.y), add2(cg.z, carry.z),
+                        add2(cg.w, carry.w)};
+        const QPair qv = cayley_pair(dl, dl * dl, lc, eps);
+        const QPair dq = qp_mul_acc(lam, qp_conj(hprev), qp_zero());
+        const float2 d2 = bc2(dl);
+        const QPair z{mul2(d2, lq.x), mul2(d2, lq.y), mul2(d2, lq.z), mul2(d2, lq.w)};
+        const QPair dz = cayley_vjp_pair(z, dq, eps);
+        const float2 pdp = qp_dot(dz, lq);
+        dlam = QPair{fma2(d2, dz.x, dlam.x), fma2(d2, dz.y, dlam.y), fma2(d2, dz.z, dlam.z),
+                     fma2(d2, dz.w, dlam.w)};
+        QPair dB;
+        float4 psum = make_float4(ng == 0 ? dsk * gy.x : 0.f, ng == 0 ? dsk * gy.y : 0.f,
+                                  ng == 0 ? dsk * gy.z : 0.f, ng == 0 ? dsk * gy.w : 0.f);
+        if constexpr (S_REAL) {
+          const float2 s2 = bc2(sv.x);
+          dB = QPair{mul2(s2, lam.x), mul2(s2, lam.y), mul2(s2, lam.z), mul2(s2, lam.w)};
+          const float2 bl = qp_dot(Bq, lam);
+          psum.x += bl.x + bl.y;
+        } else {
+          dB = qp_mul_bcast(lam, qconj(sv));
+          const QPair pl = qp_mul_acc(qp_conj(Bq), lam, qp_zero());
+          psum.x += pl.x.x + pl.x.y;
+          psum.y += pl.y.x + pl.y.y;
+          psum.z += pl.z.x + pl.z.y;
+          psum.w += pl.w.x + pl.w.y;
         }
-      } else {
-        float v[8] = {pdp.x + pdp.y, psum.x, psum.y, psum.z, psum.w, 0.f, 0.f, 0.f};
-        const int k = reduce_scatter<8, NG>(v, ng);  // one sum per lane (8 <= NG)
-        if (active && (ng >> 3) == 0 && k <= 4) {
-          const int64_t row = row0 + int64_t(tt) * D;
-          if (k == 0) QIO<T>::st1(static_cast<T*>(p.ddelta) + row, v[0]);
-          else QIO<T>::st1(static_cast<T*>(p.ds) + row * 4 + (k - 1), v[0]);
+        const QPair dC = qp_bmul(gy, qp_conj(hcur));
+        if (ok0) {
+          QIO<T>::st(dBp, qp_half(dB, 0));
+          QIO<T>::st(dCp, qp_half(dC, 0));
+        }
+        if (ok1) {
+          QIO<T>::st(dBp + NG * 4, qp_half(dB, 1));
+          QIO<T>::st(dCp + NG * 4, qp_half(dC, 1));
+        }
+        carry = qp_mul_acc(qp_conj(qv), lam, qp_zero());
+        // sum ddelta and dS over the channel's lanes at once (no partials are
+        // held across steps, which keeps the sub-block's register set small)
+        if constexpr (S_REAL) {
+          float v[2] = {pdp.x + pdp.y, psum.x};
+          const int k = reduce_scatter<2, NG>(v, ng);  // lanes with ng & 1 == k hold sum k
+          if (active && (ng >> 1) == 0) QIO<T>::st1(k == 0 ? ddp : dsp, v[0]);
+        } else {
+          float v[8] = {pdp.x + pdp.y, psum.x, psum.y, psum.z, psum.w, 0.f, 0.f, 0.f};
+          const int k = reduce_scatter<8, NG>(v, ng);  // one sum per lane (8 <= NG)
+          if (active && (ng >> 3) == 0 && k <= 4) QIO<T>::st1(k == 0 ? ddp : dsp + (k - 1), v[0]);
         }
       }
+      dBp -= bc_step;
+      dCp -= bc_step;
+      ddp -= D;
+      dsp -= int64_t(D) * (S_REAL ? 1 : 4);
     };
     // The sub-block runs in two halves so that at most five recomputed states are
     // live (instead of kSub): pass A recomputes steps 0..7 and keeps the states
@@ -394,29 +433,31 @@ __global__ void __launch_bounds__(32 * pc_warps<T>(), pc_min_ctas<T>())
       QPair hk[5];  // states after steps 3..7
       {
         QPair h = hstart;
-#pragma unroll
-        for (int tt = 0; tt < kSub; ++tt) {
-          if (FULL || tt < len) h = fwd_step(h, tt);
-          if (tt >= 3) hk[tt - 3] = h;
-        }
+        static_for<0, kSub>([&](auto tt_c) {
+          constexpr int TT = decltype(tt_c)::value;
+          if (FULL || TT < len) h = fwd_step(h, tt_c);
+          if constexpr (TT >= 3) hk[TT - 3] = h;
+        });
       }
-#pragma unroll
-      for (int tt = kSub - 1; tt >= 4; --tt)
-        if (FULL || tt < len) adj_step(tt, hk[tt - 3], hk[tt - 4]);
+      static_for_down<kSub - 1, 4>([&](auto tt_c) {
+        constexpr int TT = decltype(tt_c)::value;
+        adj_step(tt_c, FULL || TT < len, hk[TT - 3], hk[TT - 4]);
+      });
       QPair hl[3];  // states after steps 0..2
       {
         QPair h = hstart;
-#pragma unroll
-        for (int tt = 0; tt < 3; ++tt) {
-          if (FULL || tt < len) h = fwd_step(h, tt);
-          hl[tt] = h;
-        }
+        static_for<0, 3>([&](auto tt_c) {
+          constexpr int TT = decltype(tt_c)::value;
+          if (FULL || TT < len) h = fwd_step(h, tt_c);
+          hl[TT] = h;
+        });
       }
-#pragma unroll
-      for (int tt = 3; tt >= 0; --tt)
-        if (FULL || tt < len)
-          adj_step(tt, tt == 3 ? hk[0] : hl[tt < 3 ? tt : 0],
-                   tt == 0 ? hstart : hl[tt > 0 ? tt - 1 : 0]);
+      static_for_down<3, 0>([&](auto tt_c) {
+        constexpr int TT = decltype(tt_c)::value;
+        if constexpr (TT == 3) adj_step(tt_c, FULL || TT < len, hk[0], hl[2]);
+        else if constexpr (TT == 0) adj_step(tt_c, FULL || TT < len, hl[0], hstart);
+        else adj_step(tt_c, FULL || TT < len, hl[TT], hl[TT - 1]);
+      });
     };
     if (len == kSub) run_sub(std::true_type{});
     else run_sub(std::false_type{});
@@ -440,7 +481,9 @@ int launch_pc(const BwdParams& p, cudaStream_t st) {
   using G = PcGeom<T, NG>;
   constexpr int WARPS = pc_warps<T>();
   const size_t smem = size_t(WARPS) * 2 * G::STAGE_BYTES;
-  auto kern = ssm_scan_bwd_pc_kernel<T, NG, S_REAL>;
+  const bool exact = p.N == 2 * NG && p.D % G::CPW == 0;
+  auto kern = exact ? ssm_scan_bwd_pc_kernel<T, NG, S_REAL, true>
+                    : ssm_scan_bwd_pc_kernel<T, NG, S_REAL, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess)
     return fail(MQC_ERR_CUDA, "mqc_ssm_scan_bwd: smem attribute (%zu B): %s", smem,
