@@ -70,6 +70,8 @@ def parse_args():
                          "scan of the next segment")
     ap.add_argument("--decode-batch", type=int, default=4,
                     help="decode workload: sequences decoded together per GPU")
+    ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
+                    help="config5 on >1 GPU: how y is assembled on every rank")
     ap.add_argument("--shard", choices=["channel", "time"], default="channel",
                     help="config5 on >1 GPU: channel shards with y all-gathered, or time "
                          "shards exchanging range summaries (y then all-gathered too)")
@@ -439,6 +441,16 @@ def run_b200(args, world, rank, local):
         e2e = run_e2e(args, inp, dev, world, stream, ssm_scan_cayley)
 
     extras = {}
+    # the work the hot path shards over GPUs, measured at every N: config 3 as one
+    # 8192-token problem split over the ranks, and config 5 with its y exchange
+    if args.layout == "shared":
+        del inp, out
+        torch.cuda.empty_cache()
+        extras["config3_strong"] = config3_strong_measure(args, world, rank, local)
+        extras["config5"] = config5_measure(args, world, rank, local, gather=args.gather)
+        torch.cuda.empty_cache()
+        inp = make_inputs(dev, args.dtype, args.layout, seed=1234 + rank)
+        out = {}
     if not args.no_extras:
         extras["fwd_bwd"] = run_fwd_bwd(args, inp, dev, world, stream, ssm_scan_cayley)
         if args.layout == "shared":
@@ -625,11 +637,15 @@ def run_perchannel(args, dev, world, stream, op, peaks):
 C5_SEQ = 65536
 
 
-def run_config5(args, world, rank, local):
-    """Long-sequence single-block scan forward, channel-sharded: every rank holds
-    D/world channels of delta/x/Lambda/D and the shared B/C, scans them
-    time-parallel, and one NCCL all-gather assembles y [1, T, D, 4] on every rank.
-    One step = local scan + all-gather + reassembly; max over ranks."""
+def config5_measure(args, world, rank, local, gather="peer"):
+    """Config 5 (B=1, T=65536, D=1536, N=64, bf16 inputs, fp32 state),
+    channel-sharded over the ranks: every rank holds D/world channels of
+    delta/x/Lambda/D and the shared B/C, scans them time-parallel, and the
+    output y [1, T, D, 4] is assembled on every rank. ``gather="peer"``: each
+    scanned time segment is pushed straight into its channel columns of every
+    rank's output over NVLink (no permute), under the scan of the next segment;
+    ``"nccl"``: NCCL all_gather_into_tensor per segment plus a permute. One step
+    = local scan + exchange; max over ranks. Returns the measurement dict."""
     from mambaqc_b200.kernels import ssm_scan_cayley
     from mambaqc_b200.kernels.sharded import ssm_scan_cayley_channel_sharded
     from mambaqc_b200.kernels.ssm_fused import auto_time_chunks
@@ -659,7 +675,8 @@ def run_config5(args, world, rank, local):
 
     def step():
         out["y"] = ssm_scan_cayley_channel_sharded(
-            delta, lam, Bm, Cm, x, Dk, time_chunks="auto" if segs > 1 else nc, segments=segs)
+            delta, lam, Bm, Cm, x, Dk, time_chunks="auto" if segs > 1 else nc, segments=segs,
+            gather=gather)
 
     def scan_only():
         out["yl"] = ssm_scan_cayley(delta, lam, Bm, Cm, x, Dk, time_chunks=nc)
@@ -673,27 +690,89 @@ def run_config5(args, world, rank, local):
         ms_max = max_over_ranks(ms, world, dev)
         ms_scan = timed(scan_only, steps, 3, world, stream) / steps
         ms_scan_max = max_over_ranks(ms_scan, world, dev)
+    del out
     elems = C5_SEQ * CHANNELS * STATE
+    how = ("peer-memory push of every scanned segment into all ranks' outputs over NVLink "
+           "(mqc_channel_push), ordered by two 1-element NCCL all-reduces" if gather == "peer"
+           else "NCCL all_gather_into_tensor of y per time segment plus a permute")
+    return {
+        "value": C5_SEQ / (ms_max / 1e3), "unit": "tokens/s", "ms_per_step": ms_max,
+        "steps": steps, "scaling": "strong", "n_gpus": world,
+        "dtype": "bf16 inputs, f32 state",
+        "config": {"workload": "config5_channel_sharded", "batch": 1, "seq_len": C5_SEQ,
+                   "d_inner": CHANNELS, "d_state": STATE, "channels_per_gpu": dl,
+                   "time_chunks": nc, "segments": segs,
+                   "parallelism": f"channel shards x{world}" + (
+                       f", y exchange: {how}, overlapped with the scan of the next segment"
+                       if world > 1 else "")},
+        "scan_only_ms": ms_scan_max,
+        "exchange_exposed_ms": ms_max - ms_scan_max,
+        "scan_fp32_tflops_per_gpu": elems / world * FLOPS_PER_ELEM_SREAL / (ms_scan_max / 1e3) / 1e12,
+    }
+
+
+def run_config5(args, world, rank, local):
+    """`--workload config5`: the config-5 measurement as its own JSON line."""
+    res = config5_measure(args, world, rank, local, gather=args.gather)
     if rank == 0:
         line = {
             "metric": "config5 long-sequence scan forward tokens/s (B=1, T=65536, D=1536, N=64, "
-                      "channel-sharded, y all-gathered)",
-            "value": C5_SEQ / (ms_max / 1e3), "unit": "tokens/s", "n_gpus": world,
-            "steps": steps, "warmup": max(3, args.warmup), "ms_per_step": ms_max,
+                      "channel-sharded, y assembled on every rank)",
+            "value": res["value"], "unit": "tokens/s", "n_gpus": world, "steps": res["steps"],
+            "warmup": max(3, args.warmup), "ms_per_step": res["ms_per_step"],
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "bf16 inputs, f32 state", "data": "synthetic (seeded, config-3 distributions)",
-            "config": {"workload": "config5_channel_sharded", "batch": 1, "seq_len": C5_SEQ,
-                       "d_inner": CHANNELS, "d_state": STATE, "channels_per_gpu": dl,
-                       "time_chunks": nc, "segments": segs,
-                       "parallelism": f"channel shards x{world}, NCCL all_gather_into_tensor "
-                                      f"of y per time segment ({segs}), overlapped with the "
-                                      "scan of the next segment"},
-            "scan_only_ms": ms_scan_max,
-            "gather_and_reassembly_ms": ms_max - ms_scan_max,
-            "scan_fp32_tflops_per_gpu": elems / world * FLOPS_PER_ELEM_SREAL / (ms_scan_max / 1e3) / 1e12,
+            "dtype": res["dtype"], "data": "synthetic (seeded, config-3 distributions)",
+            "config": res["config"], "scan_only_ms": res["scan_only_ms"],
+            "exchange_exposed_ms": res["exchange_exposed_ms"],
+            "scan_fp32_tflops_per_gpu": res["scan_fp32_tflops_per_gpu"],
         }
         print(json.dumps(line), flush=True)
     return 0
+
+
+def config3_strong_measure(args, world, rank, local):
+    """Config 3 as one problem of 8192 tokens (B=4, T=2048, D=1536, N=64, shared
+    B/C, fp32) split over the ranks: batch shards while the ranks divide the
+    batch (4/world rows each), then batch 4-way x channel world/4-way (at 8 GPUs:
+    one batch row and 768 channels per rank). Each rank scans its shard with no
+    collective on the data path; tokens/s = 8192 / max-rank time."""
+    from mambaqc_b200.kernels import ssm_scan_cayley
+
+    dev = torch.device(f"cuda:{local}")
+    bs = math.gcd(BATCH, world)
+    cs = world // bs
+    if CHANNELS % cs:
+        raise SystemExit(f"{CHANNELS} channels do not split {cs} ways")
+    rows, dl = BATCH // bs, CHANNELS // cs
+    g = torch.Generator(device=dev).manual_seed(4000 + rank)
+    f32 = torch.float32
+    x = torch.randn(rows, SEQ, dl, generator=g, device=dev, dtype=f32)
+    delta = torch.nn.functional.softplus(torch.randn(rows, SEQ, dl, generator=g, device=dev) - 3)
+    lam = torch.empty(dl, STATE, 4, device=dev)
+    u = torch.rand(dl, STATE, generator=g, device=dev)
+    lam[..., 0] = -torch.exp(u * (math.log(1e-1) - math.log(1e-3)) + math.log(1e-3))
+    lam[..., 1:] = 0.5 * torch.randn(dl, STATE, 3, generator=g, device=dev)
+    Bm = torch.randn(rows, SEQ, STATE, 4, generator=g, device=dev) / math.sqrt(STATE)
+    Cm = torch.randn(rows, SEQ, STATE, 4, generator=g, device=dev) / math.sqrt(STATE)
+    Dk = torch.ones(dl, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    out = {}
+
+    def step():
+        out["y"] = ssm_scan_cayley(delta, lam, Bm, Cm, x, Dk)
+
+    steps = max(3, min(args.steps, 20))
+    with torch.no_grad():
+        ms = timed(step, steps, max(3, min(args.warmup, 5)), world, stream) / steps
+    ms_max = max_over_ranks(ms, world, dev)
+    del out
+    return {"value": BATCH * SEQ / (ms_max / 1e3), "unit": "tokens/s", "ms_per_step": ms_max,
+            "steps": steps, "scaling": "strong", "n_gpus": world, "dtype": "f32",
+            "config": {"workload": "config3_fused_scan_forward", "global_batch": BATCH,
+                       "seq_len": SEQ, "d_inner": CHANNELS, "d_state": STATE, "layout": "shared",
+                       "shard": {"batch_rows_per_gpu": rows, "channels_per_gpu": dl,
+                                 "batch_ways": bs, "channel_ways": cs},
+                       "parallelism": "batch x channel shards, no data-path collective"}}
 
 
 def run_config5_time(args, world, rank, local):
@@ -1152,6 +1231,8 @@ def main():
         return run_b200(args, world, rank, local)
     finally:
         if dist.is_initialized():
+            from mambaqc_b200.kernels.sharded import release_peer_outputs
+            release_peer_outputs()
             dist.destroy_process_group()
 
 

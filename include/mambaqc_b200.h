@@ -246,6 +246,31 @@ MQC_API int mqc_ssm_scan_carry(const float* P, const float* E, const float* h0, 
                                float* hT, int64_t segments, int64_t batch, int64_t lanes,
                                void* stream);
 
+/* ---- peer-memory exchange between the ranks of one node ------------------- */
+/* No counterpart in the reference, which has no multi-GPU code. Used by the
+ * channel-sharded scan to write each rank's output channels straight into every
+ * rank's full output over NVLink (plain stores to peer memory; no multicast). */
+
+#define MQC_PEER_HANDLE_BYTES 64
+
+/* cudaMalloc(bytes) on the current device, with the 64-byte IPC handle another
+ * process of this node passes to mqc_peer_open to address the same memory. */
+MQC_API int mqc_peer_alloc(size_t bytes, void** ptr, void* handle);
+MQC_API int mqc_peer_free(void* ptr);
+/* Maps a peer's buffer (from its mqc_peer_alloc handle) into this process. */
+MQC_API int mqc_peer_open(const void* handle, void** ptr);
+MQC_API int mqc_peer_close(void* ptr);
+
+/* Copies a time segment of this rank's channel shard, src [batch, seg_len,
+ * ch_local, 4] (dtype, contiguous), into rows t_off .. t_off+seg_len-1 and
+ * channels ch_off .. ch_off+ch_local-1 of each of the ndst (<= 8) outputs
+ * dsts[r] [batch, seq_total, ch_total, 4] -- local or peer memory. Ends with a
+ * system-scope fence, so a rank that synchronises with this kernel's
+ * completion (e.g. through a collective ordered after it) sees the data. */
+MQC_API int mqc_channel_push(const void* src, void* const* dsts, int ndst, int64_t batch,
+                             int64_t seg_len, int64_t ch_local, int64_t ch_total, int64_t ch_off,
+                             int64_t t_off, int64_t seq_total, int dtype, void* stream);
+
 /*
  * Backward of mqc_ssm_scan_fwd without Q_GIVEN (the fused Cayley form). The
  * reference has no GPU backward (its Triton kernels are not differentiable);

@@ -115,7 +115,14 @@ _SIGNATURES.update({
                            _i64, _c_void_p],
     "mqc_ssm_scan_fwd_chunked_resume": [ctypes.POINTER(SsmScanArgs), _i64, _c_void_p,
                                         ctypes.c_size_t, _c_void_p],
+    "mqc_peer_alloc": [ctypes.c_size_t, ctypes.POINTER(_c_void_p), _c_void_p],
+    "mqc_peer_free": [_c_void_p],
+    "mqc_peer_open": [_c_void_p, ctypes.POINTER(_c_void_p)],
+    "mqc_peer_close": [_c_void_p],
+    "mqc_channel_push": [_c_void_p, ctypes.POINTER(_c_void_p), _i32, _i64, _i64, _i64, _i64,
+                         _i64, _i64, _i64, _i32, _c_void_p],
 })
+MQC_PEER_HANDLE_BYTES = 64
 _SIZE_FUNCS = {"mqc_qln_bwd_workspace_size": [_i64, _i64],
                "mqc_ssm_scan_fwd_chunked_workspace_size": [_i64, _i64, _i64, _i64],
                "mqc_conv_silu_bwd_workspace_size": [_i64, _i64, _i64, _i64],

@@ -18,13 +18,130 @@ final state of the whole sequence is known on every rank.
 
 from __future__ import annotations
 
+import ctypes
 from typing import Callable
 
 import torch
 import torch.distributed as dist
 
 __all__ = ["channel_shard", "time_shard", "ssm_scan_cayley_channel_sharded",
-           "ssm_scan_cayley_time_sharded"]
+           "ssm_scan_cayley_time_sharded", "PeerOutput", "channel_push"]
+
+
+class _CudaArray:
+    """A device buffer presented through __cuda_array_interface__ (zero copy)."""
+
+    # bf16 is exposed as int16 and reinterpreted by the caller
+    _TYPESTR = {torch.float32: "<f4", torch.bfloat16: "<i2"}
+
+    def __init__(self, ptr: int, shape: tuple, dtype: torch.dtype):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": self._TYPESTR[dtype],
+                                         "data": (ptr, False), "version": 3, "strides": None}
+
+
+class PeerOutput:
+    """One output buffer per rank that every rank of the group can write.
+
+    Each rank allocates ``shape`` x ``dtype`` with ``mqc_peer_alloc`` and the
+    ranks exchange the IPC handles (an all-gather of 64-byte objects), so
+    ``ptrs[r]`` addresses rank r's buffer from this process (peer memory over
+    NVLink for r != rank). ``tensor`` is this rank's own buffer as a torch
+    tensor. The buffers live until ``close()``.
+    """
+
+    def __init__(self, shape: tuple, dtype: torch.dtype, device: torch.device, group=None):
+        from .. import _lib
+        lib = _lib.load()
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.shape, self.dtype = tuple(shape), dtype
+        nbytes = 1
+        for n in shape:
+            nbytes *= int(n)
+        nbytes *= torch.empty((), dtype=dtype).element_size()
+        with torch.cuda.device(device):
+            own = ctypes.c_void_p()
+            handle = ctypes.create_string_buffer(_lib.MQC_PEER_HANDLE_BYTES)
+            _lib.check(lib.mqc_peer_alloc(nbytes, ctypes.byref(own), handle), "mqc_peer_alloc")
+            handles = [None] * self.world
+            dist.all_gather_object(handles, handle.raw, group=group)
+            self._own = own.value
+            self._opened = []
+            ptrs = []
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(self._own)
+                    continue
+                peer = ctypes.c_void_p()
+                hb = ctypes.create_string_buffer(h, _lib.MQC_PEER_HANDLE_BYTES)
+                _lib.check(lib.mqc_peer_open(hb, ctypes.byref(peer)), "mqc_peer_open")
+                self._opened.append(peer.value)
+                ptrs.append(peer.value)
+        self.ptrs = ptrs
+        self.tensor = torch.as_tensor(_CudaArray(self._own, shape, dtype), device=device)
+        if dtype == torch.bfloat16:
+            self.tensor = self.tensor.view(torch.bfloat16)
+
+    def close_peers(self) -> None:
+        """Unmaps the other ranks' buffers."""
+        from .. import _lib
+        lib = _lib.load()
+        for ptr in self._opened:
+            lib.mqc_peer_close(ptr)
+        self._opened = []
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers and frees this rank's own. Every rank that
+        mapped this rank's buffer must have unmapped it first."""
+        from .. import _lib
+        lib = _lib.load()
+        self.close_peers()
+        self.tensor = None
+        if self._own is not None:
+            lib.mqc_peer_free(self._own)
+            self._own = None
+
+
+def channel_push(src: torch.Tensor, dst_ptrs: list[int], seq_total: int, ch_total: int,
+                 ch_off: int, t_off: int, stream=None) -> None:
+    """Writes src [B, seg, Dl, 4] into rows t_off.. and channels ch_off.. of every
+    destination [B, seq_total, ch_total, 4] (device addresses, local or peer)
+    with ``mqc_channel_push`` on ``stream`` (default: the current stream)."""
+    from .. import _lib
+    bsz, seg, dl = src.shape[:3]
+    arr = (ctypes.c_void_p * len(dst_ptrs))(*dst_ptrs)
+    st = stream if stream is not None else torch.cuda.current_stream(src.device)
+    _lib.call("mqc_channel_push", src.data_ptr(), arr, len(dst_ptrs), bsz, seg, dl, ch_total,
+              ch_off, t_off, seq_total, _lib.dtype_code(src), st.cuda_stream)
+
+
+_peer_outputs: dict = {}
+
+
+def _peer_output(shape, dtype, device, group) -> PeerOutput:
+    key = (tuple(shape), dtype, str(device), id(group))
+    out = _peer_outputs.get(key)
+    if out is None:
+        out = _peer_outputs[key] = PeerOutput(shape, dtype, device, group)
+    return out
+
+
+def release_peer_outputs() -> None:
+    """Closes every cached PeerOutput. Collective: every rank of each buffer's
+    group calls it, before the process group is destroyed. Ranks first unmap
+    their peers' buffers, then (after a barrier) free their own."""
+    if not _peer_outputs:
+        return
+    torch.cuda.synchronize()
+    groups = {id(o.group): o.group for o in _peer_outputs.values()}
+    for out in _peer_outputs.values():
+        out.close_peers()
+    for g in groups.values():
+        dist.barrier(group=g)
+    for out in _peer_outputs.values():
+        out.close()
+    _peer_outputs.clear()
 
 
 def channel_shard(t: torch.Tensor, rank: int, world: int, dim: int) -> torch.Tensor:
@@ -56,7 +173,7 @@ def ssm_scan_cayley_channel_sharded(delta: torch.Tensor, Lambda: torch.Tensor, B
                                     C: torch.Tensor, S: torch.Tensor, D: torch.Tensor,
                                     group=None, time_chunks: int | str = "auto",
                                     scan_fn: Callable | None = None,
-                                    segments: int = 1) -> torch.Tensor:
+                                    segments: int = 1, gather: str = "nccl") -> torch.Tensor:
     """Scan this rank's channel shard and all-gather y over ``group``.
 
     delta [B,T,Dl], Lambda [Dl,N,4], S [B,T,Dl] or [B,T,Dl,4], D [Dl] are this
@@ -71,6 +188,16 @@ def ssm_scan_cayley_channel_sharded(delta: torch.Tensor, Lambda: torch.Tensor, B
 
     ``scan_fn(delta, Lambda, B, C, S, D, h0) -> (y, h_T)`` replaces the local
     scan (default: ``ssm_scan_cayley`` with ``time_chunks``).
+
+    ``gather="peer"`` (CUDA, ranks on one node): instead of the collective
+    library's all-gather and a permute of its rank-major result, every rank
+    pushes each scanned segment straight into its channel columns of every
+    rank's output buffer over NVLink (``mqc_channel_push`` into
+    ``PeerOutput`` buffers), on a side stream under the next segment's scan. Two
+    one-element all-reduces on the compute stream order the exchange: one on
+    entry (every rank is done with the previous result before it is
+    overwritten) and one on exit (every push has landed). The returned tensor is
+    this rank's peer buffer, valid until the next call with the same shape.
     """
     if scan_fn is None:
         from .ssm_fused import ssm_scan_cayley
@@ -87,6 +214,12 @@ def ssm_scan_cayley_channel_sharded(delta: torch.Tensor, Lambda: torch.Tensor, B
         raise ValueError(f"seq_len {seqlen} does not split into {segments} equal segments")
     seg = seqlen // segments
     on_cuda = delta.is_cuda
+    if gather == "peer":
+        if not on_cuda:
+            raise ValueError("gather='peer' needs CUDA tensors")
+        return _channel_sharded_peer(delta, Lambda, B, C, S, D, group, scan_fn, segments)
+    if gather != "nccl":
+        raise ValueError(f"gather must be 'nccl' or 'peer', got {gather!r}")
     y = torch.empty((bsz, seqlen, world * dl, 4), dtype=delta.dtype, device=delta.device)
     # ranks' outputs concatenated along dim 0 (the form every backend accepts),
     # double-buffered across segments
@@ -121,6 +254,44 @@ def ssm_scan_cayley_channel_sharded(delta: torch.Tensor, Lambda: torch.Tensor, B
             b.record_stream(comm)
         compute.wait_stream(comm)
     return y
+
+
+def _channel_sharded_peer(delta, Lambda, B, C, S, D, group, scan_fn, segments):
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    bsz, seqlen, dl = delta.shape[:3]
+    seg = seqlen // segments
+    dev = delta.device
+    out = _peer_output((bsz, seqlen, world * dl, 4), delta.dtype, dev, group)
+    flag = _barrier_flag(dev)
+    compute = torch.cuda.current_stream(dev)
+    comm = _side_stream(dev)
+    dist.all_reduce(flag, group=group)  # every rank is done with the previous result
+    comm.wait_stream(compute)
+    h = None
+    for k in range(segments):
+        sl = slice(k * seg, (k + 1) * seg)
+        yk, h = scan_fn(delta[:, sl], Lambda, B[:, sl], C[:, sl], S[:, sl], D, h)
+        yk = yk.contiguous()
+        done = torch.cuda.Event()
+        done.record(compute)
+        comm.wait_event(done)
+        channel_push(yk, out.ptrs, seqlen, world * dl, rank * dl, k * seg, stream=comm)
+        yk.record_stream(comm)
+    compute.wait_stream(comm)
+    dist.all_reduce(flag, group=group)  # every rank's pushes have completed
+    return out.tensor
+
+
+_flags: dict[int, torch.Tensor] = {}
+
+
+def _barrier_flag(device: torch.device) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    f = _flags.get(idx)
+    if f is None:
+        f = _flags[idx] = torch.zeros(1, device=device)
+    return f
 
 
 def ssm_scan_cayley_time_sharded(delta: torch.Tensor, Lambda: torch.Tensor, B: torch.Tensor,

@@ -1,0 +1,97 @@
+"""The peer-memory exchange of the channel-sharded scan.
+
+* ``mqc_channel_push`` on one GPU, with several local buffers standing in for
+  the ranks' outputs: every destination must hold every rank's channel shard in
+  the final [B, T, D, 4] layout (bit-exact copy), for fp32 and bf16, and for a
+  shard width whose rows are not whole 16-byte pieces (8-byte path).
+* On two GPUs (skipped with fewer): two NCCL ranks run the channel-sharded scan
+  with ``gather="peer"`` (IPC buffers, pushes over NVLink) and ``gather="nccl"``;
+  the results must be equal bit for bit and match the unsharded scan.
+"""
+
+import os
+import socket
+
+import pytest
+import torch
+
+from tests.gpu_util import DEV, gen, make_scan_inputs, rel_l2, to_dev
+
+pytestmark = pytest.mark.gpu
+
+from mambaqc_b200.kernels.sharded import channel_push  # noqa: E402
+
+
+@pytest.mark.parametrize("dtype,dl", [(torch.float32, 6), (torch.bfloat16, 6),
+                                      (torch.bfloat16, 3)])
+def test_channel_push_emulated_ranks(dtype, dl):
+    world, bsz, seqlen, segs = 3, 2, 48, 4
+    seg = seqlen // segs
+    g = gen(1)
+    full = torch.randn(bsz, seqlen, world * dl, 4, generator=g).to(DEV, dtype)
+    outs = [torch.full_like(full, float("nan")) for _ in range(world)]
+    ptrs = [o.data_ptr() for o in outs]
+    for r in range(world):
+        shard = full[:, :, r * dl:(r + 1) * dl]
+        for k in range(segs):
+            src = shard[:, k * seg:(k + 1) * seg].contiguous()
+            channel_push(src, ptrs, seqlen, world * dl, r * dl, k * seg)
+    torch.cuda.synchronize()
+    for o in outs:
+        assert torch.equal(o, full)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _two_rank_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    from mambaqc_b200.kernels import ssm_scan_cayley
+    from mambaqc_b200.kernels.sharded import (release_peer_outputs,
+                                              ssm_scan_cayley_channel_sharded)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device(f"cuda:{rank}")
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        inp = make_scan_inputs(1, 1024, 16, 16, shared=True, s_real=True, seed=7)
+        d = {k: v.to(dev, torch.bfloat16 if k not in ("Lambda", "D") else torch.float32)
+             for k, v in inp.items()}
+        dl = 16 // world
+        sh = {k: (v[..., rank * dl:(rank + 1) * dl] if k in ("delta", "S") else v)
+              for k, v in d.items()}
+        sh["Lambda"] = d["Lambda"][rank * dl:(rank + 1) * dl]
+        sh["D"] = d["D"][rank * dl:(rank + 1) * dl]
+        args = (sh["delta"], sh["Lambda"], sh["B"], sh["C"], sh["S"], sh["D"])
+        y_nccl = ssm_scan_cayley_channel_sharded(*args, time_chunks=4, segments=4).clone()
+        for _ in range(2):  # the second call reuses the cached peer buffers
+            y_peer = ssm_scan_cayley_channel_sharded(*args, time_chunks=4, segments=4,
+                                                     gather="peer").clone()
+        y_full = ssm_scan_cayley(d["delta"], d["Lambda"], d["B"], d["C"], d["S"], d["D"])
+        torch.cuda.synchronize()
+        q.put((rank, torch.equal(y_peer, y_nccl), rel_l2(y_peer.float(), y_full.float())))
+        release_peer_outputs()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_peer_gather_matches_nccl_gather_on_two_ranks():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_two_rank_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in procs)
+    res = sorted(q.get(timeout=10) for _ in range(2))
+    for rank, equal, err in res:
+        assert equal, f"rank {rank}: peer gather differs from the NCCL gather"
+        assert err < 5e-3, f"rank {rank}: rel-L2 vs unsharded scan {err}"
