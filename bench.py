@@ -65,6 +65,10 @@ def parse_args():
     ap.add_argument("--only", choices=["fwd_bwd", "perchannel", "perchannel_fwd_bwd"],
                     default=None,
                     help="run only this sub-measurement and print it (profiling aid)")
+    ap.add_argument("--prof-batch", type=int, default=None,
+                    help="--only perchannel_fwd_bwd: batch rows (a small case for profilers)")
+    ap.add_argument("--prof-seq", type=int, default=None,
+                    help="--only perchannel_fwd_bwd: sequence length (a small case for profilers)")
     ap.add_argument("--segments", type=int, default=4,
                     help="config5 on >1 GPU: time segments whose all-gather overlaps the "
                          "scan of the next segment")
@@ -103,17 +107,20 @@ def barrier(world):
         dist.barrier()
 
 
-def make_inputs(dev, dtype, layout, seed):
+def make_inputs(dev, dtype, layout, seed, batch=None, seq=None):
+    """Config-3 inputs (batch/seq override the config's 4 x 2048, for the small
+    cases that profiler captures use)."""
+    BATCH_, SEQ_ = batch or BATCH, seq or SEQ
     g = torch.Generator(device=dev).manual_seed(seed)
     f32 = torch.float32
-    x = torch.randn(BATCH, SEQ, CHANNELS, generator=g, device=dev, dtype=f32)
+    x = torch.randn(BATCH_, SEQ_, CHANNELS, generator=g, device=dev, dtype=f32)
     delta = torch.nn.functional.softplus(
-        torch.randn(BATCH, SEQ, CHANNELS, generator=g, device=dev, dtype=f32) - 3.0)
+        torch.randn(BATCH_, SEQ_, CHANNELS, generator=g, device=dev, dtype=f32) - 3.0)
     lam = torch.empty(CHANNELS, STATE, 4, device=dev, dtype=f32)
     u = torch.rand(CHANNELS, STATE, generator=g, device=dev, dtype=f32)
     lam[..., 0] = -torch.exp(u * (math.log(1e-1) - math.log(1e-3)) + math.log(1e-3))
     lam[..., 1:] = 0.5 * torch.randn(CHANNELS, STATE, 3, generator=g, device=dev, dtype=f32)
-    bc_shape = (BATCH, SEQ, STATE, 4) if layout == "shared" else (BATCH, SEQ, CHANNELS, STATE, 4)
+    bc_shape = (BATCH_, SEQ_, STATE, 4) if layout == "shared" else (BATCH_, SEQ_, CHANNELS, STATE, 4)
     Bm = torch.randn(*bc_shape, generator=g, device=dev, dtype=f32) / math.sqrt(STATE)
     Cm = torch.randn(*bc_shape, generator=g, device=dev, dtype=f32) / math.sqrt(STATE)
     Dk = torch.ones(CHANNELS, device=dev, dtype=f32)
@@ -384,7 +391,8 @@ def run_b200(args, world, rank, local):
             res = run_fwd_bwd(args, inp, dev, world, stream, ssm_scan_cayley)
         elif args.only == "perchannel_fwd_bwd":
             res = run_perchannel_fwd_bwd(args, dev, world, stream, ssm_scan_cayley,
-                                         measured_peaks()[0], args.dtype)
+                                         measured_peaks()[0], args.dtype, args.prof_batch,
+                                         args.prof_seq)
         else:
             res = run_perchannel(args, dev, world, stream, ssm_scan_cayley, measured_peaks()[0])
         if rank == 0:
@@ -516,26 +524,56 @@ def run_e2e(args, inp, dev, world, stream, op):
                     "y -> pinned host (third stream)"}
 
 
+# Algorithmic FLOPs per (b, t, d, n) element of the scan backward with a real
+# signal: lambda = conj(C) (x) dy + carry 32, carry = conj(q) (x) lambda 28,
+# dq = lambda (x) conj(h_prev) 28, the Cayley map 15 and its vector-Jacobian
+# product 42, ddelta <dz, Lambda> 7, dLambda += delta dz 8, dB = x lambda 4,
+# dx <B, lambda> 7, dC = dy (x) conj(h) 28. The recomputation of the states
+# from the forward's checkpoints (36 more) is not counted.
+BWD_FLOPS_PER_ELEM_SREAL = 199
+
+
 def run_fwd_bwd(args, inp, dev, world, stream, op):
     """Forward + backward of the fused scan (config 3 names both): one step = the
-    forward with checkpoints plus the backward for a fixed upstream gradient."""
+    forward with checkpoints plus the backward for a fixed upstream gradient.
+    The backward alone is timed with CUDA events around the autograd backward and
+    reported against the FP32 FMA peak (channel-shared B/C: FP32-bound)."""
     leaves = {k: (v.detach().requires_grad_() if k != "D" else v) for k, v in inp.items()}
     gy = torch.randn(BATCH, SEQ, CHANNELS, 4, device=dev, dtype=inp["delta"].dtype)
+    bwd = []
 
     def step():
         for v in leaves.values():
             v.grad = None
         y = op(leaves["delta"], leaves["Lambda"], leaves["B"], leaves["C"], leaves["x"],
                leaves["D"])
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
         y.backward(gy)
+        e1.record(stream)
+        bwd.append((e0, e1))
 
     steps = max(3, min(args.steps, 10))
     ms = timed(step, steps, max(3, min(args.warmup, 3)), world, stream) / steps
+    torch.cuda.synchronize()
+    ms_bwd = sum(a.elapsed_time(b) for a, b in bwd[-steps:]) / steps
     ms = max_over_ranks(ms, world, dev)
+    ms_bwd = max_over_ranks(ms_bwd, world, dev)
+    flops = BATCH * SEQ * CHANNELS * STATE * BWD_FLOPS_PER_ELEM_SREAL
+    peak = fp32_peak_tflops(dev)
     # kernels per step: scan forward, scan backward, plus torch's zero-fill of the
     # shared dB/dC accumulators, the casts and the sums over batch
     return {"value": BATCH * SEQ * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
-            "steps": steps, "what": "scan forward (with checkpoints) + backward, fp32"}
+            "backward_ms": ms_bwd, "steps": steps,
+            "what": "scan forward (with checkpoints) + backward, "
+                    + ("fp32" if inp["delta"].dtype == torch.float32 else "bf16 inputs"),
+            "roofline": {"bound": "fp32", "kernel": "ssm_scan_bwd_packed_kernel (the backward)",
+                         "achieved": flops / (ms_bwd / 1e3) / 1e12, "peak": peak,
+                         "unit": "TFLOP/s", "frac": flops / (ms_bwd / 1e3) / 1e12 / peak,
+                         "algorithmic_flops_per_launch": flops,
+                         "flops_per_element": BWD_FLOPS_PER_ELEM_SREAL,
+                         "peak_source": "FP32 FMA probe run by bench.py"}}
 
 
 def perchannel_bwd_bytes(inp):
@@ -550,16 +588,18 @@ def perchannel_bwd_bytes(inp):
     return 4 * bc + 2 * per_tc + 2 * per_tc + per_tc * 4 + lam + BATCH * lam
 
 
-def run_perchannel_fwd_bwd(args, dev, world, stream, op, peaks, dtype_name):
+def run_perchannel_fwd_bwd(args, dev, world, stream, op, peaks, dtype_name, batch=None,
+                           seq=None):
     """Forward (with the backward's state checkpoints) + backward of the scan in
     the reference block's per-channel B/C layout [4,2048,1536,64,4], the config-4
     training case. HBM-bound: B, C, dB and dC each cross HBM once in the
     backward. Reports the step and the backward alone (CUDA events around the
     autograd backward on the launching stream), each against the measured HBM
     bandwidth."""
-    inp = make_inputs(dev, dtype_name, "perchannel", seed=2468)
+    bsz, seqlen = batch or BATCH, seq or SEQ
+    inp = make_inputs(dev, dtype_name, "perchannel", seed=2468, batch=bsz, seq=seqlen)
     leaves = {k: v.detach().requires_grad_() for k, v in inp.items()}
-    gy = torch.randn(BATCH, SEQ, CHANNELS, 4, device=dev).to(inp["delta"].dtype)
+    gy = torch.randn(bsz, seqlen, CHANNELS, 4, device=dev).to(inp["delta"].dtype)
     bwd_ms = []
 
     def step(record=False):
@@ -589,8 +629,8 @@ def run_perchannel_fwd_bwd(args, dev, world, stream, op, peaks, dtype_name):
     ms_max = max_over_ranks(ms, world, dev)
     ms_bwd_max = max_over_ranks(ms_bwd, world, dev)
     res = {
-        "value": BATCH * SEQ * world / (ms_max / 1e3), "unit": "tokens/s", "ms_per_step": ms_max,
-        "backward_ms": ms_bwd_max, "steps": steps,
+        "value": bsz * seqlen * world / (ms_max / 1e3), "unit": "tokens/s", "ms_per_step": ms_max,
+        "backward_ms": ms_bwd_max, "steps": steps, "batch": bsz, "seq_len": seqlen,
         "dtype": "bf16 inputs, f32 state" if dtype_name == "bf16" else "f32",
         "what": "per-channel B/C scan forward (with checkpoints) + backward",
         "roofline": {"bound": "hbm", "kernel": "ssm_scan_bwd_pc_kernel (the backward)",
@@ -669,7 +709,8 @@ def config5_measure(args, world, rank, local, gather="peer"):
     lam[..., 1:] = 0.5 * torch.randn(dl, STATE, 3, generator=g, device=dev)
     Dk = torch.ones(dl, device=dev)
     nc = auto_time_chunks(1, C5_SEQ, dl, STATE, dev)
-    segs = args.segments if world > 1 else 1
+    # the fused peer exchange runs in the scan kernel itself (one call, no segments)
+    segs = args.segments if (world > 1 and gather == "nccl") else 1
     stream = torch.cuda.current_stream(dev)
     out = {}
 
@@ -692,9 +733,11 @@ def config5_measure(args, world, rank, local, gather="peer"):
         ms_scan_max = max_over_ranks(ms_scan, world, dev)
     del out
     elems = C5_SEQ * CHANNELS * STATE
-    how = ("peer-memory push of every scanned segment into all ranks' outputs over NVLink "
-           "(mqc_channel_push), ordered by two 1-element NCCL all-reduces" if gather == "peer"
-           else "NCCL all_gather_into_tensor of y per time segment plus a permute")
+    how = ("every y value stored by the scan kernel into all ranks' outputs over NVLink "
+           "(mqc_ssm_scan_fwd_chunked_peer, CUDA IPC buffers), ordered by two 1-element NCCL "
+           "all-reduces" if gather == "peer"
+           else "NCCL all_gather_into_tensor of y per time segment plus a permute, overlapped "
+                "with the scan of the next segment")
     return {
         "value": C5_SEQ / (ms_max / 1e3), "unit": "tokens/s", "ms_per_step": ms_max,
         "steps": steps, "scaling": "strong", "n_gpus": world,
@@ -703,8 +746,7 @@ def config5_measure(args, world, rank, local, gather="peer"):
                    "d_inner": CHANNELS, "d_state": STATE, "channels_per_gpu": dl,
                    "time_chunks": nc, "segments": segs,
                    "parallelism": f"channel shards x{world}" + (
-                       f", y exchange: {how}, overlapped with the scan of the next segment"
-                       if world > 1 else "")},
+                       f", y exchange: {how}" if world > 1 else "")},
         "scan_only_ms": ms_scan_max,
         "exchange_exposed_ms": ms_max - ms_scan_max,
         "scan_fp32_tflops_per_gpu": elems / world * FLOPS_PER_ELEM_SREAL / (ms_scan_max / 1e3) / 1e12,

@@ -261,6 +261,21 @@ MQC_API int mqc_peer_free(void* ptr);
 MQC_API int mqc_peer_open(const void* handle, void** ptr);
 MQC_API int mqc_peer_close(void* ptr);
 
+/* mqc_ssm_scan_fwd_chunked for one channel shard of a sequence split over the
+ * ranks by channel, with the exchange of y fused into the scan: the kernel that
+ * produces y stores every value into each of the npeer (<= 8) outputs
+ * ypeer[r] [batch, seq_len, ch_total, 4] (dtype; this GPU's and the other
+ * ranks' buffers from mqc_peer_alloc / mqc_peer_open) at channels ch_off ..
+ * ch_off + channels - 1, so y crosses NVLink while the scan runs and lands in
+ * its final layout. args->y is ignored. Channel-shared B/C, the fused Cayley
+ * form, a per-channel skip weight, seq_len / nchunks > 8. The kernel ends with
+ * a system-scope fence; ranks that synchronise with its completion (e.g. a
+ * collective ordered after it) see the data. */
+MQC_API int mqc_ssm_scan_fwd_chunked_peer(const mqc_ssm_scan_args* args, int64_t nchunks,
+                                          void* workspace, size_t workspace_bytes,
+                                          void* const* ypeer, int npeer, int64_t ch_total,
+                                          int64_t ch_off, void* stream);
+
 /* Copies a time segment of this rank's channel shard, src [batch, seg_len,
  * ch_local, 4] (dtype, contiguous), into rows t_off .. t_off+seg_len-1 and
  * channels ch_off .. ch_off+ch_local-1 of each of the ndst (<= 8) outputs
@@ -340,6 +355,23 @@ MQC_API int mqc_ssm_step(const void* q, const void* Bm, const void* S, const voi
 MQC_API int mqc_qln_fwd(const void* q, const float* gamma, const float* beta, void* out, float* mean,
                 float* rstd, int64_t rows, int64_t d_model, float eps, int flags, int dtype,
                 void* stream);
+
+/* LayerNorm fused into the output projection that follows it in the block:
+ *   out[r, :] = LN(q)[r, :] @ weight^T (+ bias)
+ * with LN as mqc_qln_fwd (exact form). q [rows, d_model, 4], weight
+ * [out_features, 4 d_model], bias [out_features] or NULL, out [rows,
+ * out_features]: bf16; gamma [d_model], beta [d_model, 4] fp32; mean, rstd
+ * [rows] fp32 receive the row statistics (for the backward). The normalised
+ * activations are never written: one pass reads q for the row statistics, then
+ * a tcgen05 GEMM normalises each q tile in shared memory as its operand.
+ * d_model a multiple of 16 (<= 4096); q, weight, beta 16-byte aligned. `status`
+ * (device int, may be NULL) receives MQC_DEVICE_STATUS_TIMEOUT if a bounded
+ * wait gives up. Replaces self.out_proj(self.norm(y_quat)),
+ * models/quaternion_mamba2_block.py:154-157. */
+MQC_API int mqc_qln_linear_fwd(const void* q, const float* gamma, const float* beta,
+                               const void* weight, const void* bias, void* out, float* mean,
+                               float* rstd, int64_t rows, int64_t d_model, int64_t out_features,
+                               float eps, int* status, void* stream);
 
 /* Bytes of workspace mqc_qln_bwd needs for `rows` x `d_model` (0 if nothing to do). */
 MQC_API size_t mqc_qln_bwd_workspace_size(int64_t rows, int64_t d_model);

@@ -119,6 +119,11 @@ _SIGNATURES.update({
     "mqc_peer_free": [_c_void_p],
     "mqc_peer_open": [_c_void_p, ctypes.POINTER(_c_void_p)],
     "mqc_peer_close": [_c_void_p],
+    "mqc_ssm_scan_fwd_chunked_peer": [ctypes.POINTER(SsmScanArgs), _i64, _c_void_p,
+                                      ctypes.c_size_t, ctypes.POINTER(_c_void_p), _i32, _i64,
+                                      _i64, _c_void_p],
+    "mqc_qln_linear_fwd": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                           _c_void_p, _c_void_p, _i64, _i64, _i64, _f32, _c_void_p, _c_void_p],
     "mqc_channel_push": [_c_void_p, ctypes.POINTER(_c_void_p), _i32, _i64, _i64, _i64, _i64,
                          _i64, _i64, _i64, _i32, _c_void_p],
 })

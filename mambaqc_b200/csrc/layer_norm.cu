@@ -91,6 +91,7 @@ __global__ void __launch_bounds__(kMaxRowThreads) qln_fwd_kernel(
     if (mean_out) mean_out[row] = mu;
     if (rstd_out) rstd_out[row] = rsd;
   }
+  if (out == nullptr) return;  // row statistics only (qln_row_stats)
   // one reciprocal per quaternion (and one per row) instead of a division per
   // component: out = gamma * nh * q / (n + eps) + beta
 #pragma unroll
@@ -290,6 +291,43 @@ extern "C" int mqc_qln_fwd(const void* q, const float* gamma, const float* beta,
   }
   return check_launch("mqc_qln_fwd");
 }
+
+namespace mqc {
+
+// Mean and 1/std of the quaternion norms of every row: the first half of
+// mqc_qln_fwd (same kernel, same arithmetic, so the statistics are bit for bit
+// those the LayerNorm itself uses), without writing the normalised row.
+int qln_row_stats(const void* q, float* mean, float* rstd, int64_t rows, int64_t d_model,
+                  float eps, int dtype, cudaStream_t st) {
+  MQC_REQUIRE(d_model >= 1 && d_model <= int64_t(kMaxRowThreads) * kVpt && rows <= 0x7fffffff,
+              MQC_ERR_UNSUPPORTED, "qln_row_stats: d_model=%lld", (long long)d_model);
+  const int D = int(d_model);
+  int threads = (D + kVpt - 1) / kVpt;
+  threads = (threads + 31) / 32 * 32;
+  if (threads < 32) threads = 32;
+  const size_t srow_bytes = size_t(D) * 4 * (dtype == MQC_DTYPE_F32 ? 4 : 2);
+  if (srow_bytes > 48 * 1024) {
+    cudaError_t e = dtype == MQC_DTYPE_F32
+                        ? cudaFuncSetAttribute(qln_fwd_kernel<float>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               int(srow_bytes))
+                        : cudaFuncSetAttribute(qln_fwd_kernel<__nv_bfloat16>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               int(srow_bytes));
+    if (e != cudaSuccess)
+      return fail(MQC_ERR_CUDA, "qln_row_stats: smem attribute: %s", cudaGetErrorString(e));
+  }
+  if (rows == 0) return MQC_OK;
+  if (dtype == MQC_DTYPE_F32)
+    qln_fwd_kernel<float><<<unsigned(rows), threads, srow_bytes, st>>>(
+        static_cast<const float*>(q), nullptr, nullptr, nullptr, mean, rstd, D, eps, 0);
+  else
+    qln_fwd_kernel<__nv_bfloat16><<<unsigned(rows), threads, srow_bytes, st>>>(
+        static_cast<const __nv_bfloat16*>(q), nullptr, nullptr, nullptr, mean, rstd, D, eps, 0);
+  return check_launch("qln_row_stats");
+}
+
+}  // namespace mqc
 
 extern "C" size_t mqc_qln_bwd_workspace_size(int64_t rows, int64_t d_model) {
   if (rows <= 0 || d_model <= 0) return 0;

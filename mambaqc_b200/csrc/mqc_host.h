@@ -29,6 +29,11 @@ constexpr uint64_t kScratchKeepBytes = uint64_t(8) << 30;
 cudaError_t scratch_alloc(void** p, size_t bytes, cudaStream_t st);
 cudaError_t scratch_free(void* p, cudaStream_t st);
 
+// Row statistics of the quaternion LayerNorm (layer_norm.cu): mean and 1/std of
+// the norms of each row, exactly as mqc_qln_fwd computes them.
+int qln_row_stats(const void* q, float* mean, float* rstd, int64_t rows, int64_t d_model,
+                  float eps, int dtype, cudaStream_t st);
+
 inline bool aligned(const void* p, uintptr_t a) {
   return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
 }

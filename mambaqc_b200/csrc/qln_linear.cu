@@ -1,0 +1,410 @@
+// Quaternion LayerNorm fused into the operand load of the output projection:
+//   out[m, :] = LN(y)[m, :] @ W^T (+ bias),  y [M, Dq, 4], W [N, 4 Dq], bf16.
+//
+// The reference block runs `self.out_proj(self.norm(y_quat))`
+// (mambaqc/models/quaternion_mamba2_block.py:154-157): the LayerNorm writes
+// the normalised activations (M x 4Dq, the widest tensor after the scan) and
+// the projection reads them back. Here the LayerNorm is the prologue of a
+// hand-written sm_100a GEMM and its output never reaches global memory:
+//   1. qln_row_stats (layer_norm.cu) reads y once and writes the mean and
+//      1/std of the quaternion norms of every row (8 bytes per row);
+//   2. the GEMM streams raw y tiles into shared memory with TMA, normalises
+//      them in place (per quaternion: n = sqrt(|q|^2 + eps),
+//      out = gamma * (n - mean) * rstd * q / (n + eps) + beta, the same
+//      operations as qln_fwd_kernel, so the bf16 operand is bit for bit the
+//      LayerNorm's output), and feeds them to tcgen05.mma with the fp32
+//      accumulator in tensor memory.
+//
+// One CTA computes a BM x BN = 128 x 256 tile of out, walking K in BK = 64
+// blocks through a kStages-deep shared-memory ring. Warp roles:
+//   warp 0      TMA producer (one thread): raw y tile + W tile per stage;
+//   warp 1      tensor-memory allocation and the MMA issuer (one thread);
+//   warps 2..9  transform each landed y tile in place (a row per thread
+//               pair), fence it for the tensor core, signal the MMA issuer;
+//               after the last K block, the epilogue (tcgen05.ld -> bf16 ->
+//               global).
+// Every mbarrier wait is bounded: on timeout the CTA raises its abort flag and
+// the status word, stops issuing work, lets what was issued finish (bounded),
+// frees its tensor memory and returns. Plain TMA loads only (no multicast);
+// every tensor map covers this GPU's memory.
+#include <cuda.h>
+
+#include <mutex>
+
+#include "mqc_common.cuh"
+#include "mqc_host.h"
+
+namespace mqc {
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int kStages = 4;
+constexpr int kXformWarps = 8;
+constexpr int kThreads = 32 * (2 + kXformWarps);
+constexpr uint32_t kABytes = BM * BK * 2;  // 16 KB
+constexpr uint32_t kBBytes = BN * BK * 2;  // 32 KB
+constexpr uint32_t kStageBytes = kABytes + kBBytes;
+constexpr uint32_t kTmemCols = 256;        // fp32 accumulator 128 lanes x 256 columns
+constexpr long long kPollLimit = 1ll << 26;
+
+struct SmemCtl {
+  uint64_t full[kStages], ready[kStages], empty[kStages], accum;
+  uint32_t tmem_base;
+  int abort;
+  float mean[BM], rstd[BM];
+};
+constexpr size_t kSmemBytes = 1024 + size_t(kStages) * kStageBytes + sizeof(SmemCtl);
+
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
+                                              volatile int* abort_flag, int* status) {
+  for (long long i = 0; i < kPollLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 1023) == 1023 && *abort_flag) return false;
+  }
+  *abort_flag = 1;
+  report_status(status, MQC_DEVICE_STATUS_TIMEOUT);
+  return false;
+}
+
+__device__ __forceinline__ void mbar_arrive_plain(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major tile with the 128-byte swizzle
+// (rows of 64 bf16 = 128 bytes, 8-row atoms 1024 bytes apart): start address,
+// leading byte offset 16 (unused by this layout), stride byte offset 1024,
+// descriptor version 1, layout type 2 (128-byte swizzle).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return uint64_t((saddr >> 4) & 0x3FFF) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
+         (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+
+// Instruction descriptor of tcgen05.mma kind::f16: fp32 accumulator, bf16 A
+// and B, both K-major, M = BM, N = BN.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) |
+                            (uint32_t(BM >> 4) << 24);
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 32 consecutive fp32 accumulator columns of this thread's tensor-memory lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// The LayerNorm of one bf16 quaternion, as qln_fwd_kernel computes it.
+__device__ __forceinline__ float4 qln_point(float4 v, float mu, float rsd, float gm, float4 bt,
+                                            float eps) {
+  const float nrm = sqrtf(fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, v.w * v.w))) + eps);
+  const float nh = (nrm - mu) * rsd;
+  const float g = gm * nh * (1.f / (nrm + eps));
+  return make_float4(fmaf(g, v.x, bt.x), fmaf(g, v.y, bt.y), fmaf(g, v.z, bt.z),
+                     fmaf(g, v.w, bt.w));
+}
+
+struct QlnLinParams {
+  const float* mean;
+  const float* rstd;
+  const float* gamma;
+  const float* beta;
+  const __nv_bfloat16* bias;
+  __nv_bfloat16* out;
+  int M, N, K;  // K = 4 * Dq
+  float eps;
+  int* status;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    qln_linear_kernel(const __grid_constant__ CUtensorMap tmY,
+                      const __grid_constant__ CUtensorMap tmW, const QlnLinParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // 1024-byte aligned stage ring (the 128-byte swizzle atoms), control block after it
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  SmemCtl* ctl = reinterpret_cast<SmemCtl*>(base + size_t(kStages) * kStageBytes);
+  volatile int* abort_flag = &ctl->abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  const int nkb = p.K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&ctl->full[s], 1);
+      mbar_init(&ctl->ready[s], 32 * kXformWarps);
+      mbar_init(&ctl->empty[s], 1);
+    }
+    mbar_init(&ctl->accum, 1);
+    ctl->abort = 0;
+    fence_mbar_init();
+  }
+  if (threadIdx.x < BM) {
+    const int m = m0 + threadIdx.x;
+    ctl->mean[threadIdx.x] = m < p.M ? p.mean[m] : 0.f;
+    ctl->rstd[threadIdx.x] = m < p.M ? p.rstd[m] : 0.f;
+  }
+  if (warp == 1) {  // tensor memory for the accumulator (whole warp)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(&ctl->tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % kStages;
+        if (kb >= kStages &&
+            !wait_or_abort(&ctl->empty[s], uint32_t(((kb / kStages) - 1) & 1), abort_flag,
+                           p.status))
+          break;
+        if (*abort_flag) break;
+        unsigned char* st = base + size_t(s) * kStageBytes;
+        mbar_arrive_expect_tx(&ctl->full[s], kStageBytes);
+        tma_load_2d(st, &tmY, kb * BK, m0, &ctl->full[s]);
+        tma_load_2d(st + kABytes, &tmW, kb * BK, n0, &ctl->full[s]);
+        issued = kb + 1;
+      }
+      // the CTA must outlive its copies: wait (bounded) for the last ones issued
+      for (int kb = issued > kStages ? issued - kStages : 0; kb < issued; ++kb)
+        mbar_wait_bounded(&ctl->full[kb % kStages], uint32_t((kb / kStages) & 1), kDrainPollLimit);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % kStages;
+        if (!wait_or_abort(&ctl->ready[s], uint32_t((kb / kStages) & 1), abort_flag, p.status))
+          break;
+        tc_fence_after();
+        const uint32_t sa = smem_addr(base + size_t(s) * kStageBytes);
+        const uint32_t sb = sa + kABytes;
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k)  // 16 bf16 = 32 bytes per MMA along K
+          mma_bf16(tmem, sw128_desc(sa + 32 * k), sw128_desc(sb + 32 * k),
+                   (kb > 0 || k > 0) ? 1u : 0u);
+        mma_commit(&ctl->empty[s]);  // frees the stage once these MMAs have read it
+        issued = kb + 1;
+      }
+      if (issued == nkb) {
+        mma_commit(&ctl->accum);
+      } else if (issued > 0) {
+        // aborted: wait (bounded) until the MMAs already issued are done
+        const int kb = issued - 1;
+        mbar_wait_bounded(&ctl->empty[kb % kStages], uint32_t((kb / kStages) & 1),
+                          kDrainPollLimit);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ transform
+    const int xt = threadIdx.x - 64;  // 0 .. 255
+    const int r = xt >> 1;            // tile row
+    const int c_lo = (xt & 1) * 4;    // first of this thread's 4 16-byte chunks
+    const float mu = ctl->mean[r], rsd = ctl->rstd[r];
+    bool ok = true;
+    for (int kb = 0; kb < nkb && ok; ++kb) {
+      const int s = kb % kStages;
+      ok = wait_or_abort(&ctl->full[s], uint32_t((kb / kStages) & 1), abort_flag, p.status);
+      if (!ok) break;
+      unsigned char* rowp = base + size_t(s) * kStageBytes + r * 128;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int c = c_lo + j;                           // logical 16-byte chunk of the row
+        uint4* cp = reinterpret_cast<uint4*>(rowp + ((c ^ (r & 7)) << 4));
+        const uint4 raw = *cp;
+        const int d0 = kb * (BK / 4) + 2 * c;             // quaternion index of the chunk
+        const float4 q0 = QIO<__nv_bfloat16>::unpack(make_uint2(raw.x, raw.y));
+        const float4 q1 = QIO<__nv_bfloat16>::unpack(make_uint2(raw.z, raw.w));
+        const float4 o0 = qln_point(q0, mu, rsd, __ldg(p.gamma + d0),
+                                    QIO<float>::ld(p.beta + d0 * 4), p.eps);
+        const float4 o1 = qln_point(q1, mu, rsd, __ldg(p.gamma + d0 + 1),
+                                    QIO<float>::ld(p.beta + (d0 + 1) * 4), p.eps);
+        *cp = make_uint4(pack_bf16x2(o0.x, o0.y), pack_bf16x2(o0.z, o0.w),
+                         pack_bf16x2(o1.x, o1.y), pack_bf16x2(o1.z, o1.w));
+      }
+      fence_async_smem();  // generic-proxy writes -> visible to the tensor core
+      mbar_arrive_plain(&ctl->ready[s]);
+    }
+    // ------------------------------------------------------------ epilogue
+    // (tcgen05.ld is warp-collective: the whole warp takes the same branch)
+    bool go = ok && wait_or_abort(&ctl->accum, 0u, abort_flag, p.status);
+    go = __all_sync(0xffffffffu, go);
+    if (go) {
+      tc_fence_after();
+      const int ew = warp - 2;        // 0 .. 7
+      const int quarter = warp & 3;   // tensor-memory lanes 32*quarter .. +31
+      const int half = ew >> 2;       // columns 128*half .. +127
+      const int row = quarter * 32 + lane;
+      const int m = m0 + row;
+#pragma unroll 1
+      for (int cb = 0; cb < 4; ++cb) {
+        const int col0 = half * 128 + cb * 32;
+        float v[32];
+        tmem_ld32(tmem + (uint32_t(quarter * 32) << 16) + uint32_t(col0), v);
+        const int n = n0 + col0;
+        if (m < p.M) {
+          if (p.bias != nullptr) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (n + i < p.N) v[i] += __bfloat162float(p.bias[n + i]);
+          }
+          __nv_bfloat16* dst = p.out + int64_t(m) * p.N + n;
+          if (n + 32 <= p.N && (p.N & 7) == 0) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8)
+              *reinterpret_cast<uint4*>(dst + i) =
+                  make_uint4(pack_bf16x2(v[i], v[i + 1]), pack_bf16x2(v[i + 2], v[i + 3]),
+                             pack_bf16x2(v[i + 4], v[i + 5]), pack_bf16x2(v[i + 6], v[i + 7]));
+          } else {
+            for (int i = 0; i < 32 && n + i < p.N; ++i) dst[i] = __float2bfloat16_rn(v[i]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against the driver library).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+std::mutex g_encode_mutex;
+EncodeTiledFn g_encode = nullptr;
+
+int make_map_2d(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols, uint32_t box_rows,
+                uint32_t box_cols) {
+  {
+    std::lock_guard<std::mutex> lock(g_encode_mutex);
+    if (g_encode == nullptr) {
+      void* f = nullptr;
+      cudaDriverEntryPointQueryResult q{};
+      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) !=
+              cudaSuccess ||
+          f == nullptr)
+        return fail(MQC_ERR_CUDA, "mqc_qln_linear_fwd: cuTensorMapEncodeTiled unavailable");
+      g_encode = reinterpret_cast<EncodeTiledFn>(f);
+    }
+  }
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr),
+                              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(MQC_ERR_CUDA, "mqc_qln_linear_fwd: cuTensorMapEncodeTiled failed (%d)", int(r));
+  return MQC_OK;
+}
+
+}  // namespace
+}  // namespace mqc
+
+using namespace mqc;
+
+extern "C" int mqc_qln_linear_fwd(const void* q, const float* gamma, const float* beta,
+                                  const void* weight, const void* bias, void* out, float* mean,
+                                  float* rstd, int64_t rows, int64_t d_model,
+                                  int64_t out_features, float eps, int* status, void* stream) {
+  clear_error();
+  const char* name = "mqc_qln_linear_fwd";
+  MQC_REQUIRE(rows >= 0 && d_model >= 0 && out_features >= 0, MQC_ERR_INVALID_VALUE,
+              "%s: negative size", name);
+  if (rows == 0 || out_features == 0) return MQC_OK;
+  MQC_REQUIRE(q && gamma && beta && weight && out && mean && rstd, MQC_ERR_INVALID_VALUE,
+              "%s: null pointer", name);
+  MQC_REQUIRE(d_model >= 16 && d_model % 16 == 0 && d_model <= 4096, MQC_ERR_UNSUPPORTED,
+              "%s: d_model must be a multiple of 16 in [16, 4096] (K = 4 d_model in blocks of %d)",
+              name, BK);
+  MQC_REQUIRE(rows <= 0x7fffffff && out_features <= 0x7fffffff, MQC_ERR_UNSUPPORTED,
+              "%s: size out of range", name);
+  MQC_REQUIRE(aligned(q, 16) && aligned(weight, 16) && aligned(beta, 16) && aligned(out, 2),
+              MQC_ERR_MISALIGNED, "%s: q, weight and beta must be 16-byte aligned", name);
+  cudaStream_t st = as_stream(stream);
+  int rc = qln_row_stats(q, mean, rstd, rows, d_model, eps, MQC_DTYPE_BF16, st);
+  if (rc != MQC_OK) return rc;
+  const int64_t K = 4 * d_model;
+  CUtensorMap tmY, tmW;
+  rc = make_map_2d(&tmY, q, uint64_t(rows), uint64_t(K), BM, BK);
+  if (rc == MQC_OK) rc = make_map_2d(&tmW, weight, uint64_t(out_features), uint64_t(K), BN, BK);
+  if (rc != MQC_OK) return rc;
+  cudaError_t e = cudaFuncSetAttribute(qln_linear_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(kSmemBytes));
+  if (e != cudaSuccess)
+    return fail(MQC_ERR_CUDA, "%s: smem attribute: %s", name, cudaGetErrorString(e));
+  QlnLinParams p{mean, rstd, gamma, beta, static_cast<const __nv_bfloat16*>(bias),
+                 static_cast<__nv_bfloat16*>(out), int(rows), int(out_features), int(K), eps,
+                 status};
+  dim3 grid{unsigned((out_features + BN - 1) / BN), unsigned((rows + BM - 1) / BM), 1u};
+  MQC_REQUIRE(grid.y <= 65535, MQC_ERR_UNSUPPORTED, "%s: too many rows", name);
+  qln_linear_kernel<<<grid, kThreads, kSmemBytes, st>>>(tmY, tmW, p);
+  return check_launch(name);
+}

@@ -93,11 +93,34 @@ using namespace mqc::scan;
 
 namespace {
 
+// Peer outputs of the channel-sharded scan (mqc_ssm_scan_fwd_chunked_peer).
+struct PeerSpec {
+  void* const* ptrs;
+  int n;
+  int64_t ch_total, ch_off;
+};
+
+// Pass 2 (or the whole scan when nchunks == 1): mqc_ssm_scan_fwd, or with peer
+// outputs the packed kernel writing y into every peer buffer.
+int scan_pass(const mqc_ssm_scan_args* a2, const PeerSpec* peer, void* stream) {
+  if (peer == nullptr) return mqc_ssm_scan_fwd(a2, stream);
+  FwdParams p{};
+  int rc = validate_and_fill(a2, &p, "mqc_ssm_scan_fwd_chunked_peer");
+  if (rc != MQC_OK || p.T == 0 || p.B == 0 || p.D == 0) return rc;
+  p.npeer = peer->n;
+  for (int r = 0; r < peer->n; ++r) p.ypeer[r] = peer->ptrs[r];
+  p.y_ld = peer->ch_total * 4;
+  p.y_coff = peer->ch_off * 4;
+  return dispatch_shared_packed(p, a2->dtype, (a2->flags & MQC_SSM_S_REAL) != 0,
+                                as_stream(stream));
+}
+
 // Carry (start state of every chunk from the chunk summaries P, hloc and h0, and
 // the final state) followed by pass 2: the regular scan of every chunk from its
 // start state, chunks folded into the batch.
 int carry_and_rescan(const mqc_ssm_scan_args* a, const FwdParams& p, int64_t nchunks,
-                     const float* Pbuf, const float* hloc, float* hin, void* stream) {
+                     const float* Pbuf, const float* hloc, float* hin, const PeerSpec* peer,
+                     void* stream) {
   const int64_t lanes = int64_t(p.D) * p.N;
   cudaStream_t st = as_stream(stream);
   dim3 grid{unsigned((lanes + kCarryThreads - 1) / kCarryThreads), unsigned(p.B), 1u};
@@ -110,8 +133,11 @@ int carry_and_rescan(const mqc_ssm_scan_args* a, const FwdParams& p, int64_t nch
   a2.seq_len = p.T / nchunks;
   a2.h0 = hin;
   a2.hT = nullptr;
-  return mqc_ssm_scan_fwd(&a2, stream);
+  return scan_pass(&a2, peer, stream);
 }
+
+int chunked_impl(const mqc_ssm_scan_args* a, int64_t nchunks, void* workspace,
+                 size_t workspace_bytes, const PeerSpec* peer, void* stream);
 
 }  // namespace
 
@@ -125,7 +151,46 @@ extern "C" int mqc_ssm_scan_fwd_chunked(const mqc_ssm_scan_args* a, int64_t nchu
                                         void* workspace, size_t workspace_bytes,
                                         void* stream) {
   clear_error();
-  const char* name = "mqc_ssm_scan_fwd_chunked";
+  return chunked_impl(a, nchunks, workspace, workspace_bytes, nullptr, stream);
+}
+
+extern "C" int mqc_ssm_scan_fwd_chunked_peer(const mqc_ssm_scan_args* a, int64_t nchunks,
+                                             void* workspace, size_t workspace_bytes,
+                                             void* const* ypeer, int npeer, int64_t ch_total,
+                                             int64_t ch_off, void* stream) {
+  clear_error();
+  const char* name = "mqc_ssm_scan_fwd_chunked_peer";
+  MQC_REQUIRE(a != nullptr && ypeer != nullptr, MQC_ERR_INVALID_VALUE, "%s: null pointer", name);
+  MQC_REQUIRE(npeer >= 1 && npeer <= kMaxPeerOutputs, MQC_ERR_INVALID_VALUE,
+              "%s: 1 to %d outputs, got %d", name, kMaxPeerOutputs, npeer);
+  MQC_REQUIRE((a->flags & MQC_SSM_BC_SHARED) && !(a->flags & MQC_SSM_Q_GIVEN), MQC_ERR_UNSUPPORTED,
+              "%s: channel-shared B/C and the fused Cayley form only", name);
+  const char* impl = getenv("MQC_SCAN_IMPL");
+  MQC_REQUIRE(impl == nullptr || impl[0] == '\0', MQC_ERR_UNSUPPORTED,
+              "%s: needs the packed kernel (MQC_SCAN_IMPL is set)", name);
+  MQC_REQUIRE(a->ckpt == nullptr && a->dskip_sb == 0 && a->dskip_st == 0, MQC_ERR_UNSUPPORTED,
+              "%s: no checkpoints, per-channel skip weight only", name);
+  MQC_REQUIRE(nchunks >= 1 && a->seq_len % nchunks == 0 && a->seq_len / nchunks > kShortScan,
+              MQC_ERR_UNSUPPORTED, "%s: seq_len / nchunks must be an integer above %d", name,
+              kShortScan);
+  MQC_REQUIRE(ch_off >= 0 && ch_off + a->channels <= ch_total, MQC_ERR_INVALID_VALUE,
+              "%s: channels [%lld, +%lld) outside %lld", name, (long long)ch_off,
+              (long long)a->channels, (long long)ch_total);
+  const uintptr_t qa = a->dtype == MQC_DTYPE_F32 ? 16 : 8;
+  for (int r = 0; r < npeer; ++r)
+    MQC_REQUIRE(ypeer[r] != nullptr && aligned(ypeer[r], qa), MQC_ERR_MISALIGNED,
+                "%s: output %d null or not %d-byte aligned", name, r, int(qa));
+  mqc_ssm_scan_args a1 = *a;
+  a1.y = ypeer[0];  // validated like y; the kernel writes every ypeer[r]
+  const PeerSpec peer{ypeer, npeer, ch_total, ch_off};
+  return chunked_impl(&a1, nchunks, workspace, workspace_bytes, &peer, stream);
+}
+
+namespace {
+
+int chunked_impl(const mqc_ssm_scan_args* a, int64_t nchunks, void* workspace,
+                 size_t workspace_bytes, const PeerSpec* peer, void* stream) {
+  const char* name = peer ? "mqc_ssm_scan_fwd_chunked_peer" : "mqc_ssm_scan_fwd_chunked";
   MQC_REQUIRE(a != nullptr, MQC_ERR_INVALID_VALUE, "%s: null args", name);
   MQC_REQUIRE(!(a->flags & MQC_SSM_Q_GIVEN), MQC_ERR_UNSUPPORTED,
               "%s: explicit q is not supported (use the fused form)", name);
@@ -134,7 +199,7 @@ extern "C" int mqc_ssm_scan_fwd_chunked(const mqc_ssm_scan_args* a, int64_t nchu
   FwdParams p{};
   int rc = validate_and_fill(a, &p, name);
   if (rc != MQC_OK || p.T == 0 || p.B == 0 || p.D == 0) return rc;
-  if (nchunks == 1) return mqc_ssm_scan_fwd(a, stream);
+  if (nchunks == 1) return scan_pass(a, peer, stream);
   MQC_REQUIRE(p.T % nchunks == 0, MQC_ERR_INVALID_VALUE, "%s: seq_len %d not divisible by %lld",
               name, p.T, (long long)nchunks);
   // chunks are folded into the batch, so the skip weight may vary over channels only
@@ -172,7 +237,7 @@ extern "C" int mqc_ssm_scan_fwd_chunked(const mqc_ssm_scan_args* a, int64_t nchu
   rc = packed ? dispatch_state_only_packed(p1, a->dtype, s_real, st)
               : dispatch_state_only(p1, a->dtype, s_real, shared, st);
   if (rc != MQC_OK) return rc;
-  if (!skip_last) return carry_and_rescan(a, p, nchunks, Pbuf, hloc, hin, stream);
+  if (!skip_last) return carry_and_rescan(a, p, nchunks, Pbuf, hloc, hin, peer, stream);
 
   // one batch row: carry over the first nc-1 summaries gives every chunk's start
   // state (the last one written as the carry's final state); pass 2 then writes
@@ -188,7 +253,7 @@ extern "C" int mqc_ssm_scan_fwd_chunked(const mqc_ssm_scan_args* a, int64_t nchu
   a2.seq_len = p.T / nchunks;
   a2.h0 = hin;
   a2.hT = p.hT != nullptr ? hloc : nullptr;
-  rc = mqc_ssm_scan_fwd(&a2, stream);
+  rc = scan_pass(&a2, peer, stream);
   if (rc != MQC_OK || p.hT == nullptr) return rc;
   const cudaError_t e = cudaMemcpyAsync(p.hT, hloc + size_t(nchunks - 1) * lanes * 4,
                                         size_t(lanes) * 16, cudaMemcpyDeviceToDevice, st);
@@ -196,6 +261,8 @@ extern "C" int mqc_ssm_scan_fwd_chunked(const mqc_ssm_scan_args* a, int64_t nchu
                           : fail(MQC_ERR_CUDA, "%s: final state copy: %s", name,
                                  cudaGetErrorString(e));
 }
+
+}  // namespace
 
 extern "C" size_t mqc_ssm_scan_fwd_summary_workspace_size(int64_t batch, int64_t channels,
                                                           int64_t d_state, int64_t nchunks) {
@@ -318,5 +385,5 @@ extern "C" int mqc_ssm_scan_fwd_chunked_resume(const mqc_ssm_scan_args* a, int64
   const float* Pbuf = static_cast<const float*>(workspace);
   const float* hloc = Pbuf + size_t(p.B) * nchunks * lanes * 4;
   float* hin = static_cast<float*>(workspace) + size_t(2) * p.B * nchunks * lanes * 4;
-  return carry_and_rescan(a, p, nchunks, Pbuf, hloc, hin, stream);
+  return carry_and_rescan(a, p, nchunks, Pbuf, hloc, hin, nullptr, stream);
 }

@@ -39,7 +39,14 @@ struct FwdParams {
   int nb;   // CTAs per batch row
   int cpb;  // max channels per CTA
   int tc;   // timesteps per chunk
+  // Peer outputs of the channel-sharded scan (packed kernel only): with npeer > 0
+  // y goes to every ypeer[r] instead of y, each laid out as rows of y_ld elements
+  // per (batch, time) step with this shard's channels starting at element y_coff.
+  int npeer;
+  int64_t y_ld, y_coff;
+  void* ypeer[8];
 };
+constexpr int kMaxPeerOutputs = 8;
 
 struct SmemLayout {
   size_t off_b, off_c, off_delta, off_s, total;

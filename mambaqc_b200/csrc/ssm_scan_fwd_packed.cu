@@ -109,6 +109,42 @@ __device__ __forceinline__ void reduce_store_y_pk(float4 a, float4 sv, float dsk
   }
 }
 
+// The reduction of reduce_store_y_pk with the store left to `store(comp, value,
+// pred)` (the peer-output form writes every value to several buffers).
+template <int NG, typename Store>
+__device__ __forceinline__ void reduce_y_pk(float4 a, float4 sv, float dsk, int ng, bool active,
+                                            Store&& store) {
+  constexpr unsigned kFull = 0xffffffffu;
+  if constexpr (NG == 1) {
+    store(0, fmaf(dsk, sv.x, a.x), active);
+    store(1, fmaf(dsk, sv.y, a.y), active);
+    store(2, fmaf(dsk, sv.z, a.z), active);
+    store(3, fmaf(dsk, sv.w, a.w), active);
+  } else {
+    const bool odd = ng & 1;
+    const float s0 = odd ? a.x : a.y;
+    const float s1 = odd ? a.z : a.w;
+    const float r0 = __shfl_xor_sync(kFull, s0, 1);
+    const float r1 = __shfl_xor_sync(kFull, s1, 1);
+    const float k0 = (odd ? a.y : a.x) + r0;
+    const float k1 = (odd ? a.w : a.z) + r1;
+    if constexpr (NG == 2) {
+      const int c0 = odd ? 1 : 0;
+      store(c0, fmaf(dsk, f4_get(sv, c0), k0), active);
+      store(c0 + 2, fmaf(dsk, f4_get(sv, c0 + 2), k1), active);
+    } else {
+      const bool hi = (ng >> 1) & 1;
+      const float snd = hi ? k0 : k1;
+      const float r = __shfl_xor_sync(kFull, snd, 2);
+      float v = (hi ? k1 : k0) + r;
+#pragma unroll
+      for (int m = 4; m < NG; m <<= 1) v += __shfl_xor_sync(kFull, v, m);
+      const int comp = ng & 3;
+      store(comp, fmaf(dsk, f4_get(sv, comp), v), active && ng < 4);
+    }
+  }
+}
+
 // Bounded wait for a thread off the critical path (the producer, which runs
 // chunks ahead of the consumers): sleeps between polls so that its polling
 // does not take issue slots from the consumer warps on its sub-partition.
@@ -219,7 +255,11 @@ __host__ __device__ inline PkLayout pk_layout(int tc, int np, int warps, int cpw
 // span{1, u}, u = Im Lambda / |Im Lambda|, where quaternions commute and
 // multiply like complex numbers, so P is kept as (Pa, Pb) with P = Pa + Pb u:
 // 4 operations per step instead of a 16-term Hamilton product.
-template <typename T, int G, int NG, bool S_REAL, bool CKPT, bool DT, bool SO>
+// PEER (channel-sharded scan, not with CKPT, DT or SO): y is written into the
+// p.npeer output buffers p.ypeer[r] -- this GPU's and the other ranks' (peer
+// memory over NVLink) -- at this shard's channel columns, so the exchange of y
+// between the ranks happens in the scan's own stores, tile by tile.
+template <typename T, int G, int NG, bool S_REAL, bool CKPT, bool DT, bool SO, bool PEER = false>
 __global__ void __launch_bounds__(pk_max_threads(G), 1)
     scan_fwd_packed_kernel(const FwdParams p) {
   static_assert(G % 2 == 0, "states are processed in pairs");
@@ -362,7 +402,9 @@ __global__ void __launch_bounds__(pk_max_threads(G), 1)
   __syncwarp();
 
   const float eps = p.eps;
-  T* yb = SO ? nullptr : static_cast<T*>(p.y) + (int64_t(b) * T_ * D + c) * 4;
+  T* yb = (SO || PEER) ? nullptr : static_cast<T*>(p.y) + (int64_t(b) * T_ * D + c) * 4;
+  // peer outputs: element offset of (b, t = 0, this channel) in every buffer
+  const int64_t ypo = PEER ? int64_t(b) * T_ * p.y_ld + p.y_coff + int64_t(c) * 4 : 0;
   for (int k = 0; k < nchunks; ++k) {
     const int st = k % kRing;
     const int buf = k & 1;
@@ -386,10 +428,11 @@ __global__ void __launch_bounds__(pk_max_threads(G), 1)
     const float* rowC = sC + int64_t(st) * tc * NP * 4 + ng * 8;
     // unrolled by two so the loop-carried states alternate between two register
     // sets instead of being copied back at every step
-    T* yrow = yb + int64_t(t0) * D * 4;
-    const int64_t ystep = int64_t(D) * 4;
+    T* yrow = PEER ? nullptr : yb + int64_t(t0) * D * 4;
+    const int64_t ystep = PEER ? 0 : int64_t(D) * 4;
+    int64_t yrow_peer = ypo + int64_t(t0) * p.y_ld;
 #pragma unroll 2
-    for (int tt = 0; tt < len; ++tt, yrow += ystep) {
+    for (int tt = 0; tt < len; ++tt, yrow += ystep, yrow_peer += PEER ? p.y_ld : 0) {
       const float dl = cdel[tt * CPW + lc_ch];
       const float dl2 = dl * dl;
       float4 sv;
@@ -437,7 +480,15 @@ __global__ void __launch_bounds__(pk_max_threads(G), 1)
           dsk = (active && ng < 4) ? __ldg(p.dskip + int64_t(b) * p.dsb +
                                            int64_t(t0 + tt) * p.dst + int64_t(c) * p.dsd)
                                    : 0.f;
-        reduce_store_y_pk<T, NG>(yv, sv, dsk, ng, active, yrow);
+        if constexpr (PEER) {
+          reduce_y_pk<NG>(yv, sv, dsk, ng, active, [&](int comp, float v, bool pred) {
+#pragma unroll
+            for (int r = 0; r < kMaxPeerOutputs; ++r)
+              if (r < p.npeer) st1_pred(static_cast<T*>(p.ypeer[r]) + yrow_peer + comp, v, pred);
+          });
+        } else {
+          reduce_store_y_pk<T, NG>(yv, sv, dsk, ng, active, yrow);
+        }
       }
       if constexpr (CKPT) {
         const int t = t0 + tt;
@@ -470,6 +521,9 @@ __global__ void __launch_bounds__(pk_max_threads(G), 1)
         if (n < N) QIO<float>::st(p.hT + ((int64_t(b) * D + c) * N + n) * 4, qp_half(h[j], e));
       }
   }
+  // stores to peer memory: visible system-wide before the kernel is seen as
+  // complete by the ranks that synchronise with it
+  if constexpr (PEER) __threadfence_system();
   if constexpr (SO) {
     if (active) {
 #pragma unroll
@@ -559,6 +613,7 @@ int launch_packed(FwdParams p, bool state_only, cudaStream_t st) {
     p.tc = tc;
     const bool ck = p.ckpt != nullptr, dt = p.dst != 0;
     auto kern = state_only ? scan_fwd_packed_kernel<T, G, NG, S_REAL, false, false, true>
+                : p.npeer > 0 ? scan_fwd_packed_kernel<T, G, NG, S_REAL, false, false, false, true>
                 : ck ? (dt ? scan_fwd_packed_kernel<T, G, NG, S_REAL, true, true, false>
                            : scan_fwd_packed_kernel<T, G, NG, S_REAL, true, false, false>)
                      : (dt ? scan_fwd_packed_kernel<T, G, NG, S_REAL, false, true, false>

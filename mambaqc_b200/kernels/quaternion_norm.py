@@ -18,7 +18,7 @@ import torch
 
 from .. import _lib
 
-__all__ = ["quaternion_layer_norm_fused", "QuaternionLayerNorm"]
+__all__ = ["quaternion_layer_norm_fused", "QuaternionLayerNorm", "quaternion_layer_norm_linear"]
 
 
 def _compat_default() -> bool:
@@ -68,6 +68,88 @@ class _QLayerNorm(torch.autograd.Function):
                       dbeta.data_ptr(), ws.data_ptr(), ws_bytes, rows, dm, float(ctx.eps),
                       _lib.dtype_code(qc), _lib.stream_ptr(qc.device))
         return dq, dgamma.to(ctx.gamma_dtype), dbeta.to(ctx.beta_dtype), None, None
+
+
+class _QLNLinear(torch.autograd.Function):
+    """LN(q) @ weight^T (+ bias) with the LayerNorm as the GEMM's operand
+    prologue (``mqc_qln_linear_fwd``); bf16. The backward recomputes LN(q)
+    (``mqc_qln_fwd``) for the weight gradient, takes both GEMMs on cuBLAS and
+    the LayerNorm backward on ``mqc_qln_bwd`` with the saved row statistics."""
+
+    @staticmethod
+    def forward(ctx, q, gamma, beta, weight, bias, eps):
+        qc = _lib.aligned_contig(q, 16)
+        bsz, seqlen, dm, _ = qc.shape
+        rows = bsz * seqlen
+        nout = weight.shape[0]
+        w = _lib.aligned_contig(weight, 16)
+        bc = bias.contiguous() if bias is not None else None
+        g32 = _lib.aligned_contig(gamma.detach().float(), 4)
+        b32 = _lib.aligned_contig(beta.detach().float(), 16)
+        out = torch.empty(bsz, seqlen, nout, dtype=q.dtype, device=q.device)
+        mean = torch.empty(rows, dtype=torch.float32, device=q.device)
+        rstd = torch.empty(rows, dtype=torch.float32, device=q.device)
+        status = _lib.status_word(q.device)
+        with torch.cuda.device(q.device):
+            _lib.call("mqc_qln_linear_fwd", qc.data_ptr(), g32.data_ptr(), b32.data_ptr(),
+                      w.data_ptr(), _lib.ptr(bc), out.data_ptr(), mean.data_ptr(),
+                      rstd.data_ptr(), rows, dm, nout, float(eps), status.data_ptr(),
+                      _lib.stream_ptr(q.device))
+        if _lib.sync_checks_enabled():
+            _lib.check_device_status(q.device)
+        ctx.save_for_backward(qc, g32, b32, w, mean, rstd)
+        ctx.eps = eps
+        ctx.has_bias = bias is not None
+        ctx.dtypes = (gamma.dtype, beta.dtype)
+        return out
+
+    @staticmethod
+    def backward(ctx, gout):
+        qc, g32, b32, w, mean, rstd = ctx.saved_tensors
+        bsz, seqlen, dm, _ = qc.shape
+        rows = bsz * seqlen
+        dev = qc.device
+        yn = torch.empty_like(qc)
+        with torch.cuda.device(dev):
+            _lib.call("mqc_qln_fwd", qc.data_ptr(), g32.data_ptr(), b32.data_ptr(),
+                      yn.data_ptr(), None, None, rows, dm, float(ctx.eps), 0,
+                      _lib.dtype_code(qc), _lib.stream_ptr(dev))
+        g2 = gout.reshape(rows, -1).to(qc.dtype)
+        dw = g2.t() @ yn.reshape(rows, dm * 4)
+        dyn = (g2 @ w).reshape(bsz, seqlen, dm, 4).contiguous()
+        dbias = g2.float().sum(0).to(qc.dtype) if ctx.has_bias else None
+        dq = torch.empty_like(qc)
+        dgamma = torch.empty(dm, dtype=torch.float32, device=dev)
+        dbeta = torch.empty(dm, 4, dtype=torch.float32, device=dev)
+        lib = _lib.load()
+        ws_bytes = lib.mqc_qln_bwd_workspace_size(rows, dm)
+        ws = torch.empty(max(1, ws_bytes // 4), dtype=torch.float32, device=dev)
+        with torch.cuda.device(dev):
+            _lib.call("mqc_qln_bwd", qc.data_ptr(), g32.data_ptr(), dyn.data_ptr(),
+                      mean.data_ptr(), rstd.data_ptr(), dq.data_ptr(), dgamma.data_ptr(),
+                      dbeta.data_ptr(), ws.data_ptr(), ws_bytes, rows, dm, float(ctx.eps),
+                      _lib.dtype_code(qc), _lib.stream_ptr(dev))
+        return (dq, dgamma.to(ctx.dtypes[0]), dbeta.to(ctx.dtypes[1]), dw, dbias, None)
+
+
+def quaternion_layer_norm_linear(q: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor,
+                                 weight: torch.Tensor, bias: torch.Tensor | None = None,
+                                 eps: float = 1e-5) -> torch.Tensor:
+    """``F.linear(quaternion_layer_norm_fused(q, gamma, beta, eps).flatten(-2), weight, bias)``
+    in one pass over q: the LayerNorm is applied to each q tile inside the
+    projection GEMM (sm_100a tensor cores) and its output is never stored.
+
+    q [B, T, D, 4] bf16 with D a multiple of 16; weight [N, 4D] and bias [N]
+    bf16. Returns [B, T, N] bf16. This is the block's
+    ``out_proj(norm(y_quat))`` (quaternion_mamba2_block.py:154-157)."""
+    assert q.ndim == 4 and q.shape[-1] == 4, f"Expected [B, T, D, 4], got {q.shape}"
+    dm = q.shape[2]
+    assert gamma.shape == (dm,) and beta.shape == (dm, 4)
+    assert weight.ndim == 2 and weight.shape[1] == 4 * dm
+    assert q.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16
+    assert bias is None or (bias.shape == (weight.shape[0],) and bias.dtype == torch.bfloat16)
+    _lib.require_cuda(q, gamma, beta, weight, bias, what="quaternion_layer_norm_linear")
+    return _QLNLinear.apply(q, gamma, beta, weight, bias, eps)
 
 
 def quaternion_layer_norm_fused(q: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor,

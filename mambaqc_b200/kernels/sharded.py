@@ -190,15 +190,24 @@ def ssm_scan_cayley_channel_sharded(delta: torch.Tensor, Lambda: torch.Tensor, B
     scan (default: ``ssm_scan_cayley`` with ``time_chunks``).
 
     ``gather="peer"`` (CUDA, ranks on one node): instead of the collective
-    library's all-gather and a permute of its rank-major result, every rank
-    pushes each scanned segment straight into its channel columns of every
-    rank's output buffer over NVLink (``mqc_channel_push`` into
-    ``PeerOutput`` buffers), on a side stream under the next segment's scan. Two
-    one-element all-reduces on the compute stream order the exchange: one on
-    entry (every rank is done with the previous result before it is
-    overwritten) and one on exit (every push has landed). The returned tensor is
-    this rank's peer buffer, valid until the next call with the same shape.
+    library's all-gather and a permute of its rank-major result, y is written
+    straight into its channel columns of every rank's output buffer
+    (``PeerOutput``, CUDA IPC) over NVLink. With channel-shared B/C and the
+    default scan this happens inside the scan kernel itself
+    (``mqc_ssm_scan_fwd_chunked_peer``: every y value is stored to all ranks'
+    buffers as it is produced, and ``segments`` is not needed); otherwise each
+    scanned segment is pushed by ``mqc_channel_push`` on a side stream under
+    the next segment's scan. Two one-element all-reduces on the compute stream
+    order the exchange: one on entry (every rank is done with the previous
+    result before it is overwritten) and one on exit (every store has landed).
+    The returned tensor is this rank's peer buffer, valid until the next call
+    with the same shape.
     """
+    # the scan kernel itself writes every rank's output: channel-shared B/C, the
+    # default scan, a per-channel skip weight, inputs that need no gradient
+    fused_peer = (scan_fn is None and B.dim() == 4 and D.dim() == 1 and
+                  not (torch.is_grad_enabled() and any(
+                      t.requires_grad for t in (delta, Lambda, B, C, S, D))))
     if scan_fn is None:
         from .ssm_fused import ssm_scan_cayley
 
@@ -217,6 +226,8 @@ def ssm_scan_cayley_channel_sharded(delta: torch.Tensor, Lambda: torch.Tensor, B
     if gather == "peer":
         if not on_cuda:
             raise ValueError("gather='peer' needs CUDA tensors")
+        if fused_peer:
+            return _channel_sharded_peer_fused(delta, Lambda, B, C, S, D, group, time_chunks)
         return _channel_sharded_peer(delta, Lambda, B, C, S, D, group, scan_fn, segments)
     if gather != "nccl":
         raise ValueError(f"gather must be 'nccl' or 'peer', got {gather!r}")
@@ -280,6 +291,26 @@ def _channel_sharded_peer(delta, Lambda, B, C, S, D, group, scan_fn, segments):
         yk.record_stream(comm)
     compute.wait_stream(comm)
     dist.all_reduce(flag, group=group)  # every rank's pushes have completed
+    return out.tensor
+
+
+def _channel_sharded_peer_fused(delta, Lambda, B, C, S, D, group, time_chunks):
+    from .ssm_fused import _run_scan_chunked, auto_time_chunks
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    bsz, seqlen, dl = delta.shape[:3]
+    ds = Lambda.shape[1]
+    dev = delta.device
+    nc = (auto_time_chunks(bsz, seqlen, dl, ds, dev) if time_chunks == "auto"
+          else int(time_chunks))
+    if nc > 1 and seqlen // nc <= 8:
+        nc = 1
+    out = _peer_output((bsz, seqlen, world * dl, 4), delta.dtype, dev, group)
+    flag = _barrier_flag(dev)
+    dist.all_reduce(flag, group=group)  # every rank is done with the previous result
+    _run_scan_chunked(delta, Lambda, B, C, S, D, None, 1e-6, nc, False,
+                      peer=(out.ptrs, world * dl, rank * dl))
+    dist.all_reduce(flag, group=group)  # every rank's stores have landed
     return out.tensor
 
 

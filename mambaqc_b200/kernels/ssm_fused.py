@@ -212,8 +212,14 @@ def auto_time_chunks(bsz: int, seqlen: int, channels: int, d_state: int,
     return nc
 
 
-def _run_scan_chunked(delta, Lam, B, C, S, D, h0, eps, nchunks, return_final_state):
-    """Time-parallel forward (``mqc_ssm_scan_fwd_chunked``); no autograd."""
+def _run_scan_chunked(delta, Lam, B, C, S, D, h0, eps, nchunks, return_final_state,
+                      peer=None):
+    """Time-parallel forward (``mqc_ssm_scan_fwd_chunked``); no autograd.
+
+    ``peer = (ptrs, ch_total, ch_off)``: the channel-sharded form
+    (``mqc_ssm_scan_fwd_chunked_peer``) that writes y into every buffer of
+    ``ptrs`` ([B, T, ch_total, 4], local or peer memory) at channels
+    ch_off.. instead of returning it; y is then None."""
     dt = delta.dtype
     bsz, seqlen, dm = delta.shape
     ds = Lam.shape[1]
@@ -228,7 +234,8 @@ def _run_scan_chunked(delta, Lam, B, C, S, D, h0, eps, nchunks, return_final_sta
     if dsb != 0 or dst != 0:
         raise ValueError("time-chunked scan needs a per-channel skip weight D [D]")
     h0c = _prep(h0.float(), 16) if h0 is not None else None
-    y = torch.empty(bsz, seqlen, dm, 4, dtype=dt, device=delta.device)
+    y = (torch.empty(bsz, seqlen, dm, 4, dtype=dt, device=delta.device) if peer is None
+         else None)
     hT = (torch.empty(bsz, dm, ds, 4, dtype=torch.float32, device=delta.device)
           if return_final_state else None)
     lib = _lib.load()
@@ -240,11 +247,18 @@ def _run_scan_chunked(delta, Lam, B, C, S, D, h0, eps, nchunks, return_final_sta
         batch=bsz, seq_len=seqlen, channels=dm, d_state=ds, dtype=_lib.dtype_code(dc),
         flags=flags, eps=float(eps), reserved0=0, delta=dc.data_ptr(), lambda_=Lc.data_ptr(),
         q=None, Bm=Bc.data_ptr(), Cm=Cc.data_ptr(), s=Sc.data_ptr(), dskip=Df.data_ptr(),
-        dskip_sb=0, dskip_st=0, dskip_sd=dsd, h0=_lib.ptr(h0c), y=y.data_ptr(),
+        dskip_sb=0, dskip_st=0, dskip_sd=dsd, h0=_lib.ptr(h0c), y=_lib.ptr(y),
         hT=_lib.ptr(hT), status=status.data_ptr(), wait_poll_limit=-1, ckpt=None, ckpt_every=0)
     with torch.cuda.device(delta.device):
-        _lib.call("mqc_ssm_scan_fwd_chunked", ctypes.byref(a), int(nchunks), ws.data_ptr(),
-                  ws_bytes, _lib.stream_ptr(delta.device))
+        if peer is None:
+            _lib.call("mqc_ssm_scan_fwd_chunked", ctypes.byref(a), int(nchunks), ws.data_ptr(),
+                      ws_bytes, _lib.stream_ptr(delta.device))
+        else:
+            ptrs, ch_total, ch_off = peer
+            arr = (ctypes.c_void_p * len(ptrs))(*ptrs)
+            _lib.call("mqc_ssm_scan_fwd_chunked_peer", ctypes.byref(a), int(nchunks),
+                      ws.data_ptr(), ws_bytes, arr, len(ptrs), int(ch_total), int(ch_off),
+                      _lib.stream_ptr(delta.device))
     if _lib.sync_checks_enabled():
         _lib.check_device_status(delta.device)
     return y, hT

@@ -14,12 +14,14 @@ same initial weights. The forward follows :124-230 with two differences:
   for expand_factor != 1; its Lite block slices the same way
   (quaternion_mamba2_lite_block.py:163).
 
-The projections stay dense PyTorch linears (cuBLAS). Everything between them
-runs in ``libmambaqc_b200.so``:
+The in/dt/gate/B/C projections stay dense PyTorch linears (cuBLAS). Everything
+between them runs in ``libmambaqc_b200.so``:
 * the causal conv + SiLU, read in place from the in_proj output;
 * the step sizes and gated signal (softplus, sigmoid gate);
 * the scan, the quaternion LayerNorm, and the output gate + residual.
-Each has a forward and a backward kernel.
+Each has a forward and a backward kernel. Under bf16 autocast the LayerNorm is
+the operand prologue of the output projection's GEMM (a tcgen05 kernel of this
+library), so its output is never stored.
 """
 
 from __future__ import annotations
@@ -29,6 +31,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from mambaqc_b200.kernels.block_fused import causal_conv1d_silu, gate_residual, ssm_scan_inputs
+from mambaqc_b200.kernels.quaternion_norm import quaternion_layer_norm_linear
 from mambaqc_b200.kernels.ssm_fused import ssm_scan_cayley, ssm_step_cayley
 from mambaqc_b200.layers.causal_conv1d import CausalConv1d
 from mambaqc_b200.layers.quaternion_linear import (
@@ -80,9 +83,28 @@ class QuaternionMamba2Block(nn.Module):
         conv = self.conv1d.conv
         x_act = causal_conv1d_silu(x_inner, conv.weight, conv.bias)
         y_quat, h_T = self._ssm_forward(x_act, return_state=True)
-        y_real = self.out_proj(self.norm(y_quat))
+        y_real = self._norm_out_proj(y_quat)
         out = gate_residual(x, z[..., : self.d_model], y_real)
         return (out, h_T) if return_ssm_state else out
+
+    def _norm_out_proj(self, y_quat: torch.Tensor) -> torch.Tensor:
+        """``out_proj(norm(y_quat))`` (block lines 154-157). Under bf16 autocast --
+        where the projection would run in bf16 on the LayerNorm's bf16 output --
+        the LayerNorm is applied inside the projection GEMM
+        (``quaternion_layer_norm_linear``), so the normalised activations are
+        never written to memory; otherwise the two modules run in turn."""
+        w = self.out_proj.weight
+        fusable = (y_quat.is_cuda and y_quat.dtype == torch.bfloat16 and
+                   torch.is_autocast_enabled("cuda") and
+                   torch.get_autocast_dtype("cuda") == torch.bfloat16 and
+                   self.d_inner % 16 == 0 and y_quat.dim() == 4)
+        if not fusable:
+            return self.out_proj(self.norm(y_quat))
+        bias = self.out_proj.bias
+        with torch.autocast("cuda", enabled=False):
+            return quaternion_layer_norm_linear(
+                y_quat, self.norm.gamma, self.norm.beta, w.to(torch.bfloat16),
+                None if bias is None else bias.to(torch.bfloat16), self.norm.eps)
 
     def _ssm_forward(self, x: torch.Tensor, return_state: bool = False):
         bsz, seqlen, d_inner = x.shape

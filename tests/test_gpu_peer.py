@@ -4,9 +4,12 @@
   the ranks' outputs: every destination must hold every rank's channel shard in
   the final [B, T, D, 4] layout (bit-exact copy), for fp32 and bf16, and for a
   shard width whose rows are not whole 16-byte pieces (8-byte path).
+* ``mqc_ssm_scan_fwd_chunked_peer`` on one GPU, the scan kernel storing y into
+  several local buffers standing in for the ranks' outputs.
 * On two GPUs (skipped with fewer): two NCCL ranks run the channel-sharded scan
-  with ``gather="peer"`` (IPC buffers, pushes over NVLink) and ``gather="nccl"``;
-  the results must be equal bit for bit and match the unsharded scan.
+  with ``gather="peer"`` (IPC buffers; y stored by the scan kernel, or pushed
+  per segment) and ``gather="nccl"``; the results must be equal bit for bit
+  and match the unsharded scan.
 """
 
 import os
@@ -41,6 +44,34 @@ def test_channel_push_emulated_ranks(dtype, dl):
         assert torch.equal(o, full)
 
 
+@pytest.mark.parametrize("dtype,nc", [(torch.float32, 4), (torch.bfloat16, 4),
+                                      (torch.bfloat16, 1)])
+def test_scan_with_peer_outputs_emulated_ranks(dtype, nc):
+    """mqc_ssm_scan_fwd_chunked_peer on one GPU: three channel shards, each
+    scanned with its y stored into three local buffers standing in for the
+    ranks' outputs. Every buffer must equal the shards' ordinary chunked scans
+    laid side by side, bit for bit (same kernel, same chunks)."""
+    from mambaqc_b200.kernels.ssm_fused import _run_scan_chunked
+    world, dl = 3, 5
+    inp = to_dev(make_scan_inputs(1, 256, world * dl, 32, shared=True, s_real=True, seed=11),
+                 dtype)
+    outs = [torch.full((1, 256, world * dl, 4), float("nan"), device=DEV, dtype=dtype)
+            for _ in range(world)]
+    ptrs = [o.data_ptr() for o in outs]
+    want = []
+    for r in range(world):
+        cs = slice(r * dl, (r + 1) * dl)
+        args = (inp["delta"][..., cs], inp["Lambda"][cs], inp["B"], inp["C"], inp["S"][..., cs],
+                inp["D"][cs])
+        y, _ = _run_scan_chunked(*args, None, 1e-6, nc, False)
+        want.append(y)
+        _run_scan_chunked(*args, None, 1e-6, nc, False, peer=(ptrs, world * dl, r * dl))
+    torch.cuda.synchronize()
+    full = torch.cat(want, dim=2)
+    for o in outs:
+        assert torch.equal(o, full)
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -67,13 +98,23 @@ def _two_rank_worker(rank, world, port, q):
         sh["Lambda"] = d["Lambda"][rank * dl:(rank + 1) * dl]
         sh["D"] = d["D"][rank * dl:(rank + 1) * dl]
         args = (sh["delta"], sh["Lambda"], sh["B"], sh["C"], sh["S"], sh["D"])
-        y_nccl = ssm_scan_cayley_channel_sharded(*args, time_chunks=4, segments=4).clone()
+        # y stored into both ranks' buffers by the scan kernel itself
+        y_nccl1 = ssm_scan_cayley_channel_sharded(*args, time_chunks=4).clone()
         for _ in range(2):  # the second call reuses the cached peer buffers
-            y_peer = ssm_scan_cayley_channel_sharded(*args, time_chunks=4, segments=4,
-                                                     gather="peer").clone()
+            y_fused = ssm_scan_cayley_channel_sharded(*args, time_chunks=4,
+                                                      gather="peer").clone()
+
+        # segments pushed by mqc_channel_push (an explicit scan function)
+        def scan_fn(dd, L, Bm, Cm, s, Dk, h0=None):
+            return ssm_scan_cayley(dd, L, Bm, Cm, s, Dk, h0=h0, return_final_state=True,
+                                   time_chunks=4)
+        y_nccl4 = ssm_scan_cayley_channel_sharded(*args, scan_fn=scan_fn, segments=4).clone()
+        y_push = ssm_scan_cayley_channel_sharded(*args, scan_fn=scan_fn, segments=4,
+                                                 gather="peer").clone()
         y_full = ssm_scan_cayley(d["delta"], d["Lambda"], d["B"], d["C"], d["S"], d["D"])
         torch.cuda.synchronize()
-        q.put((rank, torch.equal(y_peer, y_nccl), rel_l2(y_peer.float(), y_full.float())))
+        q.put((rank, torch.equal(y_fused, y_nccl1) and torch.equal(y_push, y_nccl4),
+               max(rel_l2(y_fused.float(), y_full.float()), rel_l2(y_push.float(), y_full.float()))))
         release_peer_outputs()
     finally:
         dist.destroy_process_group()
