@@ -955,7 +955,36 @@ def run_config2(args, world, rank, local):
         ms = time_rotating([(lambda x=x: quaternion_layer_norm_fused(x, gamma, beta)) for x in xs])
         res["layer_norm"] = {"shape": list(xs[0].shape), "ms": ms, "sets": nx,
                              "bytes": 2 * xs[0].numel() * 4 + gamma.numel() * 4 + beta.numel() * 4}
-        del xs
+        # the LayerNorm backward (mqc_qln_bwd): reads q and dout, writes dq, and
+        # the per-CTA dgamma/dbeta partials summed in a fixed order
+        import ctypes as _ct
+
+        from mambaqc_b200 import _lib
+        rows, dm = 4 * 2048, 768
+        mean = torch.empty(rows, device=dev)
+        rstd = torch.empty(rows, device=dev)
+        douts = [torch.randn_like(x) for x in xs]
+        dqs = [torch.empty_like(x) for x in xs]
+        dgam = torch.empty(dm, device=dev)
+        dbet = torch.empty(dm, 4, device=dev)
+        lib = _lib.load()
+        ws_bytes = lib.mqc_qln_bwd_workspace_size(rows, dm)
+        ws = torch.empty(max(1, ws_bytes // 4), device=dev)
+        for x in xs[:1]:
+            _lib.call("mqc_qln_fwd", x.data_ptr(), gamma.data_ptr(), beta.data_ptr(),
+                      dqs[0].data_ptr(), mean.data_ptr(), rstd.data_ptr(), rows, dm, 1e-5, 0,
+                      _lib.MQC_DTYPE_F32, stream.cuda_stream)
+
+        def ln_bwd(i):
+            _lib.call("mqc_qln_bwd", xs[i].data_ptr(), gamma.data_ptr(), douts[i].data_ptr(),
+                      mean.data_ptr(), rstd.data_ptr(), dqs[i].data_ptr(), dgam.data_ptr(),
+                      dbet.data_ptr(), ws.data_ptr(), _ct.c_size_t(ws_bytes), rows, dm, 1e-5,
+                      _lib.MQC_DTYPE_F32, torch.cuda.current_stream(dev).cuda_stream)
+        ms = time_rotating([(lambda i=i: ln_bwd(i)) for i in range(nx)])
+        res["layer_norm_backward"] = {"shape": list(xs[0].shape), "ms": ms, "sets": nx,
+                                      "bytes": 3 * xs[0].numel() * 4 + gamma.numel() * 4 +
+                                      5 * dm * 4}
+        del xs, douts, dqs
     for v in res.values():
         v["gbps"] = v["bytes"] / (v["ms"] / 1e3) / 1e9
         v["frac_of_hbm"] = v["gbps"] / hbm
@@ -963,7 +992,8 @@ def run_config2(args, world, rank, local):
         geo = math.exp(sum(math.log(v["frac_of_hbm"]) for v in res.values()) / len(res))
         line = {
             "metric": "config2 quaternion primitives, HBM bandwidth (geometric mean fraction of "
-                      "measured HBM over qmul, Cayley, prefix scan, LayerNorm)",
+                      "measured HBM over qmul, Cayley, prefix scan, LayerNorm forward and "
+                      "backward)",
             "value": geo, "unit": "fraction of measured HBM GB/s", "n_gpus": world,
             "steps": steps, "warmup": 3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config-2 shapes)",

@@ -6,6 +6,8 @@
 // of d_model quaternions, staged in shared memory by cp.async (16-byte coalesced
 // copies), so the row is read from HBM once and written once. Mean and variance of the norms are two-pass over registers
 // (mean first, then centred squares), with warp-shuffle + shared-memory sums.
+#include <type_traits>
+
 #include "mqc_common.cuh"
 #include "mqc_host.h"
 
@@ -28,6 +30,28 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   float s = 0.f;
   for (int i = 0; i < nw; ++i) s += red[i];  // same order on every thread
   return s;
+}
+
+// Two block sums in one pass (one pair of barriers): red must hold 64 floats.
+__device__ __forceinline__ float2 block_sum2(float a, float b, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();  // red[] reuse across calls
+  if (l == 0) {
+    red[w] = a;
+    red[32 + w] = b;
+  }
+  __syncthreads();
+  float sa = 0.f, sb = 0.f;
+  for (int i = 0; i < nw; ++i) {  // same order on every thread
+    sa += red[i];
+    sb += red[32 + i];
+  }
+  return make_float2(sa, sb);
 }
 
 // 8-byte asynchronous global -> shared copy (one bf16 quaternion).
@@ -129,12 +153,39 @@ __host__ __device__ inline int64_t beta_partial_offset(int64_t parts, int64_t D)
   return (parts * D + 3) / 4 * 4;
 }
 
-template <typename T>
-__global__ void __launch_bounds__(1024) qln_bwd_kernel(
+// The rows are staged in shared memory with cp.async, double-buffered where two
+// rows of q and dout fit (nstage = 2): the copies of the next row are in flight
+// while the current one is reduced and written, so no registers wait on loads.
+// Every thread copies, and later reads, only its own quaternions
+// d = threadIdx.x + j * blockDim.x, so the staging needs no barrier.
+// MAXT: the CTA size the register budget is sized for (512 for d_model <= 2048,
+// 1024 for the widest rows).
+template <typename T, int MAXT>
+__global__ void __launch_bounds__(MAXT) qln_bwd_kernel(
     const T* __restrict__ q, const float* __restrict__ gamma, const T* __restrict__ dout,
     const float* __restrict__ mean, const float* __restrict__ rstd, T* __restrict__ dq,
-    float* __restrict__ partial, int64_t rows, int D, float eps) {
-  __shared__ float red[32];
+    float* __restrict__ partial, int64_t rows, int D, float eps, int nstage) {
+  __shared__ float red[64];
+  extern __shared__ __align__(16) unsigned char sbuf_raw[];
+  T* sbuf = reinterpret_cast<T*>(sbuf_raw);
+  const int64_t rlen = int64_t(D) * 4;  // elements of one row
+  // stage s: the q row at sbuf + 2 s rlen, the dout row right after it
+  auto stage_row = [&](int64_t row, int s) {
+    const T* qr = q + row * rlen;
+    const T* gr = dout + row * rlen;
+    T* sq = sbuf + 2 * s * rlen;
+    T* sg = sq + rlen;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+      if constexpr (sizeof(T) == 4) {
+        cp_async16(sq + d * 4, qr + d * 4, true);
+        cp_async16(sg + d * 4, gr + d * 4, true);
+      } else {
+        cp_async8(sq + d * 4, qr + d * 4);
+        cp_async8(sg + d * 4, gr + d * 4);
+      }
+    }
+    cp_async_commit();
+  };
   float dg[kVptB];
   float4 db[kVptB];
   float gm[kVptB];
@@ -145,56 +196,69 @@ __global__ void __launch_bounds__(1024) qln_bwd_kernel(
     const int d = threadIdx.x + j * blockDim.x;
     gm[j] = d < D ? __ldg(gamma + d) : 0.f;
   }
+  int s = 0;
+  if (blockIdx.x < rows) stage_row(blockIdx.x, 0);
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
-    const T* qr = q + row * D * 4;
-    const T* gr = dout + row * D * 4;
+    const int64_t nxt = row + gridDim.x;
+    if (nstage == 2 && nxt < rows) {
+      stage_row(nxt, s ^ 1);
+      cp_async_wait_group<1>();
+    } else {
+      cp_async_wait_group<0>();
+    }
+    const T* sq = sbuf + 2 * s * rlen;
+    const T* sg = sq + rlen;
     const float mu = __ldg(mean + row), rs = __ldg(rstd + row);
-    float4 qv[kVptB], gv[kVptB];
     float nrm[kVptB], nh[kVptB], av[kVptB];
     float sa = 0.f, san = 0.f;
 #pragma unroll
     for (int j = 0; j < kVptB; ++j) {
       const int d = threadIdx.x + j * blockDim.x;
-      qv[j] = f4_zero();
-      gv[j] = f4_zero();
       nrm[j] = 1.f;
       nh[j] = 0.f;
       av[j] = 0.f;
       if (d < D) {
-        qv[j] = QIO<T>::ld(qr + d * 4);
-        gv[j] = QIO<T>::ld(gr + d * 4);
-        const float4 a = qv[j];
+        const float4 a = QIO<T>::lds(sq + d * 4);
+        const float4 gv = QIO<T>::lds(sg + d * 4);
         nrm[j] = sqrtf(fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, a.w * a.w))) + eps);
         nh[j] = (nrm[j] - mu) * rs;
         const float dn = nrm[j] + eps;
-        const float gu = fmaf(gv[j].x, a.x, fmaf(gv[j].y, a.y, fmaf(gv[j].z, a.z, gv[j].w * a.w))) / dn;
+        const float gu = fmaf(gv.x, a.x, fmaf(gv.y, a.y, fmaf(gv.z, a.z, gv.w * a.w))) / dn;
         av[j] = gm[j] * gu;
         sa += av[j];
         san = fmaf(av[j], nh[j], san);
         dg[j] = fmaf(nh[j], gu, dg[j]);
-        db[j].x += gv[j].x;
-        db[j].y += gv[j].y;
-        db[j].z += gv[j].z;
-        db[j].w += gv[j].w;
+        db[j].x += gv.x;
+        db[j].y += gv.y;
+        db[j].z += gv.z;
+        db[j].w += gv.w;
       }
     }
-    const float ma = block_sum(sa, red) / float(D);
-    const float man = block_sum(san, red) / float(D);
+    const float2 sums = block_sum2(sa, san, red);
+    const float ma = sums.x / float(D);
+    const float man = sums.y / float(D);
 #pragma unroll
     for (int j = 0; j < kVptB; ++j) {
       const int d = threadIdx.x + j * blockDim.x;
       if (d < D) {
+        const float4 qv = QIO<T>::lds(sq + d * 4);
+        const float4 gv = QIO<T>::lds(sg + d * 4);
         const float dn = nrm[j] + eps;
         const float dldn = rs * (av[j] - ma - nh[j] * man) - nh[j] * av[j] / dn;
         const float cg = gm[j] * nh[j] / dn;
         const float cq = dldn / nrm[j];
         float4 o;
-        o.x = fmaf(cg, gv[j].x, cq * qv[j].x);
-        o.y = fmaf(cg, gv[j].y, cq * qv[j].y);
-        o.z = fmaf(cg, gv[j].z, cq * qv[j].z);
-        o.w = fmaf(cg, gv[j].w, cq * qv[j].w);
-        QIO<T>::st(dq + row * D * 4 + d * 4, o);
+        o.x = fmaf(cg, gv.x, cq * qv.x);
+        o.y = fmaf(cg, gv.y, cq * qv.y);
+        o.z = fmaf(cg, gv.z, cq * qv.z);
+        o.w = fmaf(cg, gv.w, cq * qv.w);
+        QIO<T>::st_stream(dq + row * rlen + d * 4, o);
       }
+    }
+    if (nstage == 2) {
+      s ^= 1;
+    } else if (nxt < rows) {
+      stage_row(nxt, 0);  // this thread has read all of its staged quaternions
     }
   }
   // partial layout: [parts][D] dgamma, then (16-byte aligned) [parts][D] float4 dbeta
@@ -229,7 +293,7 @@ __global__ void qln_bwd_reduce_kernel(const float* __restrict__ partial, float* 
 }
 
 int qln_bwd_parts(int64_t rows) {
-  int64_t p = int64_t(num_sms()) * 2;
+  int64_t p = int64_t(num_sms()) * 3;
   if (p > rows) p = rows;
   return p < 1 ? 1 : int(p);
 }
@@ -268,7 +332,7 @@ extern "C" int mqc_qln_fwd(const void* q, const float* gamma, const float* beta,
   }
   cudaStream_t st = as_stream(stream);
   const size_t srow_bytes = size_t(D) * 4 * (dtype == MQC_DTYPE_F32 ? 4 : 2);
-  if (srow_bytes > 48 * 1024) {
+  if (srow_bytes + 1024 > 48 * 1024) {  // (the static reduction buffer counts too)
     cudaError_t e = dtype == MQC_DTYPE_F32
                         ? cudaFuncSetAttribute(qln_fwd_kernel<float>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -306,7 +370,7 @@ int qln_row_stats(const void* q, float* mean, float* rstd, int64_t rows, int64_t
   threads = (threads + 31) / 32 * 32;
   if (threads < 32) threads = 32;
   const size_t srow_bytes = size_t(D) * 4 * (dtype == MQC_DTYPE_F32 ? 4 : 2);
-  if (srow_bytes > 48 * 1024) {
+  if (srow_bytes + 1024 > 48 * 1024) {  // (the static reduction buffer counts too)
     cudaError_t e = dtype == MQC_DTYPE_F32
                         ? cudaFuncSetAttribute(qln_fwd_kernel<float>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -363,15 +427,34 @@ extern "C" int mqc_qln_bwd(const void* q, const float* gamma, const void* dout, 
   threads = (threads + 31) / 32 * 32;
   const int parts = qln_bwd_parts(rows);
   float* partial = static_cast<float*>(workspace);
-  if (dtype == MQC_DTYPE_F32) {
-    qln_bwd_kernel<float><<<parts, threads, 0, st>>>(
-        static_cast<const float*>(q), gamma, static_cast<const float*>(dout), mean, rstd,
-        static_cast<float*>(dq), partial, rows, D, eps);
-  } else {
-    qln_bwd_kernel<__nv_bfloat16><<<parts, threads, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(q), gamma, static_cast<const __nv_bfloat16*>(dout), mean,
-        rstd, static_cast<__nv_bfloat16*>(dq), partial, rows, D, eps);
-  }
+  const bool wide = threads > 512;
+  // two staged rows of q and dout where they fit in 100 KB (two CTAs per SM at
+  // least), else one
+  const size_t row_bytes = size_t(D) * 4 * (dtype == MQC_DTYPE_F32 ? 4 : 2);
+  const int nstage = 4 * row_bytes <= 100 * 1024 ? 2 : 1;
+  const size_t smem = size_t(nstage) * 2 * row_bytes;
+  auto launch = [&](auto kern, auto tq) -> int {
+    using TT = std::remove_const_t<std::remove_pointer_t<decltype(tq)>>;
+    if (smem + 1024 > 48 * 1024) {  // (the static reduction buffer counts too)
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           int(smem));
+      if (e != cudaSuccess)
+        return fail(MQC_ERR_CUDA, "mqc_qln_bwd: smem attribute (%zu B): %s", smem,
+                    cudaGetErrorString(e));
+    }
+    kern<<<parts, threads, smem, st>>>(static_cast<const TT*>(q), gamma,
+                                       static_cast<const TT*>(dout), mean, rstd,
+                                       static_cast<TT*>(dq), partial, rows, D, eps, nstage);
+    return MQC_OK;
+  };
+  int rc;
+  if (dtype == MQC_DTYPE_F32)
+    rc = launch(wide ? qln_bwd_kernel<float, 1024> : qln_bwd_kernel<float, 512>,
+                static_cast<const float*>(nullptr));
+  else
+    rc = launch(wide ? qln_bwd_kernel<__nv_bfloat16, 1024> : qln_bwd_kernel<__nv_bfloat16, 512>,
+                static_cast<const __nv_bfloat16*>(nullptr));
+  if (rc != MQC_OK) return rc;
   qln_bwd_reduce_kernel<<<(5 * D + 255) / 256, 256, 0, st>>>(partial, dgamma, dbeta, parts, D);
   return check_launch("mqc_qln_bwd");
 }

@@ -229,6 +229,10 @@ int dispatch_state_only_packed(const FwdParams& p, int dtype, bool s_real, cudaS
 int dispatch_stream(const FwdParams& p, int dtype, bool s_real, bool q_given, cudaStream_t st);
 // Streaming kernel for channel-shared B/C (short sequences).
 int dispatch_stream_shared(const FwdParams& p, int dtype, bool s_real, cudaStream_t st);
+// One decode step (T = 1, channel-shared B/C, no checkpoints or operator
+// product) on the batch-blocked decode kernel (ssm_scan_decode.cu).
+bool decode_serves(const FwdParams& p);
+int dispatch_decode(const FwdParams& p, int dtype, bool s_real, cudaStream_t st);
 // Sequences up to this length with channel-shared B/C skip the packed kernel's
 // pre-pass and producer pipeline and take the streaming kernel.
 constexpr int kShortScan = 8;

@@ -344,6 +344,8 @@ extern "C" int mqc_ssm_scan_fwd(const mqc_ssm_scan_args* a, void* stream) {
   const bool q_given = (a->flags & MQC_SSM_Q_GIVEN) != 0;
   const bool s_real = (a->flags & MQC_SSM_S_REAL) != 0;
   if (!use_generic_kernel()) {
+    if (shared && !q_given && decode_serves(p))
+      return dispatch_decode(p, a->dtype, s_real, as_stream(stream));
     if (shared && !q_given && p.T <= kShortScan && p.ckpt == nullptr)
       return dispatch_stream_shared(p, a->dtype, s_real, as_stream(stream));
     if (shared && !q_given)

@@ -300,6 +300,39 @@ def test_decode_step_with_state_cache(shared, dtype):
     assert rel_l2(ys[0], y_ref[:, 0]) < tol
 
 
+@pytest.mark.parametrize("case", [
+    # (B, D, N, s_real, dtype): batch rows not a multiple of the kernel's row
+    # block, channel counts not a multiple of a CTA's channels, N from 1 to 64
+    (1, 1, 1, True, torch.float32),
+    (5, 37, 3, True, torch.float32),
+    (7, 13, 16, False, torch.float32),
+    (4, 96, 33, True, torch.float32),
+    (6, 50, 64, False, torch.float32),
+    (9, 40, 64, True, torch.bfloat16),
+    (3, 21, 18, False, torch.bfloat16),  # bf16 channel-shared B/C needs an even N
+], ids=lambda c: "B{}D{}N{}{}{}".format(c[0], c[1], c[2], "x" if c[3] else "S",
+                                      "f32" if c[4] == torch.float32 else "bf16"))
+def test_decode_kernel_odd_shapes(case):
+    """One decode step (T = 1, channel-shared B/C, state cache in place) against
+    the fp64 oracle, with and without an initial state."""
+    from mambaqc_b200.kernels import ssm_step_cayley
+    bsz, dm, ds, s_real, dtype = case
+    inp = make_scan_inputs(bsz, 1, dm, ds, shared=True, s_real=s_real, seed=bsz * 100 + dm + ds)
+    d = to_dev(inp, dtype)
+    tol = RTOL_F32 if dtype == torch.float32 else RTOL_BF16
+    for with_h0 in (False, True):
+        h0 = (torch.randn(bsz, dm, ds, 4, generator=gen(ds), dtype=torch.float64) if with_h0
+              else torch.zeros(bsz, dm, ds, 4, dtype=torch.float64))
+        h = h0.to(DEV, torch.float32)
+        y = ssm_step_cayley(d["delta"][:, 0], d["Lambda"], d["B"][:, 0], d["C"][:, 0],
+                            d["S"][:, 0], d["D"], h)
+        torch.cuda.synchronize()
+        y_ref, h_ref = ref.ssm_scan_cayley(inp["delta"], inp["Lambda"], inp["B"], inp["C"],
+                                           inp["S"], inp["D"], h0=h0)
+        assert rel_l2(y, y_ref[:, 0]) < tol
+        assert rel_l2(h, h_ref) < tol
+
+
 def test_config3_full_size_bf16_channel_sample():
     """Config 3 at full size with bf16 inputs (fp32 state): the oracle runs in fp64
     on the bf16-rounded inputs of a channel sample, so h_T differs only by the
