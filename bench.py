@@ -1256,6 +1256,62 @@ def run_config4_block(args, world, rank, local):
     ms_proj = None
     if wb is not None:
         ms_proj = max_over_ranks(timed(proj_only, steps, 3, world, stream) / steps, world, dev)
+
+    # the block's forward alone (inference, no autograd), with the B/C
+    # projections fused into the scan and without (cuBLAS projections + scan)
+    def fwd(fused):
+        def run():
+            with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+                blk(x, fused_bc_proj=fused)
+        return run
+
+    ms_fwd = {k: max_over_ranks(timed(fwd(k == "fused"), steps, 3, world, stream) / steps,
+                                world, dev) for k in ("unfused", "fused")}
+
+    # the two halves of the block that are fused into tcgen05 kernels here, each
+    # against the unfused form it replaces (forward, bf16, the block's shapes)
+    from mambaqc_b200.kernels.bc_proj_scan import bc_proj_scan
+    from mambaqc_b200.kernels import quaternion_layer_norm_fused, ssm_scan_cayley
+    from mambaqc_b200.kernels.quaternion_norm import quaternion_layer_norm_linear
+    din = 2 * dmod
+    xa3 = xa.view(bsz, seqlen, din)
+    wc = blk.C_proj.weight.detach().to(torch.bfloat16)
+    dl = torch.nn.functional.softplus(torch.randn(bsz, seqlen, din, generator=g, device=dev) - 3.0
+                                      ).bfloat16()
+    sg = torch.randn(bsz, seqlen, din, generator=g, device=dev).bfloat16()
+    lam = torch.empty(din, nst, 4, device=dev)
+    lam[..., 0] = -0.01
+    lam[..., 1:] = 0.3
+    dsk = torch.ones(din, device=dev)
+    yq = torch.randn(bsz, seqlen, din, 4, generator=g, device=dev).bfloat16()
+    gam = torch.ones(din, device=dev)
+    bet = torch.zeros(din, 4, device=dev)
+    wo = blk.out_proj.weight.detach().to(torch.bfloat16)
+
+    def bc_fused():
+        with torch.no_grad():
+            bc_proj_scan(xa3, wb, wc, dl, lam, sg, dsk)
+
+    def bc_unfused():
+        with torch.no_grad():
+            Bq = (xa3 @ wb.t()).view(bsz, seqlen, din, nst, 4)
+            Cq = (xa3 @ wc.t()).view(bsz, seqlen, din, nst, 4)
+            ssm_scan_cayley(dl, lam, Bq, Cq, sg, dsk)
+
+    def ln_fused():
+        with torch.no_grad():
+            quaternion_layer_norm_linear(yq, gam, bet, wo)
+
+    def ln_unfused():
+        with torch.no_grad():
+            quaternion_layer_norm_fused(yq, gam, bet).flatten(-2) @ wo.t()
+
+    parts = {}
+    for name, f in (("bc_proj_scan_fused", bc_fused), ("bc_proj_scan_unfused", bc_unfused),
+                    ("ln_out_proj_fused", ln_fused), ("ln_out_proj_unfused", ln_unfused)):
+        parts[name] = max_over_ranks(timed(f, steps, 3, world, stream) / steps, world, dev)
+    bc_flops = 2 * 2 * bsz * seqlen * din * din * nst * 4
+    ln_flops = 2 * bsz * seqlen * (4 * din) * dmod
     peaks, peak_kind = measured_peaks()
     din = 2 * dmod
     proj_flops = 2 * 3 * 2 * (bsz * seqlen) * din * (din * nst * 4)
@@ -1277,6 +1333,13 @@ def run_config4_block(args, world, rank, local):
                                                           peaks.get("bf16_tflops", 1590.0))
                                                 if ms_proj else None),
             "bf16_peak_source": f"MEASURED_PEAKS.json ({peak_kind})",
+            "forward_ms": {"unfused_bc_proj": ms_fwd["unfused"], "fused_bc_proj": ms_fwd["fused"]},
+            "fused_parts_ms": parts,
+            "fused_parts_tflops": {
+                "bc_proj_scan_fused": bc_flops / (parts["bc_proj_scan_fused"] / 1e3) / 1e12,
+                "bc_proj_scan_unfused": bc_flops / (parts["bc_proj_scan_unfused"] / 1e3) / 1e12,
+                "ln_out_proj_fused": ln_flops / (parts["ln_out_proj_fused"] / 1e3) / 1e12,
+                "ln_out_proj_unfused": ln_flops / (parts["ln_out_proj_unfused"] / 1e3) / 1e12},
         }
         print(json.dumps(line), flush=True)
     return 0

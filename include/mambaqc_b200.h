@@ -204,6 +204,47 @@ MQC_API int mqc_ssm_scan_fwd(const mqc_ssm_scan_args* args, void* stream);
  * models/quaternion_mamba2_block.py:214-228, with the transfers inside the call. */
 MQC_API int mqc_ssm_scan_fwd_host(const mqc_ssm_scan_args* args, int64_t segments, void* stream);
 
+/*
+ * The block's B/C projections fused into its per-channel scan (forward):
+ *
+ *   B[b,t,d,n,:] = sum_k x[b,t,k] w_b[(d*N + n)*4 + :, k]   (C likewise with w_c)
+ *   h_t = cayley(delta[b,t,d] Lambda[d,n]) (x) h_{t-1} + B_t s[b,t,d]
+ *   y[b,t,d] = sum_n C_t (x) h_t + dskip[d] (s[b,t,d], 0, 0, 0)
+ *
+ * with B and C rounded to bf16 (the projection's output in the reference's bf16
+ * autocast) and never written to memory: the tensor cores produce each
+ * channel's B/C tile on chip and the scan consumes it from shared memory.
+ * Shapes: x [batch*seq_len, in_features] bf16 (the block's activated inner
+ * signal, row-major); w_b, w_c [channels*d_state*4, in_features] bf16 (the
+ * B_proj/C_proj weights as stored); delta, s [batch, seq_len, channels] and
+ * y [batch, seq_len, channels, 4] in `dtype`; Lambda [channels, d_state, 4],
+ * h0/hT [batch, channels, d_state, 4] fp32 (optional); skip weight of channel d
+ * at dskip[d*dskip_sd]. d_state 16, 32 or 64; in_features a multiple of 64.
+ * Replaces B_proj(x), C_proj(x) and the scan of
+ * QuaternionMamba2Block._ssm_forward, models/quaternion_mamba2_block.py:186-191
+ * and 214-228 (the projections: layers/quaternion_linear.py:145-161).
+ */
+typedef struct mqc_bc_proj_scan_args {
+  int64_t batch, seq_len, channels, d_state, in_features;
+  int32_t dtype;
+  float eps;
+  const void* x;
+  const void* w_b;
+  const void* w_c;
+  const void* delta;
+  const void* s;
+  const float* lambda_;
+  const float* dskip;
+  int64_t dskip_sd;
+  const float* h0;
+  float* hT;
+  void* y;
+  int32_t* status;
+  int64_t wait_poll_limit;
+} mqc_bc_proj_scan_args;
+
+MQC_API int mqc_bc_proj_scan_fwd(const mqc_bc_proj_scan_args* args, void* stream);
+
 MQC_API size_t mqc_ssm_scan_fwd_chunked_workspace_size(int64_t batch, int64_t channels,
                                                        int64_t d_state, int64_t nchunks);
 MQC_API int mqc_ssm_scan_fwd_chunked(const mqc_ssm_scan_args* args, int64_t nchunks,

@@ -71,6 +71,19 @@ class SsmScanBwdArgs(ctypes.Structure):
     ]
 
 
+class BcProjScanArgs(ctypes.Structure):
+    """Mirror of ``mqc_bc_proj_scan_args``."""
+
+    _fields_ = [
+        ("batch", _i64), ("seq_len", _i64), ("channels", _i64), ("d_state", _i64),
+        ("in_features", _i64), ("dtype", ctypes.c_int32), ("eps", _f32),
+        ("x", _c_void_p), ("w_b", _c_void_p), ("w_c", _c_void_p), ("delta", _c_void_p),
+        ("s", _c_void_p), ("lambda_", _c_void_p), ("dskip", _c_void_p), ("dskip_sd", _i64),
+        ("h0", _c_void_p), ("hT", _c_void_p), ("y", _c_void_p), ("status", _c_void_p),
+        ("wait_poll_limit", _i64),
+    ]
+
+
 # name -> (argtypes); every function returns int status unless listed in _STR_FUNCS
 _SIGNATURES = {
     "mqc_qmul": [_c_void_p, _c_void_p, _c_void_p, _i64, _i32, _c_void_p],
@@ -124,6 +137,7 @@ _SIGNATURES.update({
                                       _i64, _c_void_p],
     "mqc_qln_linear_fwd": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                            _c_void_p, _c_void_p, _i64, _i64, _i64, _f32, _c_void_p, _c_void_p],
+    "mqc_bc_proj_scan_fwd": [ctypes.POINTER(BcProjScanArgs), _c_void_p],
     "mqc_channel_push": [_c_void_p, ctypes.POINTER(_c_void_p), _i32, _i64, _i64, _i64, _i64,
                          _i64, _i64, _i64, _i32, _c_void_p],
 })

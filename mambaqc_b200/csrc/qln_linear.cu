@@ -31,8 +31,7 @@
 
 #include <mutex>
 
-#include "mqc_common.cuh"
-#include "mqc_host.h"
+#include "tc_common.cuh"
 
 namespace mqc {
 namespace {
@@ -57,88 +56,25 @@ constexpr size_t kSmemBytes = 1024 + size_t(kStages) * kStageBytes + sizeof(Smem
 
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
                                               volatile int* abort_flag, int* status) {
-  for (long long i = 0; i < kPollLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 1023) == 1023 && *abort_flag) return false;
-  }
-  *abort_flag = 1;
-  report_status(status, MQC_DEVICE_STATUS_TIMEOUT);
-  return false;
+  return tc::wait_or_abort(bar, parity, abort_flag, status, kPollLimit);
 }
 
-__device__ __forceinline__ void mbar_arrive_plain(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
+using tc::fence_async_smem;
+using tc::mbar_arrive_plain;
+using tc::mma_commit;
+using tc::pack_bf16x2;
+using tc::tc_fence_after;
+using tc::tc_fence_before;
+using tc::tma_load_2d;
+using tc::tmem_ld32;
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
-      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
-      : "memory");
-}
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) { return tc::kmajor_desc<128>(saddr); }
 
-// Shared-memory matrix descriptor of a K-major tile with the 128-byte swizzle
-// (rows of 64 bf16 = 128 bytes, 8-row atoms 1024 bytes apart): start address,
-// leading byte offset 16 (unused by this layout), stride byte offset 1024,
-// descriptor version 1, layout type 2 (128-byte swizzle).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  return uint64_t((saddr >> 4) & 0x3FFF) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
-         (uint64_t(1) << 46) | (uint64_t(2) << 61);
-}
-
-// Instruction descriptor of tcgen05.mma kind::f16: fp32 accumulator, bf16 A
-// and B, both K-major, M = BM, N = BN.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) |
-                            (uint32_t(BM >> 4) << 24);
+constexpr uint32_t kIdesc = tc::idesc_bf16(BM, BN);
 
 __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
                                          uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_addr(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void fence_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-// 32 consecutive fp32 accumulator columns of this thread's tensor-memory lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
-      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
-      "%30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
-  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&h);
+  tc::mma_bf16<kIdesc>(tmem_d, adesc, bdesc, accumulate);
 }
 
 // The LayerNorm of one bf16 quaternion, as qln_fwd_kernel computes it.
@@ -192,11 +128,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     ctl->rstd[threadIdx.x] = m < p.M ? p.rstd[m] : 0.f;
   }
   if (warp == 1) {  // tensor memory for the accumulator (whole warp)
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_addr(&ctl->tmem_base)),
-                 "r"(kTmemCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    tc::tmem_alloc(&ctl->tmem_base, kTmemCols);
   }
   tc_fence_before();
   __syncthreads();
@@ -322,11 +254,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(kTmemCols)
-                 : "memory");
+    tc::tmem_dealloc(tmem, kTmemCols);
   }
 }
+
+}  // namespace
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link
 // against the driver library).
@@ -334,11 +266,11 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-std::mutex g_encode_mutex;
-EncodeTiledFn g_encode = nullptr;
+static std::mutex g_encode_mutex;
+static EncodeTiledFn g_encode = nullptr;
 
-int make_map_2d(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols, uint32_t box_rows,
-                uint32_t box_cols) {
+int make_map_bf16_2d(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols,
+                     uint32_t box_rows, uint32_t box_cols, int row_bytes, const char* who) {
   {
     std::lock_guard<std::mutex> lock(g_encode_mutex);
     if (g_encode == nullptr) {
@@ -347,7 +279,7 @@ int make_map_2d(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols,
       if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) !=
               cudaSuccess ||
           f == nullptr)
-        return fail(MQC_ERR_CUDA, "mqc_qln_linear_fwd: cuTensorMapEncodeTiled unavailable");
+        return fail(MQC_ERR_CUDA, "%s: cuTensorMapEncodeTiled unavailable", who);
       g_encode = reinterpret_cast<EncodeTiledFn>(f);
     }
   }
@@ -355,16 +287,16 @@ int make_map_2d(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols,
   const cuuint64_t strides[1] = {cols * 2};
   const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr),
-                              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUresult r = g_encode(
+      map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+      CU_TENSOR_MAP_INTERLEAVE_NONE,
+      row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
-    return fail(MQC_ERR_CUDA, "mqc_qln_linear_fwd: cuTensorMapEncodeTiled failed (%d)", int(r));
+    return fail(MQC_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", who, int(r));
   return MQC_OK;
 }
 
-}  // namespace
 }  // namespace mqc
 
 using namespace mqc;
@@ -392,8 +324,9 @@ extern "C" int mqc_qln_linear_fwd(const void* q, const float* gamma, const float
   if (rc != MQC_OK) return rc;
   const int64_t K = 4 * d_model;
   CUtensorMap tmY, tmW;
-  rc = make_map_2d(&tmY, q, uint64_t(rows), uint64_t(K), BM, BK);
-  if (rc == MQC_OK) rc = make_map_2d(&tmW, weight, uint64_t(out_features), uint64_t(K), BN, BK);
+  rc = make_map_bf16_2d(&tmY, q, uint64_t(rows), uint64_t(K), BM, BK, 128, name);
+  if (rc == MQC_OK)
+    rc = make_map_bf16_2d(&tmW, weight, uint64_t(out_features), uint64_t(K), BN, BK, 128, name);
   if (rc != MQC_OK) return rc;
   cudaError_t e = cudaFuncSetAttribute(qln_linear_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,

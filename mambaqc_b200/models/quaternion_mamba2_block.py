@@ -19,9 +19,11 @@ between them runs in ``libmambaqc_b200.so``:
 * the causal conv + SiLU, read in place from the in_proj output;
 * the step sizes and gated signal (softplus, sigmoid gate);
 * the scan, the quaternion LayerNorm, and the output gate + residual.
-Each has a forward and a backward kernel. Under bf16 autocast the LayerNorm is
-the operand prologue of the output projection's GEMM (a tcgen05 kernel of this
-library), so its output is never stored.
+Each has a forward and a backward kernel. Two tcgen05 fusions are opt-in
+(``fused_norm_out_proj``: the LayerNorm as the operand prologue of the output
+projection's GEMM; ``fused_bc_proj``: the B/C projections computed inside the
+scan kernel), since at the config-4 block shape both measure slower than the
+unfused kernels.
 """
 
 from __future__ import annotations
@@ -30,6 +32,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from mambaqc_b200.kernels.bc_proj_scan import bc_proj_scan, bc_proj_scan_supported
 from mambaqc_b200.kernels.block_fused import causal_conv1d_silu, gate_residual, ssm_scan_inputs
 from mambaqc_b200.kernels.quaternion_norm import quaternion_layer_norm_linear
 from mambaqc_b200.kernels.ssm_fused import ssm_scan_cayley, ssm_step_cayley
@@ -68,6 +71,15 @@ class QuaternionMamba2Block(nn.Module):
         # Optional fixed Lambda [d_inner, d_state, 4] used instead of the
         # (-softplus(alpha), tanh(imag)) parameterisation (not part of state_dict).
         self.lambda_override: torch.Tensor | None = None
+        # Under bf16 autocast, compute B_proj/C_proj inside the scan kernel
+        # (``bc_proj_scan``) instead of storing them; ``forward(..., fused_bc_proj=)``
+        # overrides it per call. Off by default: at the config-4 block shape the
+        # fused forward measures slower than cuBLAS projections + the scan.
+        self.fused_bc_proj = False
+        # Under bf16 autocast, apply the LayerNorm inside the output projection's
+        # GEMM (``quaternion_layer_norm_linear``). Off by default: at the config-4
+        # block shape it measures slower than the LayerNorm kernel + cuBLAS.
+        self.fused_norm_out_proj = False
 
     def ssm_lambda(self) -> torch.Tensor:
         """Lambda [d_inner, d_state, 4] = (-softplus(alpha), tanh(imag)) (block.py:206-212)."""
@@ -77,24 +89,27 @@ class QuaternionMamba2Block(nn.Module):
         imag = torch.tanh(self.Lambda_imag.float())
         return torch.cat([real.unsqueeze(-1), imag], dim=-1)
 
-    def forward(self, x: torch.Tensor, return_ssm_state: bool = False):
+    def forward(self, x: torch.Tensor, return_ssm_state: bool = False,
+                fused_bc_proj: bool | None = None):
         xz = self.in_proj(x)
         x_inner, z = xz.chunk(2, dim=-1)
         conv = self.conv1d.conv
         x_act = causal_conv1d_silu(x_inner, conv.weight, conv.bias)
-        y_quat, h_T = self._ssm_forward(x_act, return_state=True)
+        y_quat, h_T = self._ssm_forward(x_act, return_state=True, fused_bc_proj=fused_bc_proj)
         y_real = self._norm_out_proj(y_quat)
         out = gate_residual(x, z[..., : self.d_model], y_real)
         return (out, h_T) if return_ssm_state else out
 
     def _norm_out_proj(self, y_quat: torch.Tensor) -> torch.Tensor:
-        """``out_proj(norm(y_quat))`` (block lines 154-157). Under bf16 autocast --
-        where the projection would run in bf16 on the LayerNorm's bf16 output --
-        the LayerNorm is applied inside the projection GEMM
-        (``quaternion_layer_norm_linear``), so the normalised activations are
-        never written to memory; otherwise the two modules run in turn."""
+        """``out_proj(norm(y_quat))`` (block lines 154-157). With
+        ``fused_norm_out_proj`` set, under bf16 autocast -- where the projection
+        would run in bf16 on the LayerNorm's bf16 output -- the LayerNorm is
+        applied inside the projection GEMM (``quaternion_layer_norm_linear``), so
+        the normalised activations are never written to memory; otherwise the
+        two modules run in turn."""
         w = self.out_proj.weight
-        fusable = (y_quat.is_cuda and y_quat.dtype == torch.bfloat16 and
+        fusable = (self.fused_norm_out_proj and y_quat.is_cuda and
+                   y_quat.dtype == torch.bfloat16 and
                    torch.is_autocast_enabled("cuda") and
                    torch.get_autocast_dtype("cuda") == torch.bfloat16 and
                    self.d_inner % 16 == 0 and y_quat.dim() == 4)
@@ -106,9 +121,26 @@ class QuaternionMamba2Block(nn.Module):
                 y_quat, self.norm.gamma, self.norm.beta, w.to(torch.bfloat16),
                 None if bias is None else bias.to(torch.bfloat16), self.norm.eps)
 
-    def _ssm_forward(self, x: torch.Tensor, return_state: bool = False):
+    def _bc_fusable(self, x: torch.Tensor, fused_bc_proj: bool | None) -> bool:
+        want = self.fused_bc_proj if fused_bc_proj is None else fused_bc_proj
+        return (bool(want) and x.is_cuda and torch.is_autocast_enabled("cuda") and
+                torch.get_autocast_dtype("cuda") == torch.bfloat16 and x.dim() == 3 and
+                self.B_proj.bias is None and self.C_proj.bias is None and
+                bc_proj_scan_supported(self.d_inner, self.d_state))
+
+    def _ssm_forward(self, x: torch.Tensor, return_state: bool = False,
+                     fused_bc_proj: bool | None = None):
         bsz, seqlen, d_inner = x.shape
         delta, s_real = ssm_scan_inputs(self.dt_proj(x), self.gate_proj(x), x)
+        if self._bc_fusable(x, fused_bc_proj):
+            # B_proj / C_proj (block lines 186-191) as the scan kernel's own
+            # tensor-core prologue: the projections are never stored
+            bf = torch.bfloat16
+            with torch.autocast("cuda", enabled=False):
+                y, h_T = bc_proj_scan(x.to(bf), self.B_proj.weight.to(bf),
+                                      self.C_proj.weight.to(bf), delta.to(bf), self.ssm_lambda(),
+                                      s_real.to(bf), self.D, return_final_state=True)
+            return (y, h_T) if return_state else y
         Bq = self.B_proj(x).view(bsz, seqlen, d_inner, self.d_state, 4)
         Cq = self.C_proj(x).view(bsz, seqlen, d_inner, self.d_state, 4)
         dt = Bq.dtype

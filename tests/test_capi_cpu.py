@@ -68,7 +68,8 @@ def _c_offsets(struct, fields, tmp_path):
 
 @pytest.mark.skipif(shutil.which("gcc") is None, reason="needs gcc")
 @pytest.mark.parametrize("cstruct,pystruct", [("mqc_ssm_scan_args", "SsmScanArgs"),
-                                              ("mqc_ssm_scan_bwd_args", "SsmScanBwdArgs")])
+                                              ("mqc_ssm_scan_bwd_args", "SsmScanBwdArgs"),
+                                              ("mqc_bc_proj_scan_args", "BcProjScanArgs")])
 def test_struct_layout_matches_header(cstruct, pystruct, tmp_path):
     py = getattr(_lib, pystruct)
     fields = [f for f, _ in py._fields_]
@@ -116,6 +117,32 @@ def test_scan_argument_validation_without_gpu():
     assert call(flags=_lib.MQC_SSM_BC_SHARED, dtype=1, d_state=15) == UNSUPPORTED
     assert call(dskip=None) == INVALID
     assert call(batch=70000) == UNSUPPORTED
+    assert call(seq_len=0) == 0  # nothing to do
+
+
+@no_gpu
+def test_bc_proj_scan_argument_validation_without_gpu():
+    """mqc_bc_proj_scan_fwd rejects bad arguments on the host, before any launch."""
+    lib = _lib.load()
+    fake = 0x10000
+    base = dict(batch=2, seq_len=8, channels=4, d_state=64, in_features=128, dtype=1, eps=1e-6,
+                x=fake, w_b=fake, w_c=fake, delta=fake, s=fake, lambda_=fake, dskip=fake,
+                dskip_sd=1, h0=None, hT=None, y=fake, status=None, wait_poll_limit=-1)
+
+    def call(**kw):
+        a = _lib.BcProjScanArgs(**{**base, **kw})
+        return lib.mqc_bc_proj_scan_fwd(ctypes.byref(a), None)
+
+    assert call(dtype=3) == INVALID
+    assert call(d_state=48) == UNSUPPORTED
+    assert b"d_state" in lib.mqc_last_error()
+    assert call(in_features=100) == UNSUPPORTED
+    assert b"in_features" in lib.mqc_last_error()
+    assert call(w_c=None) == INVALID
+    assert call(x=fake + 8) == MISALIGNED
+    assert call(y=fake + 4) == MISALIGNED
+    assert call(channels=70000) == UNSUPPORTED
+    assert call(batch=-1) == INVALID
     assert call(seq_len=0) == 0  # nothing to do
 
 

@@ -89,3 +89,28 @@ def test_qln_linear_rejects_unsupported_width():
     with pytest.raises(RuntimeError, match="multiple of 16"):
         quaternion_layer_norm_linear(q, torch.ones(20, device=DEV), torch.zeros(20, 4, device=DEV),
                                      w)
+
+
+def test_block_fused_norm_out_proj_matches_unfused():
+    """QuaternionMamba2Block under bf16 autocast with ``fused_norm_out_proj``
+    against the same block with the LayerNorm kernel + cuBLAS: output and every
+    parameter gradient."""
+    from mambaqc_b200.models import QuaternionMamba2Block
+    torch.manual_seed(0)
+    blk = QuaternionMamba2Block(128, d_state=16).to(DEV)
+    g = torch.Generator(device=DEV).manual_seed(2)
+    x = torch.randn(2, 200, 128, generator=g, device=DEV)
+    gout = torch.randn(2, 200, 128, generator=g, device=DEV)
+    res = {}
+    for fused in (False, True):
+        blk.fused_norm_out_proj = fused
+        blk.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            out = blk(x)
+        (out.float() * gout).sum().backward()
+        res[fused] = (out.detach().float(), {n: p.grad.detach().float().clone()
+                                             for n, p in blk.named_parameters()})
+    torch.cuda.synchronize()
+    assert rel_l2(res[True][0], res[False][0]) < UNFUSED_TOL
+    for n in res[False][1]:
+        assert rel_l2(res[True][1][n], res[False][1][n]) < 2e-2, n
