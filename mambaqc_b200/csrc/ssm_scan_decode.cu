@@ -132,18 +132,233 @@ int dispatch_decode_t(const FwdParams& p, cudaStream_t st) {
   }
 }
 
+// ------------------------------------------------ large decode batches
+// For many batch rows the step is a pure stream of the state cache (read once,
+// written once). A CTA owns a block of CB channels -- its Lambda constants stay
+// in registers -- and walks a range of batch rows; for each row a producer warp
+// bulk-copies the block's contiguous state slab (CB x N x 16 bytes, 8 KB at
+// N = 64) and the row's B and C into a kStrStages-deep shared-memory ring, so
+// every SM keeps tens of KB of reads in flight without holding registers for
+// them. The consumer warps (a channel per NG lanes, two states per lane) compute
+// the step, store the new state straight to the cache and y, and release the
+// stage. Arithmetic and readout order are those of the streaming kernel.
+constexpr int kStrWarps = 8;   // consumer warps
+constexpr int kStrStages = 5;  // ring depth (rows in flight per CTA)
+
+__host__ __device__ inline uint32_t str_stage_bytes(int cb, int N, int tsize) {
+  return uint32_t(cb) * N * 16 + 2u * uint32_t(N) * 4 * tsize;
+}
+
+// Four CTAs per SM (56 registers per thread, 5 x 10 KB stages each): about
+// 200 KB of state reads in flight per SM.
+template <typename T, int NG, bool S_REAL>
+__global__ void __launch_bounds__(32 * (kStrWarps + 1), 4)
+    scan_decode_stream_kernel(const FwdParams p, int rows_per_cta) {
+  constexpr int CPW = 32 / NG;
+  constexpr int CB = kStrWarps * CPW;
+  constexpr unsigned kFull = 0xffffffffu;
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + kStrStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kStrStages);
+  unsigned char* ring = smem + 128;
+  const int N = p.N, D = p.D;
+  const int c0 = blockIdx.x * CB;
+  const int nch = min(CB, D - c0);
+  const int b0 = blockIdx.y * rows_per_cta;
+  const int nrows = min(rows_per_cta, p.B - b0);
+  const uint32_t hbytes = p.h0 != nullptr ? uint32_t(nch) * N * 16 : 0u;
+  const uint32_t bcbytes = uint32_t(N) * 4 * sizeof(T);
+  const uint32_t stage_bytes = str_stage_bytes(CB, N, sizeof(T));
+  const uint32_t off_b = uint32_t(CB) * N * 16;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStrStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kStrWarps);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kStrWarps) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      int issued = 0;
+      bool ok = true;
+      for (int r = 0; r < nrows; ++r) {
+        const int s = r % kStrStages;
+        if (r >= kStrStages) {
+          ok = mbar_wait_bounded(&empty[s], uint32_t(((r / kStrStages) - 1) & 1), p.wait_limit);
+          if (!ok) break;
+        }
+        if (*abort_flag) break;
+        const int64_t b = b0 + r;
+        unsigned char* st = ring + size_t(s) * stage_bytes;
+        mbar_arrive_expect_tx(&full[s], hbytes + 2 * bcbytes);
+        if (hbytes != 0) bulk_g2s(st, p.h0 + (b * D + c0) * int64_t(N) * 4, hbytes, &full[s]);
+        bulk_g2s(st + off_b, static_cast<const T*>(p.Bm) + b * N * 4, bcbytes, &full[s]);
+        bulk_g2s(st + off_b + bcbytes, static_cast<const T*>(p.Cm) + b * N * 4, bcbytes,
+                 &full[s]);
+        issued = r + 1;
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        report_status(p.status, MQC_DEVICE_STATUS_TIMEOUT);
+      }
+      // the CTA must outlive its copies: wait (bounded) for the last ones issued
+      for (int r = issued > kStrStages ? issued - kStrStages : 0; r < issued; ++r)
+        mbar_wait_bounded(&full[r % kStrStages], uint32_t((r / kStrStages) & 1), kDrainPollLimit);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------ consumers
+  const int ng = lane % NG;
+  const int cl = warp * CPW + lane / NG;
+  const bool active = cl < nch;
+  const int c = active ? c0 + cl : c0;
+  const int n0 = ng, n1 = ng + NG;
+  const bool ok0 = active && n0 < N, ok1 = active && n1 < N;
+  LamConst l0{0.f, 0.f, 0.f, 0.f, 0.f}, l1{0.f, 0.f, 0.f, 0.f, 0.f};
+  if (ok0) l0 = make_lam_const(QIO<float>::ld(p.lam + (int64_t(c) * N + n0) * 4));
+  if (ok1) l1 = make_lam_const(QIO<float>::ld(p.lam + (int64_t(c) * N + n1) * 4));
+  const T* gdelta = static_cast<const T*>(p.delta);
+  const T* gs = static_cast<const T*>(p.s);
+  // Delta and the signal of the next row, loaded one row ahead
+  auto load_row = [&](int r, float& dl, float4& sv) {
+    dl = 0.f;
+    sv = f4_zero();
+    if (active && r < nrows) {
+      const int64_t row = int64_t(b0 + r) * D + c;
+      dl = to_f(gdelta[row]);
+      if (S_REAL) sv.x = to_f(gs[row]);
+      else sv = QIO<T>::ld(gs + row * 4);
+    }
+  };
+  float dl_n;
+  float4 sv_n;
+  load_row(0, dl_n, sv_n);
+  const float eps = p.eps;
+  for (int r = 0; r < nrows; ++r) {
+    const int s = r % kStrStages;
+    bool ok = *abort_flag == 0 &&
+              mbar_wait_bounded(&full[s], uint32_t((r / kStrStages) & 1), p.wait_limit);
+    if (!__all_sync(kFull, ok)) {
+      if (lane == 0) {
+        *abort_flag = 1;
+        report_status(p.status, MQC_DEVICE_STATUS_TIMEOUT);
+      }
+      return;
+    }
+    const float dl = dl_n;
+    const float4 sv = sv_n;
+    load_row(r + 1, dl_n, sv_n);
+    const int b = b0 + r;
+    const unsigned char* st = ring + size_t(s) * stage_bytes;
+    const float* sh = reinterpret_cast<const float*>(st) + int64_t(cl) * N * 4;
+    const T* sB = reinterpret_cast<const T*>(st + off_b);
+    const T* sC = reinterpret_cast<const T*>(st + off_b + bcbytes);
+    float4 h[2], Bv[2], Cv[2];
+    h[0] = h[1] = Bv[0] = Bv[1] = Cv[0] = Cv[1] = f4_zero();
+    if (ok0) {
+      if (hbytes != 0) h[0] = QIO<float>::lds(sh + n0 * 4);
+      Bv[0] = QIO<T>::lds(sB + n0 * 4);
+      Cv[0] = QIO<T>::lds(sC + n0 * 4);
+    }
+    if (ok1) {
+      if (hbytes != 0) h[1] = QIO<float>::lds(sh + n1 * 4);
+      Bv[1] = QIO<T>::lds(sB + n1 * 4);
+      Cv[1] = QIO<T>::lds(sC + n1 * 4);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);  // the stage is read: free for the producer
+    const float d2 = dl * dl;
+    float4 hn[2];
+    float4 ya = f4_zero(), yb = f4_zero();
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float4 qv = cayley_from_const(dl, d2, e ? l1 : l0, eps);
+      float4 inj;
+      if (S_REAL)
+        inj = make_float4(sv.x * Bv[e].x, sv.x * Bv[e].y, sv.x * Bv[e].z, sv.x * Bv[e].w);
+      else
+        inj = qmul(Bv[e], sv);
+      hn[e] = qmul_acc(qv, h[e], inj);
+      if (e) yb = qmul_acc(Cv[e], hn[e], yb);
+      else ya = qmul_acc(Cv[e], hn[e], ya);
+    }
+    ya.x += yb.x;
+    ya.y += yb.y;
+    ya.z += yb.z;
+    ya.w += yb.w;
+    const float dsk = active ? __ldg(p.dskip + int64_t(b) * p.dsb + int64_t(c) * p.dsd) : 0.f;
+    reduce_store_y<T, NG>(ya, sv, dsk, ng, active,
+                          static_cast<T*>(p.y) + (int64_t(b) * D + c) * 4);
+    const int64_t hs = (int64_t(b) * D + c) * N;
+    if (ok0) QIO<float>::st(p.hT + (hs + n0) * 4, hn[0]);
+    if (ok1) QIO<float>::st(p.hT + (hs + n1) * 4, hn[1]);
+  }
+}
+
+template <typename T, int NG, bool S_REAL>
+int launch_decode_stream(const FwdParams& p, cudaStream_t st) {
+  constexpr int CB = kStrWarps * (32 / NG);
+  const int nblk = (p.D + CB - 1) / CB;
+  // about eight CTAs per SM in total: rows per CTA so that the grid has that many
+  const int64_t want = int64_t(num_sms()) * 8;
+  int rpc = int((int64_t(p.B) * nblk + want - 1) / want);
+  if (rpc < 4) rpc = 4;
+  if (rpc > p.B) rpc = p.B;
+  const unsigned gy = unsigned((p.B + rpc - 1) / rpc);
+  const size_t smem = 128 + size_t(kStrStages) * str_stage_bytes(CB, p.N, sizeof(T));
+  auto kern = scan_decode_stream_kernel<T, NG, S_REAL>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         int(smem));
+    if (e != cudaSuccess)
+      return fail(MQC_ERR_CUDA, "mqc_ssm_scan_fwd(decode): smem attribute: %s",
+                  cudaGetErrorString(e));
+  }
+  dim3 grid{unsigned(nblk), gy, 1u};
+  kern<<<grid, 32 * (kStrWarps + 1), smem, st>>>(p, rpc);
+  return check_launch("mqc_ssm_scan_fwd(decode stream)");
+}
+
+template <typename T, bool S_REAL>
+int dispatch_decode_stream_t(const FwdParams& p, cudaStream_t st) {
+  const int need = (p.N + 1) / 2;
+  int ng = 1;
+  while (ng < need) ng <<= 1;
+  switch (ng) {
+    case 1: return launch_decode_stream<T, 1, S_REAL>(p, st);
+    case 2: return launch_decode_stream<T, 2, S_REAL>(p, st);
+    case 4: return launch_decode_stream<T, 4, S_REAL>(p, st);
+    case 8: return launch_decode_stream<T, 8, S_REAL>(p, st);
+    case 16: return launch_decode_stream<T, 16, S_REAL>(p, st);
+    default: return launch_decode_stream<T, 32, S_REAL>(p, st);
+  }
+}
+
 }  // namespace
 
-// Up to 32 batch rows: measured at config-3 channel and state sizes, this
-// kernel takes 4.0 / 13.2 us per step at 4 / 16 rows against 4.4 / 13.8 us on
-// the streaming kernel, and 63.5 / 250 us at 64 / 256 rows against 62 / 242 us
-// (there the state stream, not Lambda, limits both).
+// Up to 32 batch rows: the row-blocked kernel (measured at config-3 channel and
+// state sizes: 4.0 / 13.2 us per step at 4 / 16 rows, against 4.4 / 13.8 us on
+// the general streaming kernel); more rows: the state-streaming kernel.
 bool decode_serves(const FwdParams& p) {
-  return p.T == 1 && p.B <= 32 && p.N <= 64 && p.hT != nullptr && p.ckpt == nullptr &&
-         p.pout == nullptr;
+  return p.T == 1 && p.N <= 64 && p.hT != nullptr && p.ckpt == nullptr && p.pout == nullptr;
 }
 
 int dispatch_decode(const FwdParams& p, int dtype, bool s_real, cudaStream_t st) {
+  if (p.B > 32) {  // the state-streaming kernel
+    if (dtype == MQC_DTYPE_F32)
+      return s_real ? dispatch_decode_stream_t<float, true>(p, st)
+                    : dispatch_decode_stream_t<float, false>(p, st);
+    return s_real ? dispatch_decode_stream_t<__nv_bfloat16, true>(p, st)
+                  : dispatch_decode_stream_t<__nv_bfloat16, false>(p, st);
+  }
   if (dtype == MQC_DTYPE_F32)
     return s_real ? dispatch_decode_t<float, true>(p, st) : dispatch_decode_t<float, false>(p, st);
   return s_real ? dispatch_decode_t<__nv_bfloat16, true>(p, st)

@@ -310,6 +310,12 @@ def test_decode_step_with_state_cache(shared, dtype):
     (6, 50, 64, False, torch.float32),
     (9, 40, 64, True, torch.bfloat16),
     (3, 21, 18, False, torch.bfloat16),  # bf16 channel-shared B/C needs an even N
+    # more than 32 rows: the state-streaming kernel (ragged row ranges and
+    # channel blocks)
+    (40, 37, 64, True, torch.float32),
+    (33, 13, 3, False, torch.float32),
+    (70, 50, 64, True, torch.bfloat16),
+    (48, 100, 16, False, torch.float32),
 ], ids=lambda c: "B{}D{}N{}{}{}".format(c[0], c[1], c[2], "x" if c[3] else "S",
                                       "f32" if c[4] == torch.float32 else "bf16"))
 def test_decode_kernel_odd_shapes(case):
