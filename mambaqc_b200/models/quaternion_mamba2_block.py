@@ -19,11 +19,11 @@ between them runs in ``libmambaqc_b200.so``:
 * the causal conv + SiLU, read in place from the in_proj output;
 * the step sizes and gated signal (softplus, sigmoid gate);
 * the scan, the quaternion LayerNorm, and the output gate + residual.
-Each has a forward and a backward kernel. Two tcgen05 fusions are opt-in
-(``fused_norm_out_proj``: the LayerNorm as the operand prologue of the output
-projection's GEMM; ``fused_bc_proj``: the B/C projections computed inside the
-scan kernel), since at the config-4 block shape both measure slower than the
-unfused kernels.
+Each has a forward and a backward kernel. Two tcgen05 fusions replace pairs of
+ops under bf16 autocast, both opt-in because at the config-4 block shape they
+still measure slower than the unfused kernels: ``fused_norm_out_proj`` (the
+LayerNorm as the operand prologue of the output projection's GEMM) and
+``fused_bc_proj`` (the B/C projections computed inside the scan kernel).
 """
 
 from __future__ import annotations
@@ -77,9 +77,11 @@ class QuaternionMamba2Block(nn.Module):
         # fused forward measures slower than cuBLAS projections + the scan.
         self.fused_bc_proj = False
         # Under bf16 autocast, apply the LayerNorm inside the output projection's
-        # GEMM (``quaternion_layer_norm_linear``). Off by default: at the config-4
-        # block shape it measures slower than the LayerNorm kernel + cuBLAS.
-        self.fused_norm_out_proj = False
+        # GEMM (``quaternion_layer_norm_linear``): True, False, or "auto" (fused
+        # when no gradient is needed). Off by default: at the config-4 block
+        # shape the fused forward measures 0.14-0.18 ms against 0.11-0.14 ms
+        # for the LayerNorm kernel + cuBLAS on the same box.
+        self.fused_norm_out_proj: bool | str = False
 
     def ssm_lambda(self) -> torch.Tensor:
         """Lambda [d_inner, d_state, 4] = (-softplus(alpha), tanh(imag)) (block.py:206-212)."""
@@ -102,13 +104,18 @@ class QuaternionMamba2Block(nn.Module):
 
     def _norm_out_proj(self, y_quat: torch.Tensor) -> torch.Tensor:
         """``out_proj(norm(y_quat))`` (block lines 154-157). With
-        ``fused_norm_out_proj`` set, under bf16 autocast -- where the projection
+        ``fused_norm_out_proj`` (True, or "auto" when no gradient is needed),
+        under bf16 autocast -- where the projection
         would run in bf16 on the LayerNorm's bf16 output -- the LayerNorm is
         applied inside the projection GEMM (``quaternion_layer_norm_linear``), so
         the normalised activations are never written to memory; otherwise the
         two modules run in turn."""
         w = self.out_proj.weight
-        fusable = (self.fused_norm_out_proj and y_quat.is_cuda and
+        want = self.fused_norm_out_proj
+        if want == "auto":
+            want = not (torch.is_grad_enabled() and
+                        (y_quat.requires_grad or w.requires_grad))
+        fusable = (bool(want) and y_quat.is_cuda and
                    y_quat.dtype == torch.bfloat16 and
                    torch.is_autocast_enabled("cuda") and
                    torch.get_autocast_dtype("cuda") == torch.bfloat16 and

@@ -3,8 +3,9 @@
 whose operand prologue is the LayerNorm).
 
 Checked against (a) the unfused pair -- the LayerNorm kernel's bf16 output fed
-to cuBLAS -- which sees the same bf16 operands, so only the GEMM's summation
-order and the output rounding differ (rel-L2 < 4e-3); and (b) the fp64 oracle
+to cuBLAS -- whose bf16 operands differ only where the fused prologue's
+Newton-refined reciprocal rounds differently, so the GEMM's summation order and
+the output rounding dominate (rel-L2 < 4e-3); and (b) the fp64 oracle
 (LayerNorm restated from the reference, then the linear map), within the bf16
 tolerance of the contract (2e-2). Gradients of every input against torch
 autograd through the unfused pair."""
