@@ -307,11 +307,13 @@ template <typename T, int NG, bool S_REAL>
 int launch_decode_stream(const FwdParams& p, cudaStream_t st) {
   constexpr int CB = kStrWarps * (32 / NG);
   const int nblk = (p.D + CB - 1) / CB;
-  // about eight CTAs per SM in total: rows per CTA so that the grid has that many
-  const int64_t want = int64_t(num_sms()) * 8;
-  int rpc = int((int64_t(p.B) * nblk + want - 1) / want);
-  if (rpc < 4) rpc = 4;
-  if (rpc > p.B) rpc = p.B;
+  // one resident wave (four CTAs per SM): as many row ranges per channel block
+  // as fit beside the blocks, so no SM waits on a partial second wave
+  const int64_t slots = int64_t(num_sms()) * 4;
+  int64_t ranges = slots / nblk;
+  if (ranges < 1) ranges = 1;
+  if (ranges > p.B) ranges = p.B;
+  const int rpc = int((p.B + ranges - 1) / ranges);
   const unsigned gy = unsigned((p.B + rpc - 1) / rpc);
   const size_t smem = 128 + size_t(kStrStages) * str_stage_bytes(CB, p.N, sizeof(T));
   auto kern = scan_decode_stream_kernel<T, NG, S_REAL>;
