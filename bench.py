@@ -69,6 +69,9 @@ def parse_args():
                     help="--only perchannel_fwd_bwd: batch rows (a small case for profilers)")
     ap.add_argument("--prof-seq", type=int, default=None,
                     help="--only perchannel_fwd_bwd: sequence length (a small case for profilers)")
+    ap.add_argument("--prof-channels", type=int, default=None,
+                    help="--workload fused_parts: scan channels of the projections (a small "
+                         "case for profilers)")
     ap.add_argument("--segments", type=int, default=4,
                     help="config5 on >1 GPU: time segments whose all-gather overlaps the "
                          "scan of the next segment")
@@ -80,7 +83,7 @@ def parse_args():
                     help="config5 on >1 GPU: channel shards with y all-gathered, or time "
                          "shards exchanging range summaries (y then all-gathered too)")
     ap.add_argument("--workload", choices=["config3", "config5", "config2", "decode", "block_glue",
-                                           "config4_block"],
+                                           "config4_block", "fused_parts"],
                     default="config3",
                     help="config5: B=1, T=65536, D=1536, N=64, bf16, channel-sharded over the "
                          "GPUs with an NCCL all-gather of y (strong scaling)")
@@ -1212,6 +1215,93 @@ def run_block_glue(args, world, rank, local):
     return 0
 
 
+def time_fused_parts(bsz, seqlen, din, dmod, nst, chans, dev, world, stream, steps, seed=1):
+    """The two halves of the block fused into tcgen05 kernels here, each timed
+    against the unfused form it replaces (forward, bf16): the B/C projections +
+    per-channel scan over ``chans`` channels (``bc_proj_scan`` against cuBLAS
+    projections + ``ssm_scan_cayley``), and the LayerNorm + output projection
+    (``quaternion_layer_norm_linear`` against the LayerNorm kernel + cuBLAS).
+    Returns ({name: ms}, {name: TFLOP/s of the projections})."""
+    from mambaqc_b200.kernels import quaternion_layer_norm_fused, ssm_scan_cayley
+    from mambaqc_b200.kernels.bc_proj_scan import bc_proj_scan
+    from mambaqc_b200.kernels.quaternion_norm import quaternion_layer_norm_linear
+
+    g = torch.Generator(device=dev).manual_seed(seed)
+    bf = torch.bfloat16
+    xa3 = torch.randn(bsz, seqlen, din, generator=g, device=dev).to(bf)
+    std = (2.0 / (din + chans * nst)) ** 0.5
+    wb = (torch.randn(chans * nst * 4, din, generator=g, device=dev) * std).to(bf)
+    wc = (torch.randn(chans * nst * 4, din, generator=g, device=dev) * std).to(bf)
+    dl = torch.nn.functional.softplus(torch.randn(bsz, seqlen, chans, generator=g, device=dev)
+                                      - 3.0).to(bf)
+    sg = torch.randn(bsz, seqlen, chans, generator=g, device=dev).to(bf)
+    lam = torch.empty(chans, nst, 4, device=dev)
+    lam[..., 0] = -0.01
+    lam[..., 1:] = 0.3
+    dsk = torch.ones(chans, device=dev)
+    yq = torch.randn(bsz, seqlen, din, 4, generator=g, device=dev).to(bf)
+    gam = torch.ones(din, device=dev)
+    bet = torch.zeros(din, 4, device=dev)
+    wo = (torch.randn(dmod, 4 * din, generator=g, device=dev) * (4 * din) ** -0.5).to(bf)
+
+    def bc_fused():
+        with torch.no_grad():
+            bc_proj_scan(xa3, wb, wc, dl, lam, sg, dsk)
+
+    def bc_unfused():
+        with torch.no_grad():
+            Bq = (xa3 @ wb.t()).view(bsz, seqlen, chans, nst, 4)
+            Cq = (xa3 @ wc.t()).view(bsz, seqlen, chans, nst, 4)
+            ssm_scan_cayley(dl, lam, Bq, Cq, sg, dsk)
+
+    def ln_fused():
+        with torch.no_grad():
+            quaternion_layer_norm_linear(yq, gam, bet, wo)
+
+    def ln_unfused():
+        with torch.no_grad():
+            quaternion_layer_norm_fused(yq, gam, bet).flatten(-2) @ wo.t()
+
+    parts = {}
+    for name, f in (("bc_proj_scan_fused", bc_fused), ("bc_proj_scan_unfused", bc_unfused),
+                    ("ln_out_proj_fused", ln_fused), ("ln_out_proj_unfused", ln_unfused)):
+        parts[name] = max_over_ranks(timed(f, 4 * steps, 3, world, stream) / (4 * steps), world,
+                                     dev)
+    bc_flops = 2 * 2 * bsz * seqlen * din * chans * nst * 4
+    ln_flops = 2 * bsz * seqlen * (4 * din) * dmod
+    tflops = {k: (bc_flops if k.startswith("bc") else ln_flops) / (v / 1e3) / 1e12
+              for k, v in parts.items()}
+    return parts, tflops
+
+
+def run_fused_parts(args, world, rank, local):
+    """`--workload fused_parts`: the tcgen05 fusions against their unfused forms
+    at the config-4 block shape (B=4, T=2048, d_inner 1536, d_state 64, d_model
+    768), or a smaller case with --prof-batch / --prof-seq / --prof-channels
+    (the number of scan channels the projections produce)."""
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    bsz = args.prof_batch or 4
+    seqlen = args.prof_seq or 2048
+    chans = args.prof_channels or 1536
+    steps = max(1, min(args.steps, 10))
+    parts, tflops = time_fused_parts(bsz, seqlen, 1536, 768, 64, chans, dev, world, stream, steps,
+                                     seed=1 + rank)
+    if rank == 0:
+        line = {
+            "metric": "tcgen05 fusions of the block against their unfused forms (forward ms)",
+            "value": parts["bc_proj_scan_fused"], "unit": "ms", "n_gpus": world,
+            "steps": 4 * steps, "warmup": 3, "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+            "config": {"workload": "fused_parts", "batch": bsz, "seq_len": seqlen,
+                       "d_inner": 1536, "d_model": 768, "d_state": 64, "scan_channels": chans},
+            "parts_ms": parts, "parts_tflops": tflops,
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_config4_block(args, world, rank, local):
     """One block of the config-4 base preset (d_model 768, d_state 64, d_inner
     1536) at B=4 per GPU, T=2048: forward + loss + backward under bf16 autocast,
@@ -1268,51 +1358,9 @@ def run_config4_block(args, world, rank, local):
     ms_fwd = {k: max_over_ranks(timed(fwd(k == "fused"), steps, 3, world, stream) / steps,
                                 world, dev) for k in ("unfused", "fused")}
 
-    # the two halves of the block that are fused into tcgen05 kernels here, each
-    # against the unfused form it replaces (forward, bf16, the block's shapes)
-    from mambaqc_b200.kernels.bc_proj_scan import bc_proj_scan
-    from mambaqc_b200.kernels import quaternion_layer_norm_fused, ssm_scan_cayley
-    from mambaqc_b200.kernels.quaternion_norm import quaternion_layer_norm_linear
-    din = 2 * dmod
-    xa3 = xa.view(bsz, seqlen, din)
-    wc = blk.C_proj.weight.detach().to(torch.bfloat16)
-    dl = torch.nn.functional.softplus(torch.randn(bsz, seqlen, din, generator=g, device=dev) - 3.0
-                                      ).bfloat16()
-    sg = torch.randn(bsz, seqlen, din, generator=g, device=dev).bfloat16()
-    lam = torch.empty(din, nst, 4, device=dev)
-    lam[..., 0] = -0.01
-    lam[..., 1:] = 0.3
-    dsk = torch.ones(din, device=dev)
-    yq = torch.randn(bsz, seqlen, din, 4, generator=g, device=dev).bfloat16()
-    gam = torch.ones(din, device=dev)
-    bet = torch.zeros(din, 4, device=dev)
-    wo = blk.out_proj.weight.detach().to(torch.bfloat16)
+    parts, parts_tflops = time_fused_parts(bsz, seqlen, 2 * dmod, dmod, nst, 2 * dmod, dev, world,
+                                           stream, steps, seed=1 + rank)
 
-    def bc_fused():
-        with torch.no_grad():
-            bc_proj_scan(xa3, wb, wc, dl, lam, sg, dsk)
-
-    def bc_unfused():
-        with torch.no_grad():
-            Bq = (xa3 @ wb.t()).view(bsz, seqlen, din, nst, 4)
-            Cq = (xa3 @ wc.t()).view(bsz, seqlen, din, nst, 4)
-            ssm_scan_cayley(dl, lam, Bq, Cq, sg, dsk)
-
-    def ln_fused():
-        with torch.no_grad():
-            quaternion_layer_norm_linear(yq, gam, bet, wo)
-
-    def ln_unfused():
-        with torch.no_grad():
-            quaternion_layer_norm_fused(yq, gam, bet).flatten(-2) @ wo.t()
-
-    parts = {}
-    for name, f in (("bc_proj_scan_fused", bc_fused), ("bc_proj_scan_unfused", bc_unfused),
-                    ("ln_out_proj_fused", ln_fused), ("ln_out_proj_unfused", ln_unfused)):
-        parts[name] = max_over_ranks(timed(f, 4 * steps, 3, world, stream) / (4 * steps), world,
-                                     dev)
-    bc_flops = 2 * 2 * bsz * seqlen * din * din * nst * 4
-    ln_flops = 2 * bsz * seqlen * (4 * din) * dmod
     peaks, peak_kind = measured_peaks()
     din = 2 * dmod
     proj_flops = 2 * 3 * 2 * (bsz * seqlen) * din * (din * nst * 4)
@@ -1336,11 +1384,7 @@ def run_config4_block(args, world, rank, local):
             "bf16_peak_source": f"MEASURED_PEAKS.json ({peak_kind})",
             "forward_ms": {"unfused_bc_proj": ms_fwd["unfused"], "fused_bc_proj": ms_fwd["fused"]},
             "fused_parts_ms": parts,
-            "fused_parts_tflops": {
-                "bc_proj_scan_fused": bc_flops / (parts["bc_proj_scan_fused"] / 1e3) / 1e12,
-                "bc_proj_scan_unfused": bc_flops / (parts["bc_proj_scan_unfused"] / 1e3) / 1e12,
-                "ln_out_proj_fused": ln_flops / (parts["ln_out_proj_fused"] / 1e3) / 1e12,
-                "ln_out_proj_unfused": ln_flops / (parts["ln_out_proj_unfused"] / 1e3) / 1e12},
+            "fused_parts_tflops": parts_tflops,
         }
         print(json.dumps(line), flush=True)
     return 0
@@ -1360,6 +1404,8 @@ def main():
             return run_config2(args, world, rank, local)
         if args.workload == "decode":
             return run_decode(args, world, rank, local)
+        if args.workload == "fused_parts":
+            return run_fused_parts(args, world, rank, local)
         if args.workload == "block_glue":
             return run_block_glue(args, world, rank, local)
         if args.workload == "config4_block":
