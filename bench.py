@@ -77,8 +77,9 @@ def parse_args():
                          "scan of the next segment")
     ap.add_argument("--decode-batch", type=int, default=4,
                     help="decode workload: sequences decoded together per GPU")
-    ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
-                    help="config5 on >1 GPU: how y is assembled on every rank")
+    ap.add_argument("--gather", choices=["peer", "nccl", "multicast"], default="peer",
+                    help="config5 on >1 GPU: how y is assembled on every rank (multicast: "
+                         "NVLink SHARP multimem stores, where the platform has them)")
     ap.add_argument("--shard", choices=["channel", "time"], default="channel",
                     help="config5 on >1 GPU: channel shards with y all-gathered, or time "
                          "shards exchanging range summaries (y then all-gathered too)")
@@ -736,11 +737,17 @@ def config5_measure(args, world, rank, local, gather="peer"):
         ms_scan_max = max_over_ranks(ms_scan, world, dev)
     del out
     elems = C5_SEQ * CHANNELS * STATE
-    how = ("every y value stored by the scan kernel into all ranks' outputs over NVLink "
-           "(mqc_ssm_scan_fwd_chunked_peer, CUDA IPC buffers), ordered by two 1-element NCCL "
-           "all-reduces" if gather == "peer"
-           else "NCCL all_gather_into_tensor of y per time segment plus a permute, overlapped "
-                "with the scan of the next segment")
+    used = gather
+    how = {"multicast": "every y quaternion stored once by the scan kernel with multimem.st to "
+                        "the multicast address of a symmetric-memory output (NVLink SHARP: "
+                        "NVSwitch writes all ranks' buffers; "
+                        "mqc_ssm_scan_fwd_chunked_multicast), ordered by two 1-element NCCL "
+                        "all-reduces",
+           "peer": "every y value stored by the scan kernel into all ranks' outputs over NVLink "
+                   "(mqc_ssm_scan_fwd_chunked_peer, CUDA IPC buffers), ordered by two "
+                   "1-element NCCL all-reduces",
+           "nccl": "NCCL all_gather_into_tensor of y per time segment plus a permute, "
+                   "overlapped with the scan of the next segment"}.get(used, used)
     return {
         "value": C5_SEQ / (ms_max / 1e3), "unit": "tokens/s", "ms_per_step": ms_max,
         "steps": steps, "scaling": "strong", "n_gpus": world,

@@ -317,6 +317,19 @@ MQC_API int mqc_ssm_scan_fwd_chunked_peer(const mqc_ssm_scan_args* args, int64_t
                                           void* const* ypeer, int npeer, int64_t ch_total,
                                           int64_t ch_off, void* stream);
 
+/* mqc_ssm_scan_fwd_chunked_peer with one multicast output: ymc is the multicast
+ * address of a [batch, seq_len, ch_total, 4] buffer (dtype) bound on every rank
+ * (an NVLink SHARP multicast object, e.g. the multicast_ptr of a torch
+ * symmetric-memory tensor). The kernel gathers each y quaternion on one lane and
+ * stores it once with multimem.st; NVSwitch writes it into every rank's buffer,
+ * so one store replaces one per rank. d_state in (16, 256]; the other rules are
+ * those of mqc_ssm_scan_fwd_chunked_peer. No counterpart in the reference, which
+ * has no multi-GPU code. */
+MQC_API int mqc_ssm_scan_fwd_chunked_multicast(const mqc_ssm_scan_args* args, int64_t nchunks,
+                                               void* workspace, size_t workspace_bytes,
+                                               void* ymc, int64_t ch_total, int64_t ch_off,
+                                               void* stream);
+
 /* Copies a time segment of this rank's channel shard, src [batch, seg_len,
  * ch_local, 4] (dtype, contiguous), into rows t_off .. t_off+seg_len-1 and
  * channels ch_off .. ch_off+ch_local-1 of each of the ndst (<= 8) outputs

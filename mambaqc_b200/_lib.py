@@ -138,6 +138,8 @@ _SIGNATURES.update({
     "mqc_qln_linear_fwd": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                            _c_void_p, _c_void_p, _i64, _i64, _i64, _f32, _c_void_p, _c_void_p],
     "mqc_bc_proj_scan_fwd": [ctypes.POINTER(BcProjScanArgs), _c_void_p],
+    "mqc_ssm_scan_fwd_chunked_multicast": [ctypes.POINTER(SsmScanArgs), _i64, _c_void_p,
+                                           ctypes.c_size_t, _c_void_p, _i64, _i64, _c_void_p],
     "mqc_channel_push": [_c_void_p, ctypes.POINTER(_c_void_p), _i32, _i64, _i64, _i64, _i64,
                          _i64, _i64, _i64, _i32, _c_void_p],
 })

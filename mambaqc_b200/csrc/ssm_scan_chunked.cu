@@ -98,6 +98,7 @@ struct PeerSpec {
   void* const* ptrs;
   int n;
   int64_t ch_total, ch_off;
+  bool mc;  // ptrs[0] is a multicast address (n == 1)
 };
 
 // Pass 2 (or the whole scan when nchunks == 1): mqc_ssm_scan_fwd, or with peer
@@ -111,6 +112,7 @@ int scan_pass(const mqc_ssm_scan_args* a2, const PeerSpec* peer, void* stream) {
   for (int r = 0; r < peer->n; ++r) p.ypeer[r] = peer->ptrs[r];
   p.y_ld = peer->ch_total * 4;
   p.y_coff = peer->ch_off * 4;
+  p.peer_mc = peer->mc ? 1 : 0;
   return dispatch_shared_packed(p, a2->dtype, (a2->flags & MQC_SSM_S_REAL) != 0,
                                 as_stream(stream));
 }
@@ -182,7 +184,41 @@ extern "C" int mqc_ssm_scan_fwd_chunked_peer(const mqc_ssm_scan_args* a, int64_t
                 "%s: output %d null or not %d-byte aligned", name, r, int(qa));
   mqc_ssm_scan_args a1 = *a;
   a1.y = ypeer[0];  // validated like y; the kernel writes every ypeer[r]
-  const PeerSpec peer{ypeer, npeer, ch_total, ch_off};
+  const PeerSpec peer{ypeer, npeer, ch_total, ch_off, false};
+  return chunked_impl(&a1, nchunks, workspace, workspace_bytes, &peer, stream);
+}
+
+extern "C" int mqc_ssm_scan_fwd_chunked_multicast(const mqc_ssm_scan_args* a, int64_t nchunks,
+                                                  void* workspace, size_t workspace_bytes,
+                                                  void* ymc, int64_t ch_total, int64_t ch_off,
+                                                  void* stream) {
+  clear_error();
+  const char* name = "mqc_ssm_scan_fwd_chunked_multicast";
+  MQC_REQUIRE(a != nullptr && ymc != nullptr, MQC_ERR_INVALID_VALUE, "%s: null pointer", name);
+  MQC_REQUIRE((a->flags & MQC_SSM_BC_SHARED) && !(a->flags & MQC_SSM_Q_GIVEN), MQC_ERR_UNSUPPORTED,
+              "%s: channel-shared B/C and the fused Cayley form only", name);
+  // the packed kernel gathers a quaternion from four lanes of its channel: at
+  // least four lanes per channel, i.e. d_state above 16
+  MQC_REQUIRE(a->d_state > 16 && a->d_state <= 256, MQC_ERR_UNSUPPORTED,
+              "%s: d_state must be in (16, 256] (got %lld)", name, (long long)a->d_state);
+  const char* impl = getenv("MQC_SCAN_IMPL");
+  MQC_REQUIRE(impl == nullptr || impl[0] == '\0', MQC_ERR_UNSUPPORTED,
+              "%s: needs the packed kernel (MQC_SCAN_IMPL is set)", name);
+  MQC_REQUIRE(a->ckpt == nullptr && a->dskip_sb == 0 && a->dskip_st == 0, MQC_ERR_UNSUPPORTED,
+              "%s: no checkpoints, per-channel skip weight only", name);
+  MQC_REQUIRE(nchunks >= 1 && a->seq_len % nchunks == 0 && a->seq_len / nchunks > kShortScan,
+              MQC_ERR_UNSUPPORTED, "%s: seq_len / nchunks must be an integer above %d", name,
+              kShortScan);
+  MQC_REQUIRE(ch_off >= 0 && ch_off + a->channels <= ch_total, MQC_ERR_INVALID_VALUE,
+              "%s: channels [%lld, +%lld) outside %lld", name, (long long)ch_off,
+              (long long)a->channels, (long long)ch_total);
+  const uintptr_t qa = a->dtype == MQC_DTYPE_F32 ? 16 : 8;
+  MQC_REQUIRE(aligned(ymc, qa), MQC_ERR_MISALIGNED, "%s: output not %d-byte aligned", name,
+              int(qa));
+  mqc_ssm_scan_args a1 = *a;
+  a1.y = ymc;  // validated like y; the kernel writes it only with multimem stores
+  void* const ptrs[1] = {ymc};
+  const PeerSpec peer{ptrs, 1, ch_total, ch_off, true};
   return chunked_impl(&a1, nchunks, workspace, workspace_bytes, &peer, stream);
 }
 

@@ -45,6 +45,10 @@ struct FwdParams {
   int npeer;
   int64_t y_ld, y_coff;
   void* ypeer[8];
+  // With peer_mc set (npeer == 1), ypeer[0] is the multicast address of a
+  // buffer bound on every rank (NVLink SHARP): each y quaternion is stored once
+  // with multimem.st and the switch writes it to all ranks.
+  int peer_mc;
 };
 constexpr int kMaxPeerOutputs = 8;
 

@@ -72,6 +72,20 @@ __device__ __forceinline__ void st1_pred(__nv_bfloat16* p, float v, bool pred) {
                : "memory");
 }
 
+// One multimem store of a y quaternion to a multicast address: NVSwitch writes
+// it into the buffer of every rank bound to the multicast object.
+__device__ __forceinline__ void mc_store_q(float* p, float4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p),
+               "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void mc_store_q(__nv_bfloat16* p, float4 v) {
+  const uint2 u = QIO<__nv_bfloat16>::pack(v);
+  asm volatile("multimem.st.relaxed.sys.global.v2.f32 [%0], {%1, %2};" ::"l"(p), "r"(u.x),
+               "r"(u.y)
+               : "memory");
+}
+
 // reduce_store_y (ssm_scan_common.cuh) with predicated stores: sums the partial
 // readouts `a` over the NG lanes of a channel (reduce-scatter: afterwards lane ng
 // holds component ng & 3), adds dsk * s and stores y[t, c, 0..3].
@@ -481,11 +495,29 @@ __global__ void __launch_bounds__(pk_max_threads(G), 1)
                                            int64_t(t0 + tt) * p.dst + int64_t(c) * p.dsd)
                                    : 0.f;
         if constexpr (PEER) {
-          reduce_y_pk<NG>(yv, sv, dsk, ng, active, [&](int comp, float v, bool pred) {
+          bool mc_done = false;
+          if constexpr (NG >= 4) {
+            if (p.peer_mc) {
+              // lanes ng = 0..3 of the channel hold components 0..3 after the
+              // reduction: gather them on lane 0 for one multicast store
+              float mv = 0.f;
+              reduce_y_pk<NG>(yv, sv, dsk, ng, active,
+                              [&](int, float v, bool) { mv = v; });
+              const int base = lane - ng;
+              const float4 q = make_float4(__shfl_sync(kFull, mv, base),
+                                           __shfl_sync(kFull, mv, base + 1),
+                                           __shfl_sync(kFull, mv, base + 2),
+                                           __shfl_sync(kFull, mv, base + 3));
+              if (ng == 0 && active) mc_store_q(static_cast<T*>(p.ypeer[0]) + yrow_peer, q);
+              mc_done = true;
+            }
+          }
+          if (!mc_done)
+            reduce_y_pk<NG>(yv, sv, dsk, ng, active, [&](int comp, float v, bool pred) {
 #pragma unroll
-            for (int r = 0; r < kMaxPeerOutputs; ++r)
-              if (r < p.npeer) st1_pred(static_cast<T*>(p.ypeer[r]) + yrow_peer + comp, v, pred);
-          });
+              for (int r = 0; r < kMaxPeerOutputs; ++r)
+                if (r < p.npeer) st1_pred(static_cast<T*>(p.ypeer[r]) + yrow_peer + comp, v, pred);
+            });
         } else {
           reduce_store_y_pk<T, NG>(yv, sv, dsk, ng, active, yrow);
         }

@@ -131,6 +131,7 @@ def release_peer_outputs() -> None:
     """Closes every cached PeerOutput. Collective: every rank of each buffer's
     group calls it, before the process group is destroyed. Ranks first unmap
     their peers' buffers, then (after a barrier) free their own."""
+    _mc_outputs.clear()
     if not _peer_outputs:
         return
     torch.cuda.synchronize()
@@ -202,6 +203,16 @@ def ssm_scan_cayley_channel_sharded(delta: torch.Tensor, Lambda: torch.Tensor, B
     result before it is overwritten) and one on exit (every store has landed).
     The returned tensor is this rank's peer buffer, valid until the next call
     with the same shape.
+
+    ``gather="multicast"`` (CUDA, NVSwitch with NVLink SHARP): the output is a
+    symmetric-memory tensor bound to a multicast object on every rank, and the
+    scan kernel stores each y quaternion once, with ``multimem.st`` to the
+    multicast address (``mqc_ssm_scan_fwd_chunked_multicast``); the switch
+    writes it into every rank's buffer. Needs the fused conditions above,
+    d_state > 16 and a platform with multicast (else RuntimeError). Measured on
+    config 5 at 2 GPUs it is much slower than ``"peer"`` (60.2 ms per step
+    against 12.7 ms): one 8- or 16-byte multimem store per channel and step is
+    far below the transfer size the switch's multicast serves well.
     """
     # the scan kernel itself writes every rank's output: channel-shared B/C, the
     # default scan, a per-channel skip weight, inputs that need no gradient
@@ -223,6 +234,17 @@ def ssm_scan_cayley_channel_sharded(delta: torch.Tensor, Lambda: torch.Tensor, B
         raise ValueError(f"seq_len {seqlen} does not split into {segments} equal segments")
     seg = seqlen // segments
     on_cuda = delta.is_cuda
+    if gather == "multicast":
+        if not on_cuda:
+            raise ValueError("gather='multicast' needs CUDA tensors")
+        ds = Lambda.shape[1]
+        mc = None
+        if fused_peer and 16 < ds <= 256:
+            mc = _mc_output((bsz, seqlen, world * dl, 4), delta.dtype, delta.device, group)
+        if mc is None or not mc.mc_ptr:
+            raise RuntimeError("gather='multicast': no multicast support on this platform, or "
+                               "not the fused form (channel-shared B/C, d_state > 16, no grad)")
+        return _channel_sharded_mc_fused(delta, Lambda, B, C, S, D, group, time_chunks, mc)
     if gather == "peer":
         if not on_cuda:
             raise ValueError("gather='peer' needs CUDA tensors")
@@ -230,7 +252,7 @@ def ssm_scan_cayley_channel_sharded(delta: torch.Tensor, Lambda: torch.Tensor, B
             return _channel_sharded_peer_fused(delta, Lambda, B, C, S, D, group, time_chunks)
         return _channel_sharded_peer(delta, Lambda, B, C, S, D, group, scan_fn, segments)
     if gather != "nccl":
-        raise ValueError(f"gather must be 'nccl' or 'peer', got {gather!r}")
+        raise ValueError(f"gather must be 'nccl', 'peer' or 'multicast', got {gather!r}")
     y = torch.empty((bsz, seqlen, world * dl, 4), dtype=delta.dtype, device=delta.device)
     # ranks' outputs concatenated along dim 0 (the form every backend accepts),
     # double-buffered across segments
@@ -312,6 +334,56 @@ def _channel_sharded_peer_fused(delta, Lambda, B, C, S, D, group, time_chunks):
                       peer=(out.ptrs, world * dl, rank * dl))
     dist.all_reduce(flag, group=group)  # every rank's stores have landed
     return out.tensor
+
+
+class McOutput:
+    """A [B, T, channels, 4] output in symmetric memory on every rank of ``group``
+    (``torch.distributed._symmetric_memory``), with the multicast address of the
+    buffer set when the platform supports NVLink SHARP multicast (``mc_ptr``,
+    0 otherwise). ``tensor`` is this rank's buffer."""
+
+    def __init__(self, shape: tuple, dtype: torch.dtype, device: torch.device, group=None):
+        import torch.distributed._symmetric_memory as symm
+        self.group = group
+        self.tensor = symm.empty(shape, dtype=dtype, device=device)
+        self.handle = symm.rendezvous(self.tensor,
+                                      group if group is not None else dist.group.WORLD)
+        ok = bool(self.handle.has_multicast_support())
+        self.mc_ptr = int(self.handle.multicast_ptr) if ok else 0
+
+
+_mc_outputs: dict = {}
+
+
+def _mc_output(shape, dtype, device, group) -> McOutput | None:
+    key = (tuple(shape), dtype, str(device), id(group))
+    out = _mc_outputs.get(key)
+    if out is None:
+        try:
+            out = McOutput(shape, dtype, device, group)
+        except Exception:  # no symmetric-memory support: callers fall back to "peer"
+            out = None
+        _mc_outputs[key] = out
+    return out
+
+
+def _channel_sharded_mc_fused(delta, Lambda, B, C, S, D, group, time_chunks, mc: McOutput):
+    from .ssm_fused import _run_scan_chunked, auto_time_chunks
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    bsz, seqlen, dl = delta.shape[:3]
+    ds = Lambda.shape[1]
+    dev = delta.device
+    nc = (auto_time_chunks(bsz, seqlen, dl, ds, dev) if time_chunks == "auto"
+          else int(time_chunks))
+    if nc > 1 and seqlen // nc <= 8:
+        nc = 1
+    flag = _barrier_flag(dev)
+    dist.all_reduce(flag, group=group)  # every rank is done with the previous result
+    _run_scan_chunked(delta, Lambda, B, C, S, D, None, 1e-6, nc, False,
+                      peer=((mc.mc_ptr,), world * dl, rank * dl, True))
+    dist.all_reduce(flag, group=group)  # every rank's stores have landed
+    return mc.tensor
 
 
 _flags: dict[int, torch.Tensor] = {}

@@ -216,7 +216,7 @@ def _run_scan_chunked(delta, Lam, B, C, S, D, h0, eps, nchunks, return_final_sta
                       peer=None):
     """Time-parallel forward (``mqc_ssm_scan_fwd_chunked``); no autograd.
 
-    ``peer = (ptrs, ch_total, ch_off)``: the channel-sharded form
+    ``peer = (ptrs, ch_total, ch_off[, multicast])``: the channel-sharded form
     (``mqc_ssm_scan_fwd_chunked_peer``) that writes y into every buffer of
     ``ptrs`` ([B, T, ch_total, 4], local or peer memory) at channels
     ch_off.. instead of returning it; y is then None."""
@@ -253,8 +253,13 @@ def _run_scan_chunked(delta, Lam, B, C, S, D, h0, eps, nchunks, return_final_sta
         if peer is None:
             _lib.call("mqc_ssm_scan_fwd_chunked", ctypes.byref(a), int(nchunks), ws.data_ptr(),
                       ws_bytes, _lib.stream_ptr(delta.device))
+        elif len(peer) == 4 and peer[3]:  # (multicast address,), ch_total, ch_off, True
+            ptrs, ch_total, ch_off, _ = peer
+            _lib.call("mqc_ssm_scan_fwd_chunked_multicast", ctypes.byref(a), int(nchunks),
+                      ws.data_ptr(), ws_bytes, int(ptrs[0]), int(ch_total), int(ch_off),
+                      _lib.stream_ptr(delta.device))
         else:
-            ptrs, ch_total, ch_off = peer
+            ptrs, ch_total, ch_off = peer[:3]
             arr = (ctypes.c_void_p * len(ptrs))(*ptrs)
             _lib.call("mqc_ssm_scan_fwd_chunked_peer", ctypes.byref(a), int(nchunks),
                       ws.data_ptr(), ws_bytes, arr, len(ptrs), int(ch_total), int(ch_off),

@@ -147,6 +147,31 @@ def test_bc_proj_scan_argument_validation_without_gpu():
 
 
 @no_gpu
+def test_multicast_scan_argument_validation_without_gpu():
+    """mqc_ssm_scan_fwd_chunked_multicast rejects bad arguments on the host."""
+    lib = _lib.load()
+    fake = 0x10000
+    base = dict(batch=1, seq_len=64, channels=4, d_state=32, dtype=0,
+                flags=_lib.MQC_SSM_BC_SHARED | _lib.MQC_SSM_S_REAL, eps=1e-6, reserved0=0,
+                delta=fake, lambda_=fake, q=None, Bm=fake, Cm=fake, s=fake, dskip=fake,
+                dskip_sb=0, dskip_st=0, dskip_sd=1, h0=None, y=None, hT=None, status=None,
+                wait_poll_limit=-1, ckpt=None, ckpt_every=0)
+
+    def call(ymc=fake, ch_total=8, ch_off=0, nchunks=2, **kw):
+        a = _lib.SsmScanArgs(**{**base, **kw})
+        return lib.mqc_ssm_scan_fwd_chunked_multicast(ctypes.byref(a), nchunks, None, 0, ymc,
+                                                      ch_total, ch_off, None)
+
+    assert call(d_state=16) == UNSUPPORTED  # four lanes per channel are needed
+    assert b"d_state" in lib.mqc_last_error()
+    assert call(flags=_lib.MQC_SSM_S_REAL) == UNSUPPORTED  # per-channel B/C
+    assert call(ymc=None) == INVALID
+    assert call(ymc=fake + 8) == MISALIGNED
+    assert call(ch_off=6) == INVALID  # channels [6, 10) outside 8
+    assert call(nchunks=64) == UNSUPPORTED  # chunks of one step
+
+
+@no_gpu
 def test_host_scan_argument_validation_without_gpu():
     """mqc_ssm_scan_fwd_host rejects bad arguments before any CUDA call."""
     lib = _lib.load()

@@ -89,7 +89,7 @@ def _two_rank_worker(rank, world, port, q):
     dev = torch.device(f"cuda:{rank}")
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
     try:
-        inp = make_scan_inputs(1, 1024, 16, 16, shared=True, s_real=True, seed=7)
+        inp = make_scan_inputs(1, 1024, 16, 32, shared=True, s_real=True, seed=7)
         d = {k: v.to(dev, torch.bfloat16 if k not in ("Lambda", "D") else torch.float32)
              for k, v in inp.items()}
         dl = 16 // world
@@ -103,6 +103,15 @@ def _two_rank_worker(rank, world, port, q):
         for _ in range(2):  # the second call reuses the cached peer buffers
             y_fused = ssm_scan_cayley_channel_sharded(*args, time_chunks=4,
                                                       gather="peer").clone()
+        # NVLink SHARP multicast stores, where the platform has them: the same bits
+        used_mc = True
+        try:
+            for _ in range(2):
+                y_mc = ssm_scan_cayley_channel_sharded(*args, time_chunks=4,
+                                                       gather="multicast").clone()
+        except RuntimeError:  # no multicast on this platform
+            used_mc = False
+            y_mc = y_fused
 
         # segments pushed by mqc_channel_push (an explicit scan function)
         def scan_fn(dd, L, Bm, Cm, s, Dk, h0=None):
@@ -113,8 +122,10 @@ def _two_rank_worker(rank, world, port, q):
                                                  gather="peer").clone()
         y_full = ssm_scan_cayley(d["delta"], d["Lambda"], d["B"], d["C"], d["S"], d["D"])
         torch.cuda.synchronize()
-        q.put((rank, torch.equal(y_fused, y_nccl1) and torch.equal(y_push, y_nccl4),
-               max(rel_l2(y_fused.float(), y_full.float()), rel_l2(y_push.float(), y_full.float()))))
+        q.put((rank, torch.equal(y_fused, y_nccl1) and torch.equal(y_push, y_nccl4) and
+               torch.equal(y_mc, y_nccl1),
+               max(rel_l2(y_fused.float(), y_full.float()), rel_l2(y_push.float(), y_full.float())),
+               used_mc))
         release_peer_outputs()
     finally:
         dist.destroy_process_group()
@@ -133,6 +144,7 @@ def test_peer_gather_matches_nccl_gather_on_two_ranks():
         p.join(timeout=300)
     assert all(p.exitcode == 0 for p in procs)
     res = sorted(q.get(timeout=10) for _ in range(2))
-    for rank, equal, err in res:
+    print("multicast stores used:", [r[3] for r in res])
+    for rank, equal, err, _ in res:
         assert equal, f"rank {rank}: peer gather differs from the NCCL gather"
         assert err < 5e-3, f"rank {rank}: rel-L2 vs unsharded scan {err}"
