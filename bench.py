@@ -62,7 +62,7 @@ def parse_args():
                     help="seconds of CPU work for the cpu_baseline sample")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the forward+backward and per-channel-layout sub-measurements")
-    ap.add_argument("--only", choices=["fwd_bwd", "perchannel", "perchannel_fwd_bwd"],
+    ap.add_argument("--only", choices=["fwd", "fwd_bwd", "perchannel", "perchannel_fwd_bwd"],
                     default=None,
                     help="run only this sub-measurement and print it (profiling aid)")
     ap.add_argument("--prof-batch", type=int, default=None,
@@ -390,7 +390,14 @@ def run_b200(args, world, rank, local):
     torch.cuda.set_device(dev)
     if args.only is not None:
         stream = torch.cuda.current_stream(dev)
-        if args.only == "fwd_bwd":
+        if args.only == "fwd":
+            inp = make_inputs(dev, args.dtype, args.layout, seed=1234 + rank)
+            ms = timed(lambda: ssm_scan_cayley(inp["delta"], inp["Lambda"], inp["B"], inp["C"],
+                                               inp["x"], inp["D"]),
+                       args.steps, args.warmup, world, stream)
+            _lib.check_device_status(dev)
+            res = {"ms_per_step": max_over_ranks(ms / args.steps, world, dev)}
+        elif args.only == "fwd_bwd":
             inp = make_inputs(dev, args.dtype, args.layout, seed=1234 + rank)
             res = run_fwd_bwd(args, inp, dev, world, stream, ssm_scan_cayley)
         elif args.only == "perchannel_fwd_bwd":

@@ -399,10 +399,14 @@ __global__ void __launch_bounds__(32 * bwd_warps(G, BC_SHARED))
 // Packed backward: channel-shared B/C with d_state <= 2*NG, G = 2 states per lane
 // forming one pair (ng, ng + NG), on packed two-lane FP32 (packed_math.cuh).
 // Same algorithm as ssm_scan_bwd_kernel:
-//  * B/C come from the pair-interleaved pre-pass (pack_bc_pairs);
+//  * B/C come from the pair-interleaved pre-pass (pack_bc_pairs), whose rows
+//    keep the two 16-byte parts of a pair NG*16 bytes apart, so a warp's loads
+//    are contiguous;
 //  * delta, x (or S) and dy are fp32 (bf16 inputs widened first);
 //  * all inputs of a sub-block are staged one sub-block ahead with cp.async;
-//  * the per-warp dB/dC slices are pair-interleaved and are un-interleaved only
+//  * the per-warp dB/dC slices are pair-interleaved, stored component-major
+//    ([t][tensor][component][pair] float2: contiguous 8-byte stores across the
+//    lanes), and are un-interleaved only
 //    in the per-CTA summation.
 constexpr int kPbWarps = 8;
 
@@ -410,7 +414,7 @@ struct PbLayout {
   size_t slices, bc, dl, sx, gy, hst, stage, total;
 };
 
-// [slices: warps x kSub x 2 x NG pairs x 8 f32] then 2 stages of
+// [slices: warps x kSub x 2 tensors x 4 components x NG pairs x 2 f32] then 2 stages of
 // [bc: kSub x 2 x NG x 8 f32 | dl: kSub x cpb f32 | sx: kSub x cpb x sw f32 |
 //  gy: kSub x cpb x 4 f32 | hst: warps x 32 lanes x 8 f32]; stage offsets are
 // relative to the stage.
@@ -530,7 +534,7 @@ __global__ void __launch_bounds__(32 * kPbWarps)
     const int64_t row0 = (int64_t(b) * T_ + t0) * D + c;  // (b, t0, c) in [B,T,D]
     const int buf = (nsub - 1 - sb) & 1;
     const unsigned char* stg = stage_base + size_t(buf) * L.stage;
-    const float* sbc = reinterpret_cast<const float*>(stg + L.bc) + ng * 8;
+    const float* sbc = reinterpret_cast<const float*>(stg + L.bc) + ng * 4;
     const float* sdl = reinterpret_cast<const float*>(stg + L.dl) + cl;
     const float* ssx = reinterpret_cast<const float*>(stg + L.sx);
     const float4* sgy = reinterpret_cast<const float4*>(stg + L.gy) + cl;
@@ -538,7 +542,7 @@ __global__ void __launch_bounds__(32 * kPbWarps)
     auto ld_pair = [&](int tt, int which) -> QPair {
       const float* q = sbc + (tt * 2 + which) * NG * 8;
       const float4 u = *reinterpret_cast<const float4*>(q);
-      const float4 w = *reinterpret_cast<const float4*>(q + 4);
+      const float4 w = *reinterpret_cast<const float4*>(q + NG * 4);
       return QPair{make_float2(u.x, u.y), make_float2(u.z, u.w), make_float2(w.x, w.y),
                    make_float2(w.z, w.w)};
     };
@@ -636,17 +640,17 @@ __global__ void __launch_bounds__(32 * kPbWarps)
         }
         // the warp's first channel lanes write every (tt, pair) slot, so the slice
         // needs no clearing
-        if (lane < NG) {  // one 8-byte store per pair: no register assembly
-          float2* sbw = reinterpret_cast<float2*>(slice + ((tt * 2) * NG + ng) * 8);
+        if (lane < NG) {  // one 8-byte store per pair component: no register assembly
+          float2* sbw = reinterpret_cast<float2*>(slice + (tt * 2) * NG * 8) + ng;
           sbw[0] = dB.x;
-          sbw[1] = dB.y;
-          sbw[2] = dB.z;
-          sbw[3] = dB.w;
-          float2* scw = reinterpret_cast<float2*>(slice + ((tt * 2 + 1) * NG + ng) * 8);
+          sbw[NG] = dB.y;
+          sbw[2 * NG] = dB.z;
+          sbw[3 * NG] = dB.w;
+          float2* scw = reinterpret_cast<float2*>(slice + (tt * 2 + 1) * NG * 8) + ng;
           scw[0] = dC.x;
-          scw[1] = dC.y;
-          scw[2] = dC.z;
-          scw[3] = dC.w;
+          scw[NG] = dC.y;
+          scw[2 * NG] = dC.z;
+          scw[3 * NG] = dC.w;
         }
         carry = qp_mul_acc(qp_conj(qv), lam, qp_zero());
         part[tt * NV + 0] = pdp.x + pdp.y;
@@ -689,16 +693,15 @@ __global__ void __launch_bounds__(32 * kPbWarps)
     float* dCg = static_cast<float*>(p.dC);
     for (int e = threadIdx.x; e < len * 2 * NG; e += blockDim.x) {
       const int pg = e % NG, tw = e / NG;  // tw = tt * 2 + which
-      const float* s0 = slices + size_t(tw * NG + pg) * 8;
-      const float2* p0 = reinterpret_cast<const float2*>(s0);
-      float2 px = p0[0], py = p0[1], pz = p0[2], pw = p0[3];
+      const float2* p0 = reinterpret_cast<const float2*>(slices + size_t(tw) * NG * 8) + pg;
+      float2 px = p0[0], py = p0[NG], pz = p0[2 * NG], pw = p0[3 * NG];
 #pragma unroll
       for (int k = 1; k < kPbWarps; ++k) {
-        const float2* pk2 = reinterpret_cast<const float2*>(s0 + size_t(k) * kSub * 2 * NG * 8);
+        const float2* pk2 = p0 + size_t(k) * kSub * 2 * NG * 4;
         px = add2(px, pk2[0]);
-        py = add2(py, pk2[1]);
-        pz = add2(pz, pk2[2]);
-        pw = add2(pw, pk2[3]);
+        py = add2(py, pk2[NG]);
+        pz = add2(pz, pk2[2 * NG]);
+        pw = add2(pw, pk2[3 * NG]);
       }
       const float4 u = make_float4(px.x, px.y, py.x, py.y);
       const float4 w = make_float4(pz.x, pz.y, pw.x, pw.y);

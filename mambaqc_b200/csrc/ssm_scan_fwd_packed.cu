@@ -15,7 +15,10 @@
 // the two states of a pair side by side. Hence:
 //
 //  * a small pre-pass (`pack_bc_kernel`) rewrites B and C once per call into
-//    fp32 rows of NP = NG*G states ordered [pair j][lane ng][component][half],
+//    fp32 rows of NP = NG*G states ordered [pair j][part][lane ng][4 floats]
+//    (part 0: components x, y of both halves; part 1: z, w), so the 16-byte
+//    loads of the NG lanes of a channel cover one contiguous 128-byte line (no
+//    shared-memory bank conflicts),
 //    state n = ng + NG*(2j + half), zero-padded above N (bf16 inputs are
 //    widened here, so the scan never converts B/C);
 //  * warp 0 is the producer: one lane streams tc packed rows of B and C per
@@ -52,9 +55,11 @@ namespace {
 using namespace ::mqc::pk;
 
 constexpr int kRing = 3;
-// CTA size cap: 8 states per lane need ~128 registers per thread (512 threads).
+// CTA size cap: 8 states per lane run at ~160 registers per thread, which the
+// register file holds for 3 warps per sub-partition (384 threads); capped at 512
+// threads (128 registers) the kernel ran 3 % slower.
 // (4 states per lane with twice the warps measured slower on config 3.)
-__host__ __device__ constexpr int pk_max_threads(int g) { return g == 4 ? 768 : 512; }
+__host__ __device__ constexpr int pk_max_threads(int g) { return g == 4 ? 768 : 384; }
 constexpr size_t kPkSmemBudget = 220 * 1024;
 constexpr int kPackThreads = 256;
 
@@ -173,8 +178,9 @@ __device__ __forceinline__ bool mbar_wait_bounded_backoff(uint64_t* bar, uint32_
 
 // ------------------------------------------------------------ B/C pre-pass
 // One thread per (row, pair j, lane ng): reads states n0 = ng + 2*NG*j and
-// n1 = n0 + NG of B and C and writes their 8 interleaved floats
-// [x0 x1 y0 y1 | z0 z1 w0 w1]. Rows are the B*T (b, t) rows; output rows hold
+// n1 = n0 + NG of B and C and writes their 8 interleaved floats as two 16-byte
+// parts, [x0 x1 y0 y1] and [z0 z1 w0 w1], NG*16 bytes apart: a row is
+// [pair j][part][lane ng][4]. Rows are the B*T (b, t) rows; output rows hold
 // np = NG*G states (np*4 floats).
 template <typename T>
 __global__ void __launch_bounds__(kPackThreads)
@@ -192,15 +198,16 @@ __global__ void __launch_bounds__(kPackThreads)
     const int64_t base = row * N;
     const float4 b0 = n0 < N ? QIO<T>::ld(Bm + (base + n0) * 4) : f4_zero();
     const float4 b1 = n1 < N ? QIO<T>::ld(Bm + (base + n1) * 4) : f4_zero();
-    float4* ob = reinterpret_cast<float4*>(Bp + idx * 8);
+    const int64_t o0 = (row * per_row * 2 + (int64_t(j) << ng_log2) * 2 + ng) * 4;
+    float4* ob = reinterpret_cast<float4*>(Bp + o0);
     ob[0] = make_float4(b0.x, b1.x, b0.y, b1.y);
-    ob[1] = make_float4(b0.z, b1.z, b0.w, b1.w);
+    ob[NG] = make_float4(b0.z, b1.z, b0.w, b1.w);
     if (Cm != nullptr) {  // C is not needed by the state-only pass
       const float4 c0 = n0 < N ? QIO<T>::ld(Cm + (base + n0) * 4) : f4_zero();
       const float4 c1 = n1 < N ? QIO<T>::ld(Cm + (base + n1) * 4) : f4_zero();
-      float4* oc = reinterpret_cast<float4*>(Cp + idx * 8);
+      float4* oc = reinterpret_cast<float4*>(Cp + o0);
       oc[0] = make_float4(c0.x, c1.x, c0.y, c1.y);
-      oc[1] = make_float4(c0.z, c1.z, c0.w, c1.w);
+      oc[NG] = make_float4(c0.z, c1.z, c0.w, c1.w);
     }
   }
 }
@@ -437,9 +444,9 @@ __global__ void __launch_bounds__(pk_max_threads(G), 1)
     const int len = min(tc, T_ - t0);
     const float* cdel = wdel + buf * per_chunk;
     const float* csig = wsig + buf * per_chunk * SW;
-    // this lane's 8-float pair slots: [j][ng][x0 x1 y0 y1 z0 z1 w0 w1]
-    const float* rowB = sB + int64_t(st) * tc * NP * 4 + ng * 8;
-    const float* rowC = sC + int64_t(st) * tc * NP * 4 + ng * 8;
+    // this lane's pair slots: [j][part][ng][4], parts [x0 x1 y0 y1], [z0 z1 w0 w1]
+    const float* rowB = sB + int64_t(st) * tc * NP * 4 + ng * 4;
+    const float* rowC = sC + int64_t(st) * tc * NP * 4 + ng * 4;
     // unrolled by two so the loop-carried states alternate between two register
     // sets instead of being copied back at every step
     T* yrow = PEER ? nullptr : yb + int64_t(t0) * D * 4;
@@ -457,7 +464,7 @@ __global__ void __launch_bounds__(pk_max_threads(G), 1)
       for (int j = 0; j < G2; ++j) {
         const float* pb = rowB + tt * NP * 4 + j * NG * 8;
         const float4 b01 = *reinterpret_cast<const float4*>(pb);
-        const float4 b23 = *reinterpret_cast<const float4*>(pb + 4);
+        const float4 b23 = *reinterpret_cast<const float4*>(pb + NG * 4);
         const QPair Bq{make_float2(b01.x, b01.y), make_float2(b01.z, b01.w),
                        make_float2(b23.x, b23.y), make_float2(b23.z, b23.w)};
         float2 sq;
@@ -479,7 +486,7 @@ __global__ void __launch_bounds__(pk_max_threads(G), 1)
         } else {
           const float* pc = rowC + tt * NP * 4 + j * NG * 8;
           const float4 c01 = *reinterpret_cast<const float4*>(pc);
-          const float4 c23 = *reinterpret_cast<const float4*>(pc + 4);
+          const float4 c23 = *reinterpret_cast<const float4*>(pc + NG * 4);
           const QPair Cq{make_float2(c01.x, c01.y), make_float2(c01.z, c01.w),
                          make_float2(c23.x, c23.y), make_float2(c23.z, c23.w)};
           ya = qp_mul_acc(Cq, h[j], ya);
