@@ -62,6 +62,17 @@ MQC_API const char* mqc_last_error(void);
  * quaternion_multiply_batched, quaternion_ops.py:306-357 (dense case). */
 MQC_API int mqc_qmul(const void* p, const void* q, void* out, int64_t n, int dtype, void* stream);
 
+/* out[i0,i1,i2,i3] = p[i0,i1,i2,i3] (x) q[i0,i1,i2,i3] over the index space
+ * shape[0..3] = [batch, seq_len, d_model, d_state], p and q read through element
+ * strides per axis (non-negative multiples of 4; 0 broadcasts; the quaternion
+ * axis itself contiguous), out dense [shape..., 4]. shape[0]*shape[1] and
+ * shape[2]*shape[3] below 2^31. Replaces quaternion_multiply_batched with its
+ * stride arguments, quaternion_ops.py:306-357 (kernel :77-160), without a copy
+ * of non-contiguous inputs. */
+MQC_API int mqc_qmul_strided(const void* p, const void* q, void* out, const int64_t* shape,
+                             const int64_t* p_strides, const int64_t* q_strides, int dtype,
+                             void* stream);
+
 /* out[i] = conj(q[i]). Replaces quaternion_conjugate, quaternion_ops.py:360-391. */
 MQC_API int mqc_qconj(const void* q, void* out, int64_t n, int dtype, void* stream);
 

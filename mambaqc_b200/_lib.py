@@ -87,6 +87,8 @@ class BcProjScanArgs(ctypes.Structure):
 # name -> (argtypes); every function returns int status unless listed in _STR_FUNCS
 _SIGNATURES = {
     "mqc_qmul": [_c_void_p, _c_void_p, _c_void_p, _i64, _i32, _c_void_p],
+    "mqc_qmul_strided": [_c_void_p, _c_void_p, _c_void_p, ctypes.POINTER(_i64),
+                         ctypes.POINTER(_i64), ctypes.POINTER(_i64), _i32, _c_void_p],
     "mqc_qconj": [_c_void_p, _c_void_p, _i64, _i32, _c_void_p],
     "mqc_qinv": [_c_void_p, _c_void_p, _i64, _f32, _i32, _c_void_p],
     "mqc_qnorm": [_c_void_p, _c_void_p, _i64, _i32, _c_void_p],

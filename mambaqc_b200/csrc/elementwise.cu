@@ -104,6 +104,61 @@ __global__ void __launch_bounds__(kThreads) norm_kernel(const T* __restrict__ a,
   }
 }
 
+// Division by a fixed divisor d >= 1 of numerators below 2^31 with one
+// multiply-high and a shift (Granlund & Montgomery, "Division by invariant
+// integers using multiplication", 1994): s = ceil(log2 d),
+// m = floor(2^32 (2^s - d) / d) + 1, x / d = (umulhi(x, m) + x) >> s.
+struct FastDiv {
+  uint32_t d, m, s;
+  explicit FastDiv(uint32_t div = 1) : d(div), m(0), s(0) {
+    while ((uint64_t(1) << s) < d) ++s;
+    m = uint32_t(((uint64_t(1) << 32) * ((uint64_t(1) << s) - d)) / d + 1);
+  }
+  __device__ __forceinline__ uint32_t div(uint32_t x) const { return (__umulhi(x, m) + x) >> s; }
+};
+
+// Strided Hamilton product over a 4-axis index space (i0, i1, i2, i3), the
+// [batch, seq_len, d_model, d_state] of the reference's batched multiply. p and
+// q are addressed by per-axis element strides (quaternion axis contiguous); out
+// is dense, so stores are coalesced. Rows (i0, i1) are walked by blockIdx.y,
+// the inner (i2, i3) plane by x, kUnroll quaternions per thread in flight.
+struct StridedArgs {
+  int64_t ps[4], qs[4];
+  uint32_t rows, inner;  // s0 * s1 and s2 * s3
+  FastDiv div1, div3;    // by s1 and s3
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+    qmul_strided_kernel(const T* __restrict__ p, const T* __restrict__ q, T* __restrict__ out,
+                        const StridedArgs a) {
+  const uint32_t stride = gridDim.x * kThreads;
+  for (uint32_t r = blockIdx.y; r < a.rows; r += gridDim.y) {
+    const uint32_t i0 = a.div1.div(r), i1 = r - i0 * a.div1.d;
+    const int64_t prow = int64_t(i0) * a.ps[0] + int64_t(i1) * a.ps[1];
+    const int64_t qrow = int64_t(i0) * a.qs[0] + int64_t(i1) * a.qs[1];
+    T* orow = out + int64_t(r) * a.inner * 4;
+    for (uint32_t base = blockIdx.x * kThreads + threadIdx.x; base < a.inner;
+         base += stride * kUnroll) {
+      float4 va[kUnroll], vb[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const uint32_t j = base + u * stride;
+        if (j < a.inner) {
+          const uint32_t i2 = a.div3.div(j), i3 = j - i2 * a.div3.d;
+          va[u] = QIO<T>::ld_stream(p + prow + int64_t(i2) * a.ps[2] + int64_t(i3) * a.ps[3]);
+          vb[u] = QIO<T>::ld_stream(q + qrow + int64_t(i2) * a.qs[2] + int64_t(i3) * a.qs[3]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const uint32_t j = base + u * stride;
+        if (j < a.inner) QIO<T>::st_stream(orow + int64_t(j) * 4, qmul(va[u], vb[u]));
+      }
+    }
+  }
+}
+
 int grid_for(int64_t n) {
   const int64_t per_cta = int64_t(kThreads) * kUnroll;
   int64_t g = (n + per_cta - 1) / per_cta;
@@ -227,4 +282,57 @@ extern "C" int mqc_qnorm(const void* q, void* out, int64_t n, int dtype, void* s
         static_cast<const __nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(out), n);
   }
   return check_launch("mqc_qnorm");
+}
+
+extern "C" int mqc_qmul_strided(const void* p, const void* q, void* out, const int64_t* shape,
+                                const int64_t* p_strides, const int64_t* q_strides, int dtype,
+                                void* stream) {
+  clear_error();
+  MQC_REQUIRE(dtype_ok(dtype), MQC_ERR_INVALID_VALUE, "mqc_qmul_strided: unknown dtype %d", dtype);
+  MQC_REQUIRE(shape != nullptr && p_strides != nullptr && q_strides != nullptr,
+              MQC_ERR_INVALID_VALUE, "mqc_qmul_strided: null shape or strides");
+  int64_t n = 1;
+  for (int k = 0; k < 4; ++k) {
+    MQC_REQUIRE(shape[k] >= 0, MQC_ERR_INVALID_VALUE, "mqc_qmul_strided: negative extent");
+    MQC_REQUIRE(p_strides[k] >= 0 && q_strides[k] >= 0 && p_strides[k] % 4 == 0 &&
+                    q_strides[k] % 4 == 0,
+                MQC_ERR_INVALID_VALUE,
+                "mqc_qmul_strided: strides must be non-negative multiples of 4 elements");
+    n *= shape[k];
+  }
+  if (n == 0) return MQC_OK;
+  MQC_REQUIRE(p != nullptr && q != nullptr && out != nullptr, MQC_ERR_INVALID_VALUE,
+              "mqc_qmul_strided: null pointer");
+  const uintptr_t al = dtype == MQC_DTYPE_F32 ? 16 : 8;
+  MQC_REQUIRE(aligned(p, al) && aligned(q, al) && aligned(out, al), MQC_ERR_MISALIGNED,
+              "mqc_qmul_strided: quaternion pointers must be %d-byte aligned", int(al));
+  const int64_t rows = shape[0] * shape[1], inner = shape[2] * shape[3];
+  MQC_REQUIRE(rows < (int64_t(1) << 31) && inner < (int64_t(1) << 31), MQC_ERR_UNSUPPORTED,
+              "mqc_qmul_strided: more than 2^31 rows or inner quaternions");
+  StridedArgs a;
+  for (int k = 0; k < 4; ++k) {
+    a.ps[k] = p_strides[k];
+    a.qs[k] = q_strides[k];
+  }
+  a.rows = uint32_t(rows);
+  a.inner = uint32_t(inner);
+  a.div1 = FastDiv(uint32_t(shape[1]));
+  a.div3 = FastDiv(uint32_t(shape[3]));
+  // x covers the inner plane, y the rows: about 8 CTAs per SM in all
+  const int64_t per_cta = int64_t(kThreads) * kUnroll;
+  int64_t gx = (inner + per_cta - 1) / per_cta;
+  const int64_t want = int64_t(num_sms()) * 8;
+  if (gx > want) gx = want;
+  int64_t gy = (want + gx - 1) / gx;
+  if (gy > rows) gy = rows;
+  if (gy > 65535) gy = 65535;
+  const dim3 grid{unsigned(gx), unsigned(gy), 1u};
+  if (dtype == MQC_DTYPE_F32)
+    qmul_strided_kernel<float><<<grid, kThreads, 0, as_stream(stream)>>>(
+        static_cast<const float*>(p), static_cast<const float*>(q), static_cast<float*>(out), a);
+  else
+    qmul_strided_kernel<__nv_bfloat16><<<grid, kThreads, 0, as_stream(stream)>>>(
+        static_cast<const __nv_bfloat16*>(p), static_cast<const __nv_bfloat16*>(q),
+        static_cast<__nv_bfloat16*>(out), a);
+  return check_launch("mqc_qmul_strided");
 }

@@ -2,13 +2,15 @@
 
 Same names, argument meaning and preconditions (``assert``) as the reference
 (mambaqc/kernels/quaternion_ops.py:259-461); the work runs in
-``libmambaqc_b200.so`` (``mqc_qmul``, ``mqc_qconj``, ``mqc_qinv``,
+``libmambaqc_b200.so`` (``mqc_qmul``, ``mqc_qmul_strided``, ``mqc_qconj``, ``mqc_qinv``,
 ``mqc_qnorm``). Inputs must be CUDA float32 or bfloat16 tensors; there is no CPU
 path. ``quaternion_multiply`` is differentiable (dp = g (x) conj(q),
 dq = conj(p) (x) g), which the reference's Triton path is not.
 """
 
 from __future__ import annotations
+
+import ctypes
 
 import torch
 
@@ -75,15 +77,54 @@ def quaternion_multiply(p: torch.Tensor, q: torch.Tensor) -> torch.Tensor:
     return _QuaternionMultiply.apply(p, q)
 
 
-def quaternion_multiply_batched(p: torch.Tensor, q: torch.Tensor) -> torch.Tensor:
-    """Hamilton product on [batch, seq_len, d_model, d_state, 4] tensors (any strides).
+def _strided_ok(t: torch.Tensor) -> bool:
+    """Whether ``mqc_qmul_strided`` reads ``t`` in place: quaternion axis
+    contiguous, the other strides multiples of a quaternion, vector alignment."""
+    align = 16 if t.dtype == torch.float32 else 8
+    return (t.stride(-1) == 1 and all(s % 4 == 0 for s in t.stride()[:-1])
+            and t.data_ptr() % align == 0)
 
-    Mirrors ``quaternion_multiply_batched`` (quaternion_ops.py:306-357).
+
+def _qmul_strided_raw(p: torch.Tensor, q: torch.Tensor) -> torch.Tensor:
+    if p.dtype != q.dtype:
+        raise TypeError(f"quaternion_multiply_batched: dtype mismatch {p.dtype} vs {q.dtype}")
+    _lib.require_cuda(p, what="quaternion_multiply_batched")
+    _lib.require_cuda(q, what="quaternion_multiply_batched")
+    if not (_strided_ok(p) and _strided_ok(q)):
+        return _qmul_raw(p, q)
+    out = torch.empty(p.shape, dtype=p.dtype, device=p.device)
+    i64x4 = ctypes.c_int64 * 4
+    shape = i64x4(*p.shape[:4])
+    ps, qs = i64x4(*p.stride()[:4]), i64x4(*q.stride()[:4])
+    with torch.cuda.device(p.device):
+        _lib.call("mqc_qmul_strided", p.data_ptr(), q.data_ptr(), out.data_ptr(), shape, ps, qs,
+                  _lib.dtype_code(p), _lib.stream_ptr(p.device))
+    return out
+
+
+class _QuaternionMultiplyBatched(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, p, q):
+        ctx.save_for_backward(p, q)
+        return _qmul_strided_raw(p, q)
+
+    @staticmethod
+    def backward(ctx, g):
+        return _QuaternionMultiply.backward(ctx, g)
+
+
+def quaternion_multiply_batched(p: torch.Tensor, q: torch.Tensor) -> torch.Tensor:
+    """Hamilton product on [batch, seq_len, d_model, d_state, 4] tensors.
+
+    Mirrors ``quaternion_multiply_batched`` (quaternion_ops.py:306-357): like the
+    reference kernel, p and q are read through their strides (``mqc_qmul_strided``;
+    the quaternion axis must be contiguous, otherwise they are copied first). The
+    output is a dense tensor.
     """
     assert p.shape == q.shape
     assert p.shape[-1] == 4
     assert p.ndim == 5, f"Expected 5D tensor, got {p.ndim}D"
-    return _QuaternionMultiply.apply(p, q)
+    return _QuaternionMultiplyBatched.apply(p, q)
 
 
 def quaternion_conjugate(q: torch.Tensor) -> torch.Tensor:

@@ -88,6 +88,16 @@ def test_elementwise_argument_validation_without_gpu():
     assert lib.mqc_qmul(None, fake, fake, 4, 0, None) == INVALID
     assert lib.mqc_qmul(fake + 4, fake, fake, 4, 0, None) == MISALIGNED
     assert lib.mqc_qinv(fake, fake + 2, 4, 1e-6, 1, None) == MISALIGNED
+    i64x4 = ctypes.c_int64 * 4
+    shape, st = i64x4(2, 3, 4, 5), i64x4(240, 80, 20, 4)
+    assert lib.mqc_qmul_strided(fake, fake, fake, shape, st, i64x4(240, 80, 20, 2), 0,
+                                None) == INVALID  # stride not a whole quaternion
+    assert lib.mqc_qmul_strided(fake, fake, fake, shape, st, i64x4(240, 80, -20, 4), 0,
+                                None) == INVALID  # negative stride
+    assert lib.mqc_qmul_strided(fake, fake, fake, shape, st, st, 5, None) == INVALID
+    assert lib.mqc_qmul_strided(fake, None, fake, shape, st, st, 0, None) == INVALID
+    assert lib.mqc_qmul_strided(fake, fake, fake + 8, shape, st, st, 0, None) == MISALIGNED
+    assert lib.mqc_qmul_strided(None, None, None, i64x4(2, 0, 4, 5), st, st, 0, None) == 0
     assert lib.mqc_cayley(fake, fake, 0, 1e-6, 0, None) == 0  # empty input is a no-op
     assert lib.mqc_prefix_prod(fake, fake, 1, 4, -3, 0, None) == INVALID
     assert lib.mqc_prefix_prod(fake + 4, fake, 1, 4, 3, 0, None) == MISALIGNED

@@ -138,6 +138,57 @@ def test_qmul_large_and_noncontiguous_and_bf16():
     assert rel_l2(out, ref.qmul(p5.cpu().double(), q5.cpu().double())) < RTOL_F32
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_qmul_batched_reads_strided_inputs_in_place(dtype, monkeypatch):
+    """quaternion_multiply_batched on permuted, sliced and broadcast operands goes
+    through the strided kernel (no contiguous copy) and matches the oracle."""
+    from mambaqc_b200.kernels import quaternion_ops as qo
+
+    def no_copy(*a, **k):
+        raise AssertionError("strided operands were copied to the dense path")
+
+    monkeypatch.setattr(qo, "_qmul_raw", no_copy)
+    g = gen(41)
+    tol = RTOL_F32 if dtype == torch.float32 else RTOL_BF16
+    base_p = torch.randn(3, 2 * 37, 16, 24, 4, generator=g)
+    base_q = torch.randn(3, 37, 24, 16, 4, generator=g)
+    p = base_p.to(DEV, dtype)[:, ::2]                    # every other step
+    q = base_q.to(DEV, dtype).transpose(2, 3)            # d_model <-> d_state
+    out = quaternion_multiply_batched(p, q)
+    assert out.shape == p.shape and out.is_contiguous()
+    assert rel_l2(out, ref.qmul(p.cpu().double(), q.cpu().double())) < tol
+    # a broadcast operand (stride 0 over batch and sequence)
+    w = torch.randn(1, 1, 16, 24, 4, generator=g).to(DEV, dtype).expand(3, 37, 16, 24, 4)
+    out = quaternion_multiply_batched(p, w)
+    assert rel_l2(out, ref.qmul(p.cpu().double(), w.cpu().double())) < tol
+    # bitwise equal to the dense kernel on the same values
+    monkeypatch.undo()
+    assert torch.equal(quaternion_multiply_batched(p, q),
+                       quaternion_multiply(p.contiguous(), q.contiguous()))
+
+
+def test_qmul_batched_strided_large_and_gradients():
+    """A transposed [2, 256, 768, 64, 4] operand (the config-2 prefix-scan shape)
+    and the autograd path of the batched multiply."""
+    g = torch.Generator(device=DEV).manual_seed(42)
+    p = torch.randn(2, 256, 64, 768, 4, generator=g, device=DEV).transpose(2, 3)
+    q = torch.randn(2, 256, 768, 64, 4, generator=g, device=DEV)
+    out = quaternion_multiply_batched(p, q)
+    sl = (slice(None), slice(0, 256, 17), slice(0, 768, 29))
+    assert rel_l2(out[sl], ref.qmul(p[sl].cpu().double(), q[sl].cpu().double())) < RTOL_F32
+    del p, q, out
+    p64 = torch.randn(2, 5, 3, 7, 4, generator=gen(43), dtype=torch.float64)
+    q64 = torch.randn(2, 5, 7, 3, 4, generator=gen(44), dtype=torch.float64).transpose(2, 3)
+    w = torch.randn(2, 5, 3, 7, 4, generator=gen(45), dtype=torch.float64)
+    pr, qr = p64.clone().requires_grad_(), q64.clone().requires_grad_()
+    (ref.qmul(pr, qr) * w).sum().backward()
+    pg = g32(p64).requires_grad_()
+    qg = g32(q64.transpose(2, 3).contiguous()).transpose(2, 3).detach().requires_grad_()
+    (quaternion_multiply_batched(pg, qg) * g32(w)).sum().backward()
+    assert rel_l2(pg.grad, pr.grad) < RTOL_F32
+    assert rel_l2(qg.grad, qr.grad) < RTOL_F32
+
+
 def test_qmul_order_matters():
     """Swapping operands must break parity: the Hamilton product is exercised."""
     g = gen(5)
