@@ -371,7 +371,7 @@ def run_reference(args, world, rank):
 # (dram__bytes_read.sum + dram__bytes_write.sum), keyed by (dtype, layout). This
 # run does not measure it (no profiler runs inside the bench); None where no
 # capture exists.
-NCU_TRAFFIC_BYTES = {("fp32", "shared"): 119.68e6 + 152.29e6}
+NCU_TRAFFIC_BYTES = {("fp32", "shared"): 119.57e6 + 151.86e6}
 NCU_TRAFFIC_SOURCE = ("ncu capture of the same kernel and workload, summarised in "
                       "profiles/scan_fwd_packed_config3.md; not measured by this run")
 
