@@ -79,6 +79,19 @@ __device__ __forceinline__ QPair cayley_pair(float dl, float dl2, const LamPair&
   return QPair{fma2(neg2(P), inv, inv), mul2(s, c.li), mul2(s, c.lj), mul2(s, c.lk)};
 }
 
+// cayley_pair that also hands out 1 / max(den, eps) and the unclamped
+// den = 1 + P - delta*lr, for cayley_vjp_pair_shared at the same step.
+__device__ __forceinline__ QPair cayley_pair_keep(float dl, float dl2, const LamPair& c, float eps,
+                                                  float2* inv_out, float2* den_out) {
+  const float2 P = mul2(bc2(dl2), c.m);
+  const float2 den = fma2(bc2(-dl), c.lr, add2(bc2(1.f), P));
+  const float2 inv = rcp_nr2(make_float2(fmaxf(den.x, eps), fmaxf(den.y, eps)));
+  const float2 s = mul2(bc2(dl), inv);
+  *inv_out = inv;
+  *den_out = den;
+  return QPair{fma2(neg2(P), inv, inv), mul2(s, c.li), mul2(s, c.lj), mul2(s, c.lk)};
+}
+
 __device__ __forceinline__ float4 qp_half(const QPair& q, int e) {
   return e == 0 ? make_float4(q.x.x, q.y.x, q.z.x, q.w.x) : make_float4(q.x.y, q.y.y, q.z.y, q.w.y);
 }
@@ -125,6 +138,30 @@ __device__ __forceinline__ QPair cayley_vjp_pair(const QPair& z, const QPair& g,
   const float2 den = fma2(om, om, vv);
   const float2 Dd = make_float2(fmaxf(den.x, eps), fmaxf(den.y, eps));
   const float2 inv = rcp_nr2(Dd);
+  float2 w = mul2(inv, inv);
+  w.x = den.x >= eps ? w.x : 0.f;
+  w.y = den.y >= eps ? w.y : 0.f;
+  const float2 num_r = fma2(om, add2(bc2(1.f), a), neg2(vv));
+  const float2 gv = fma2(g.y, v1, fma2(g.z, v2, mul2(g.w, v3)));
+  const float2 hw = mul2(w, om);
+  const float2 da = fma2(g.x, fma2(hw, num_r, neg2(mul2(a, inv))), mul2(mul2(bc2(2.f), hw), gv));
+  const float2 cv = neg2(add2(mul2(g.x, fma2(w, num_r, inv)), mul2(mul2(bc2(2.f), w), gv)));
+  return QPair{da, fma2(cv, v1, mul2(g.y, inv)), fma2(cv, v2, mul2(g.z, inv)),
+               fma2(cv, v3, mul2(g.w, inv))};
+}
+
+// cayley_vjp_pair for z = delta * Lambda, given the reciprocal and unclamped
+// denominator of the forward map at the same step (cayley_pair_keep):
+// |1 - z/2|^2 = (1 - a)^2 + |v|^2 = 1 + P - delta*lr is that denominator, so no
+// second reciprocal is taken, and a, v come from delta/2 directly. Same
+// formulas as cayley_vjp_pair otherwise.
+__device__ __forceinline__ QPair cayley_vjp_pair_shared(float dl, const LamPair& c, float2 inv,
+                                                        float2 den, const QPair& g, float eps) {
+  const float2 hd = bc2(0.5f * dl);
+  const float2 a = mul2(hd, c.lr);
+  const float2 v1 = mul2(hd, c.li), v2 = mul2(hd, c.lj), v3 = mul2(hd, c.lk);
+  const float2 om = add2(bc2(1.f), neg2(a));
+  const float2 vv = fma2(v1, v1, fma2(v2, v2, mul2(v3, v3)));
   float2 w = mul2(inv, inv);
   w.x = den.x >= eps ? w.x : 0.f;
   w.y = den.y >= eps ? w.y : 0.f;

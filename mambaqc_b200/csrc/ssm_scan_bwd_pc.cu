@@ -372,11 +372,11 @@ __global__ void __launch_bounds__(32 * pc_warps<T>(), pc_min_ctas<T>())
         const QPair cg = qp_mul_bcast(qp_conj(Cq), gy);
         const QPair lam{add2(cg.x, carry.x), add2(cg.y, carry.y), add2(cg.z, carry.z),
                         add2(cg.w, carry.w)};
-        const QPair qv = cayley_pair(dl, dl * dl, lc, eps);
+        float2 cinv, cden;
+        const QPair qv = cayley_pair_keep(dl, dl * dl, lc, eps, &cinv, &cden);
         const QPair dq = qp_mul_acc(lam, qp_conj(hprev), qp_zero());
         const float2 d2 = bc2(dl);
-        const QPair z{mul2(d2, lq.x), mul2(d2, lq.y), mul2(d2, lq.z), mul2(d2, lq.w)};
-        const QPair dz = cayley_vjp_pair(z, dq, eps);
+        const QPair dz = cayley_vjp_pair_shared(dl, lc, cinv, cden, dq, eps);
         const float2 pdp = qp_dot(dz, lq);
         dlam = QPair{fma2(d2, dz.x, dlam.x), fma2(d2, dz.y, dlam.y), fma2(d2, dz.z, dlam.z),
                      fma2(d2, dz.w, dlam.w)};
