@@ -209,7 +209,9 @@ __global__ void __launch_bounds__(MAXT) qln_bwd_kernel(
     const T* sq = sbuf + 2 * s * rlen;
     const T* sg = sq + rlen;
     const float mu = __ldg(mean + row), rs = __ldg(rstd + row);
-    float nrm[kVptB], nh[kVptB], av[kVptB];
+    // rdn = 1 / (n + eps) and rn = 1 / n, Newton-refined reciprocals: each
+    // quaternion takes two instead of four divisions
+    float nrm[kVptB], nh[kVptB], av[kVptB], rdn[kVptB];
     float sa = 0.f, san = 0.f;
 #pragma unroll
     for (int j = 0; j < kVptB; ++j) {
@@ -217,13 +219,14 @@ __global__ void __launch_bounds__(MAXT) qln_bwd_kernel(
       nrm[j] = 1.f;
       nh[j] = 0.f;
       av[j] = 0.f;
+      rdn[j] = 0.f;
       if (d < D) {
         const float4 a = QIO<T>::lds(sq + d * 4);
         const float4 gv = QIO<T>::lds(sg + d * 4);
         nrm[j] = sqrtf(fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, a.w * a.w))) + eps);
         nh[j] = (nrm[j] - mu) * rs;
-        const float dn = nrm[j] + eps;
-        const float gu = fmaf(gv.x, a.x, fmaf(gv.y, a.y, fmaf(gv.z, a.z, gv.w * a.w))) / dn;
+        rdn[j] = rcp_nr(nrm[j] + eps);
+        const float gu = fmaf(gv.x, a.x, fmaf(gv.y, a.y, fmaf(gv.z, a.z, gv.w * a.w))) * rdn[j];
         av[j] = gm[j] * gu;
         sa += av[j];
         san = fmaf(av[j], nh[j], san);
@@ -243,10 +246,9 @@ __global__ void __launch_bounds__(MAXT) qln_bwd_kernel(
       if (d < D) {
         const float4 qv = QIO<T>::lds(sq + d * 4);
         const float4 gv = QIO<T>::lds(sg + d * 4);
-        const float dn = nrm[j] + eps;
-        const float dldn = rs * (av[j] - ma - nh[j] * man) - nh[j] * av[j] / dn;
-        const float cg = gm[j] * nh[j] / dn;
-        const float cq = dldn / nrm[j];
+        const float dldn = rs * (av[j] - ma - nh[j] * man) - nh[j] * av[j] * rdn[j];
+        const float cg = gm[j] * nh[j] * rdn[j];
+        const float cq = dldn * rcp_nr(nrm[j]);
         float4 o;
         o.x = fmaf(cg, gv.x, cq * qv.x);
         o.y = fmaf(cg, gv.y, cq * qv.y);
