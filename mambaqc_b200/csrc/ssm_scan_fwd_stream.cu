@@ -13,6 +13,7 @@
 #include <cstdlib>
 #include <cstring>
 
+#include "packed_math.cuh"
 #include "ssm_scan_common.cuh"
 
 namespace mqc {
@@ -108,6 +109,47 @@ __global__ void __launch_bounds__(kStreamThreads)
   load_step(0, cur);
   const float eps = p.eps;
   T* yb = static_cast<T*>(p.y) + (int64_t(b) * T_ * D + c) * 4;
+  // two states per lane with the Cayley map formed here: run them as one packed
+  // pair (n0, n1) through two-lane FP32 instructions, with the rounding and order
+  // of the scalar formulas below (packed_math.cuh), so the results are the same
+  if constexpr (G == 2 && !Q_GIVEN && !STATE_ONLY) {
+    const pk::LamPair lp{make_float2(lc[0].lr, lc[1].lr), make_float2(lc[0].li, lc[1].li),
+                         make_float2(lc[0].lj, lc[1].lj), make_float2(lc[0].lk, lc[1].lk),
+                         make_float2(lc[0].m, lc[1].m)};
+    pk::QPair hq = pk::qp_from(h[0], h[1]);
+    for (int t = 0; t < T_; ++t) {
+      if (t + 1 < T_) load_step(t + 1, nxt);
+      const float dl = cur.dl;
+      const float4 sv = cur.sv;
+      const pk::QPair qv = pk::cayley_pair(dl, dl * dl, lp, eps);
+      const pk::QPair Bq = pk::qp_from(cur.Bv[0], cur.Bv[1]);
+      pk::QPair inj;
+      if (S_REAL) {
+        const float2 s2 = pk::bc2(sv.x);
+        inj = pk::QPair{pk::mul2(s2, Bq.x), pk::mul2(s2, Bq.y), pk::mul2(s2, Bq.z),
+                        pk::mul2(s2, Bq.w)};
+      } else {
+        inj = pk::qp_mul_bcast(Bq, sv);
+      }
+      hq = pk::qp_mul_acc(qv, hq, inj);
+      const pk::QPair y2 = pk::qp_mul_acc(pk::qp_from(cur.Cv[0], cur.Cv[1]), hq, pk::qp_zero());
+      const float4 ya =
+          make_float4(y2.x.x + y2.x.y, y2.y.x + y2.y.y, y2.z.x + y2.z.y, y2.w.x + y2.w.y);
+      float dsk = dsk0;
+      if (!d_const)
+        dsk = (active && ng < 4)
+                  ? __ldg(p.dskip + int64_t(b) * p.dsb + int64_t(t) * p.dst + int64_t(c) * p.dsd)
+                  : 0.f;
+      reduce_store_y<T, NG>(ya, sv, dsk, ng, active, yb + int64_t(t) * D * 4);
+      if (p.ckpt != nullptr && active && (t + 1) % p.ckpt_every == 0 && t + 1 < T_) {
+        const float4 hh[2] = {pk::qp_half(hq, 0), pk::qp_half(hq, 1)};
+        store_ckpt<G, NG>(p, b, c, ng, (t + 1) / p.ckpt_every - 1, hh);
+      }
+      cur = nxt;
+    }
+    h[0] = pk::qp_half(hq, 0);
+    h[1] = pk::qp_half(hq, 1);
+  } else
   for (int t = 0; t < T_; ++t) {
     if (t + 1 < T_) load_step(t + 1, nxt);
     const float dl = cur.dl, dl2 = dl * dl;
