@@ -33,6 +33,8 @@ def _prep(t: torch.Tensor, what: str) -> torch.Tensor:
 def _qmul_raw(p: torch.Tensor, q: torch.Tensor) -> torch.Tensor:
     if p.dtype != q.dtype:
         raise TypeError(f"quaternion_multiply: dtype mismatch {p.dtype} vs {q.dtype}")
+    if p.device != q.device:
+        raise ValueError(f"quaternion_multiply: operands on {p.device} and {q.device}")
     pc, qc = _prep(p, "quaternion_multiply"), _prep(q, "quaternion_multiply")
     out = torch.empty_like(pc)
     with torch.cuda.device(pc.device):
@@ -90,6 +92,8 @@ def _qmul_strided_raw(p: torch.Tensor, q: torch.Tensor) -> torch.Tensor:
         raise TypeError(f"quaternion_multiply_batched: dtype mismatch {p.dtype} vs {q.dtype}")
     _lib.require_cuda(p, what="quaternion_multiply_batched")
     _lib.require_cuda(q, what="quaternion_multiply_batched")
+    if p.device != q.device:
+        raise ValueError(f"quaternion_multiply_batched: operands on {p.device} and {q.device}")
     if not (_strided_ok(p) and _strided_ok(q)):
         return _qmul_raw(p, q)
     out = torch.empty(p.shape, dtype=p.dtype, device=p.device)
