@@ -12,6 +12,7 @@
 // prefetched the same way. Same per-element math as the fused kernels.
 #include <cstdlib>
 #include <cstring>
+#include <type_traits>
 
 #include "packed_math.cuh"
 #include "ssm_scan_common.cuh"
@@ -117,12 +118,56 @@ __global__ void __launch_bounds__(kStreamThreads)
                          make_float2(lc[0].lj, lc[1].lj), make_float2(lc[0].lk, lc[1].lk),
                          make_float2(lc[0].m, lc[1].m)};
     pk::QPair hq = pk::qp_from(h[0], h[1]);
+    // B and C of the next step are held as loaded (bf16: 8 bytes a quaternion)
+    // and unpacked straight into the pair registers when used
+    using Raw = typename std::conditional<sizeof(T) == 2, uint2, float4>::type;
+    struct RStep {
+      float dl;
+      float4 sv;
+      Raw B[2], C[2];
+    };
+    auto ld_raw = [&](const T* ptr) -> Raw {
+      if constexpr (sizeof(T) == 2) return __ldcs(reinterpret_cast<const uint2*>(ptr));
+      else return __ldcs(reinterpret_cast<const float4*>(ptr));
+    };
+    auto load_raw = [&](int t, RStep& s) {
+      const int64_t row = row0 + int64_t(t) * row_stride;
+      const int64_t ebc = bc0 + int64_t(t) * bc_stride;
+      s.dl = active ? to_f(gdelta[row]) : 0.f;
+      s.sv = f4_zero();
+      if (active) {
+        if (S_REAL) s.sv.x = to_f(gs[row]);
+        else s.sv = QIO<T>::ld(gs + row * 4);
+      }
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        s.B[i] = s.C[i] = Raw{};
+        if (nok[i]) {
+          s.B[i] = ld_raw(gB + ebc + NG * i * 4);
+          s.C[i] = ld_raw(gC + ebc + NG * i * 4);
+        }
+      }
+    };
+    auto to_pair = [&](const Raw& a, const Raw& b) -> pk::QPair {
+      if constexpr (sizeof(T) == 2) {
+        return pk::QPair{make_float2(__uint_as_float(a.x << 16), __uint_as_float(b.x << 16)),
+                         make_float2(__uint_as_float(a.x & 0xffff0000u),
+                                     __uint_as_float(b.x & 0xffff0000u)),
+                         make_float2(__uint_as_float(a.y << 16), __uint_as_float(b.y << 16)),
+                         make_float2(__uint_as_float(a.y & 0xffff0000u),
+                                     __uint_as_float(b.y & 0xffff0000u))};
+      } else {
+        return pk::qp_from(a, b);
+      }
+    };
+    RStep rc, rn;
+    load_raw(0, rc);
     for (int t = 0; t < T_; ++t) {
-      if (t + 1 < T_) load_step(t + 1, nxt);
-      const float dl = cur.dl;
-      const float4 sv = cur.sv;
+      if (t + 1 < T_) load_raw(t + 1, rn);
+      const float dl = rc.dl;
+      const float4 sv = rc.sv;
       const pk::QPair qv = pk::cayley_pair(dl, dl * dl, lp, eps);
-      const pk::QPair Bq = pk::qp_from(cur.Bv[0], cur.Bv[1]);
+      const pk::QPair Bq = to_pair(rc.B[0], rc.B[1]);
       pk::QPair inj;
       if (S_REAL) {
         const float2 s2 = pk::bc2(sv.x);
@@ -132,7 +177,7 @@ __global__ void __launch_bounds__(kStreamThreads)
         inj = pk::qp_mul_bcast(Bq, sv);
       }
       hq = pk::qp_mul_acc(qv, hq, inj);
-      const pk::QPair y2 = pk::qp_mul_acc(pk::qp_from(cur.Cv[0], cur.Cv[1]), hq, pk::qp_zero());
+      const pk::QPair y2 = pk::qp_mul_acc(to_pair(rc.C[0], rc.C[1]), hq, pk::qp_zero());
       const float4 ya =
           make_float4(y2.x.x + y2.x.y, y2.y.x + y2.y.y, y2.z.x + y2.z.y, y2.w.x + y2.w.y);
       float dsk = dsk0;
@@ -145,7 +190,7 @@ __global__ void __launch_bounds__(kStreamThreads)
         const float4 hh[2] = {pk::qp_half(hq, 0), pk::qp_half(hq, 1)};
         store_ckpt<G, NG>(p, b, c, ng, (t + 1) / p.ckpt_every - 1, hh);
       }
-      cur = nxt;
+      rc = rn;
     }
     h[0] = pk::qp_half(hq, 0);
     h[1] = pk::qp_half(hq, 1);
